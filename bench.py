@@ -1,0 +1,323 @@
+"""Benchmark of the Qwen2.5 QLoRA training step on B200 (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 7b|1.5b|0.5b] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
+
+Workload (default): BASELINE configs[4], the Qwen2.5-7B-shaped QLoRA step — 28 layers, hidden
+3584, intermediate 18944, 28/4 heads x 128, vocab 152064, NF4 (bs 64, double quant) base, LoRA
+r=64 alpha=128 (dropout 0.05) on all seven linears, batch 4 x 4096 per GPU, activation
+checkpointing, AdamW on the adapters; data-parallel with an fp32 NCCL all-reduce of the adapter
+gradients. Synthetic data and random weights (no network). Per-GPU work is fixed as N grows
+(weak scaling).
+
+Prints ONE JSON line (rank 0): tokens/s of the whole job timed with CUDA events (max over
+ranks), the end-to-end number through the public API with host<->device copies, per-kernel
+device times of this package's kernels with their roofline fractions, the roofline of the
+dominant one, the CPU baseline (the reference's eager path on the host cores, a bounded sample),
+and the SM clocks sampled during the timed region.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "QLoRA step tokens/s (Qwen2.5 shapes) + per-kernel % of HBM/tensor roofline"
+WORKLOADS = {
+    "7b": ("configs[4]: Qwen2.5-7B-shaped QLoRA step, data-parallel, 4 x 4096 tokens per GPU",
+           4, 4096),
+    "1.5b": ("configs[3]: Qwen2.5-1.5B-shaped QLoRA step, 4 x 2048 tokens per GPU", 4, 2048),
+    "0.5b": ("configs[0] shapes: Qwen2.5-0.5B-shaped QLoRA step, 2 x 256 tokens per GPU", 2, 256),
+}
+# per-kernel roofline class: "hbm" (bytes) or "tensor" (flops)
+BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hbm",
+         "qb_rope_qk": "hbm", "qb_swiglu_fwd": "hbm", "qb_swiglu_bwd": "hbm",
+         "qb_dropout_scale": "hbm", "qb_scaled_add": "hbm", "qb_ce_rows": "hbm"}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons every 200 ms while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in getattr(self, "out", "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), float(f[4]), f[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[3] >= 50] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[4]) if v == "Active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": rows[0][1],
+                "power_w_max": max(r[2] for r in rows), "samples": len(loaded),
+                "reasons": reasons}
+
+
+def kernel_table(summary, pk):
+    """Per kernel: launches, ms, achieved GB/s (algorithmic bytes / device time), fraction."""
+    table = {}
+    for name, d in summary.items():
+        ms = d["ms_total"]
+        entry = {"launches": d["launches"], "ms_total": round(ms, 3),
+                 "bound": BOUND.get(name, "hbm")}
+        if ms > 0 and entry["bound"] == "hbm":
+            gbs = d["bytes"] / (ms * 1e-3) / 1e9
+            entry.update(achieved_gbs=round(gbs, 1), frac=round(gbs / pk["hbm_gbs"], 3),
+                         bytes_per_launch=d["bytes"] // max(1, d["launches"]))
+        elif ms > 0:
+            tf = d["flops"] / (ms * 1e-3) / 1e12
+            entry.update(achieved_tflops=round(tf, 1), frac=round(tf / pk["bf16_tflops"], 3),
+                         flops_per_launch=d["flops"] // max(1, d["launches"]))
+        table[name] = entry
+    return table
+
+
+def cpu_baseline(shape, tokens):
+    from oracle import cpu_step  # the checker's eager path, timed on the host cores
+    v, threads, desc = cpu_step.time_sample(shape, tokens=tokens)
+    return {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": desc["sample"], "layer_s": desc["layer_s"], "head_s": desc["head_s"]}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's eager CPU path (the oracle port) on the host cores."""
+    if rank != 0:
+        return
+    from hackathon_b200.qlora import preset
+    workload, _, _ = WORKLOADS[args.config]
+    shape = preset(args.config)
+    from oracle import cpu_step
+    vals = []
+    for _ in range(args.warmup):
+        cpu_step.time_sample(shape, tokens=args.cpu_tokens)
+    threads, desc = None, None
+    for _ in range(max(1, args.steps)):
+        v, threads, desc = cpu_step.time_sample(shape, tokens=args.cpu_tokens)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * args.cpu_tokens / value, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload, "parallelism": "none (host CPU)",
+                       "sample_tokens": args.cpu_tokens},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
+                             "kind": "port", "sample": desc["sample"]},
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="7b", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
+    ap.add_argument("--cpu-tokens", type=int, default=128)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if args.warmup < 3:
+        print("bench.py: at least 3 warm-up steps are required", file=sys.stderr)
+        args.warmup = 3
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from hackathon_b200 import _lib
+    from hackathon_b200.dp import AdapterGradSync, global_label_count
+    from hackathon_b200.qlora import QwenQLoRA, make_optimizer, preset, synthetic_batch, train_step
+
+    workload, batch, seq = WORKLOADS[args.config]
+    batch = args.batch or batch
+    seq = args.seq or seq
+    shape = preset(args.config)
+    model = QwenQLoRA(shape, dev, seed=0)
+    opt = make_optimizer(model)
+    sync = AdapterGradSync(model.adapter_parameters()) if world > 1 else None
+    data = [synthetic_batch(shape, batch, seq, dev, seed=1000 * rank + i) for i in range(2)]
+    counts = [global_label_count(lb) for _, lb in data]
+
+    def step(i):
+        ids, labels = data[i % 2]
+        return train_step(model, opt, ids, labels, grad_sync=sync,
+                          num_items_in_batch=counts[i % 2])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, inputs resident in HBM (working set >> 126 MB L2)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(args.steps):
+            step(i)
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    tokens_per_step = batch * seq * world
+    value = tokens_per_step / (ms * 1e-3)
+
+    # ---- per-kernel device times inside one step (events around every C-ABI call)
+    barrier()
+    with _lib.KernelTimer() as kt:
+        step(0)
+    ksum = kt.summary()
+
+    # ---- end to end through the public API: pinned host inputs copied in, loss read back
+    host = [(ids.cpu().pin_memory(), lb.cpu().pin_memory()) for ids, lb in data]
+    h2d = sum(x.numel() * x.element_size() for x in host[0])
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        ids_h, lb_h = host[i % 2]
+        ids = ids_h.to(dev, non_blocking=True)
+        lb = lb_h.to(dev, non_blocking=True)
+        loss = train_step(model, opt, ids, lb, grad_sync=sync,
+                          num_items_in_batch=global_label_count(lb))
+        loss_value = float(loss.cpu())     # device -> host read of the step's result
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ems = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    e2e = tokens_per_step / (float(ems[0]) * 1e-3)
+
+    pk = peaks()
+    table = kernel_table(ksum, pk)
+    ours_ms = sum(v["ms_total"] for v in table.values())
+    dom_name = max(table, key=lambda k: table[k]["ms_total"]) if table else None
+    roofline = None
+    if dom_name is not None:
+        d = table[dom_name]
+        avg_ms = d["ms_total"] / d["launches"]
+        if d["bound"] == "hbm":
+            per = ksum[dom_name]["bytes"] / d["launches"]
+            achieved = per / (avg_ms * 1e-3) / 1e9
+            roofline = {"kernel": dom_name, "bound": "hbm", "achieved": round(achieved, 1),
+                        "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None,
+                        "algorithmic_bytes_per_launch": int(per),
+                        "peak_source": pk["source"]}
+        else:
+            per = ksum[dom_name]["flops"] / d["launches"]
+            achieved = per / (avg_ms * 1e-3) / 1e12
+            roofline = {"kernel": dom_name, "bound": "tensor", "achieved": round(achieved, 1),
+                        "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                        "frac": round(achieved / pk["bf16_tflops"], 3), "traffic": None,
+                        "algorithmic_flops_per_launch": int(per), "peak_source": pk["source"]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(shape, args.cpu_tokens)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random token ids, random-init weights quantised to NF4)",
+            "config": {"workload": workload, "model": shape.name, "global_batch": batch * world,
+                       "seq_len": seq, "parallelism": f"dp{world}", "lora_r": shape.lora_r,
+                       "lora_dropout": shape.lora_dropout, "activation_checkpointing": True,
+                       "l2": "working set (NF4 weights, activations) far larger than the 126 MB L2"},
+            "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4, "last_loss": round(loss_value, 4)},
+            "gpu_launches": sum(v["launches"] for v in table.values()) * args.steps,
+            "roofline": roofline,
+            "kernels": table,
+            "kernel_ms_per_step_ours": round(ours_ms, 2),
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "peaks": pk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,275 @@
+"""NF4 (4-bit NormalFloat) weights with double-quantised block scales, and the 4-bit linear.
+
+Mirrors the API of solution/nf4.py:
+  dequantize_nf4(packed, quant_state, dtype)  -> dense weight (nf4.py:71-92)
+  supported(quant_state)                      -> admission check (nf4.py:65-68)
+  NF4Linear.apply(x, packed, quant_state, bias) (nf4.py:95-112)
+  linear4bit / patch_linear4bit / project     (nf4.py:115-176)
+and adds the producer of the format, `quantize_nf4`, since bitsandbytes is not a dependency.
+
+Format (bitsandbytes' 4-bit layout): weight i of the flattened [out, in] matrix is a 4-bit index
+into the 16-entry NF4 table; byte j holds weights 2j (high nibble) and 2j+1 (low nibble). Each
+block of `blocksize` (64) weights has a scale. With double quantisation ("nested") the scales are
+themselves stored as uint8 indices into a 256-entry signed dynamic table (`state2.code`) with one
+fp32 scale per `state2.blocksize` (256) of them, after subtracting their mean (`offset`).
+
+Every op here runs on the GPU through libqlora_b200.so; there is no CPU path.
+"""
+
+import numpy as np
+import torch
+
+from . import _lib
+
+# The NF4 code book of the QLoRA paper (Dettmers et al., 2023, appendix E): quantiles of N(0,1)
+# normalised to [-1, 1], with an exact zero.
+NF4_CODE = (
+    -1.0, -0.6961928009986877, -0.5250730514526367, -0.39491748809814453,
+    -0.28444138169288635, -0.18477343022823334, -0.09105003625154495, 0.0,
+    0.07958029955625534, 0.16093020141124725, 0.24611230194568634, 0.33791524171829224,
+    0.44070982933044434, 0.5626170039176941, 0.7229568362236023, 1.0,
+)
+
+
+def signed_dynamic_code(exponent_bits=7):
+    """The 256-entry signed dynamic-tree code book used for the second-level scales.
+
+    Dynamic tree quantisation (Dettmers, "8-bit approximations for parallelism in deep
+    learning", 2016): for decade e = 0..exponent_bits-1 the magnitudes 10^(e-exponent_bits+1)
+    times the midpoints of 2^e + 1 evenly spaced points in [0.1, 1], with both signs; plus 0
+    and 1. Sorted ascending (the quantiser searches it)."""
+    vals = []
+    for e in range(exponent_bits):
+        pts = np.linspace(0.1, 1.0, 2 ** e + 1)
+        mids = (pts[:-1] + pts[1:]) / 2.0
+        mag = (10.0 ** (e - exponent_bits + 1)) * mids
+        vals.extend(mag.tolist())
+        vals.extend((-mag).tolist())
+    vals += [0.0, 1.0]
+    vals += [0.0] * (256 - len(vals))
+    return torch.tensor(sorted(vals), dtype=torch.float32)
+
+
+_NF4_TABLES = {}
+_CODE2_TABLES = {}
+
+
+def nf4_table(device):
+    """The NF4 code book as fp32 on `device` (cached per device)."""
+    key = torch.device(device)
+    table = _NF4_TABLES.get(key)
+    if table is None:
+        table = torch.tensor(NF4_CODE, dtype=torch.float32, device=key)
+        _NF4_TABLES[key] = table
+    return table
+
+
+def _code2_table(device):
+    key = torch.device(device)
+    table = _CODE2_TABLES.get(key)
+    if table is None:
+        table = signed_dynamic_code().to(key)
+        _CODE2_TABLES[key] = table
+    return table
+
+
+class QuantState:
+    """The attributes of bitsandbytes' QuantState that the kernels read (duck-type compatible):
+    shape, dtype, blocksize, quant_type, code (the NF4 table), absmax, nested, offset, state2."""
+
+    def __init__(self, absmax, shape=None, code=None, blocksize=None, quant_type="nf4",
+                 dtype=None, offset=None, state2=None):
+        self.absmax = absmax
+        self.shape = shape
+        self.code = code
+        self.blocksize = blocksize
+        self.quant_type = quant_type
+        self.dtype = dtype
+        self.offset = offset
+        self.state2 = state2
+        self.nested = state2 is not None
+
+    def to(self, device):
+        """Moves every tensor to `device` (like bitsandbytes' QuantState.to)."""
+        self.absmax = self.absmax.to(device)
+        if self.code is not None:
+            self.code = self.code.to(device)
+        if self.nested:
+            if torch.is_tensor(self.offset):
+                self.offset = self.offset.to(device)
+            self.state2.absmax = self.state2.absmax.to(device)
+            self.state2.code = self.state2.code.to(device)
+        return self
+
+
+def supported(quant_state):
+    """True when the kernels handle this quant state: NF4, 2-D, even block sizes."""
+    return (quant_state is not None and quant_state.quant_type == "nf4"
+            and len(quant_state.shape) == 2 and quant_state.blocksize % 2 == 0
+            and (not quant_state.nested or quant_state.state2.blocksize % 2 == 0))
+
+
+def quantize_nf4(weight, blocksize=64, compress_statistics=True, blocksize2=256):
+    """(packed uint8 [n/2, 1], QuantState) of a 2-D CUDA weight, in the layout that
+    bitsandbytes' quantize_4bit(quant_type="nf4") produces: blockwise absmax, nearest NF4 code,
+    high nibble first; with compress_statistics the block scales are double-quantised.
+    One device->host read fetches the offset (a Python float in the returned state)."""
+    _lib.require_cuda(weight, what="quantize_nf4")
+    if weight.dim() != 2:
+        raise ValueError("quantize_nf4: expects a 2-D weight")
+    w = weight.contiguous()
+    n = w.numel()
+    if n % 2:
+        raise ValueError("quantize_nf4: the weight must have an even number of elements")
+    dev = w.device
+    lut = nf4_table(dev)
+    n_blocks = (n + blocksize - 1) // blocksize
+    packed = torch.empty((n // 2, 1), dtype=torch.uint8, device=dev)
+    absmax = torch.empty(n_blocks, dtype=torch.float32, device=dev)
+    s = _lib.stream(dev)
+    _lib.call("qb_nf4_quantize", w.data_ptr(), _lib.tag(w.dtype), n, blocksize, lut.data_ptr(),
+              packed.data_ptr(), absmax.data_ptr(), s)
+    state = QuantState(absmax=absmax, shape=torch.Size(w.shape), code=lut, blocksize=blocksize,
+                       quant_type="nf4", dtype=w.dtype)
+    if compress_statistics:
+        code2 = _code2_table(dev)
+        n2 = (n_blocks + blocksize2 - 1) // blocksize2
+        q = torch.empty(n_blocks, dtype=torch.uint8, device=dev)
+        absmax2 = torch.empty(n2, dtype=torch.float32, device=dev)
+        offset = torch.empty(1, dtype=torch.float32, device=dev)
+        ws = torch.empty(int(_lib.load().qb_nf4_double_quant_workspace(n_blocks)),
+                         dtype=torch.uint8, device=dev)
+        _lib.call("qb_nf4_double_quant", absmax.data_ptr(), n_blocks, blocksize2, code2.data_ptr(),
+                  q.data_ptr(), absmax2.data_ptr(), offset.data_ptr(), ws.data_ptr(), s)
+        state2 = QuantState(absmax=absmax2, code=code2, blocksize=blocksize2,
+                            quant_type="dynamic", dtype=torch.float32)
+        state = QuantState(absmax=q, shape=torch.Size(w.shape), code=lut, blocksize=blocksize,
+                           quant_type="nf4", dtype=w.dtype, offset=float(offset.item()),
+                           state2=state2)
+    return packed, state
+
+
+def dequantize_nf4(packed, quant_state, dtype=torch.float16, out=None):
+    """The weight [out_features, in_features] in `dtype`, rebuilt from the packed NF4 bytes.
+    Bit-exact with the reference kernel: fp32 scale = code2[q]*absmax2 + offset (two roundings),
+    w = nf4[nibble]*scale, rounded to nearest even in `dtype`."""
+    _lib.require_cuda(packed, what="dequantize_nf4")
+    shape = tuple(quant_state.shape)
+    if out is None:
+        out = torch.empty(shape, dtype=dtype, device=packed.device)
+    n = out.numel()
+    if quant_state.nested:
+        absmax = quant_state.absmax.contiguous()
+        code2 = quant_state.state2.code.float().contiguous()
+        absmax2 = quant_state.state2.absmax.float().contiguous()
+        offset = float(quant_state.offset)
+        blocksize2 = int(quant_state.state2.blocksize)
+        c2p, a2p = code2.data_ptr(), absmax2.data_ptr()
+    else:
+        absmax = quant_state.absmax.float().contiguous()
+        offset, blocksize2, c2p, a2p = 0.0, 2, None, None
+    lut = nf4_table(packed.device)
+    packed = packed.reshape(-1)
+    n_blocks = absmax.numel()
+    work = (n // 2 + n * out.element_size() + n_blocks * absmax.element_size()
+            + (quant_state.state2.absmax.numel() * 4 if quant_state.nested else 0), 0)
+    _lib.call("qb_nf4_dequant", packed.data_ptr(), n, absmax.data_ptr(),
+              int(bool(quant_state.nested)), c2p, a2p, offset, int(quant_state.blocksize),
+              blocksize2, lut.data_ptr(), out.data_ptr(), _lib.tag(out.dtype),
+              _lib.stream(packed.device), work=work)
+    return out
+
+
+class NF4Linear(torch.autograd.Function):
+    """y = x @ W.T + b, W rebuilt from NF4 in forward and again in backward (nothing dense is kept
+    between them). W and b are frozen: the backward returns dX only (nf4.py:95-112)."""
+
+    @staticmethod
+    def forward(ctx, x, packed, quant_state, bias):
+        weight = dequantize_nf4(packed, quant_state, x.dtype)
+        out = torch.nn.functional.linear(x, weight, bias)
+        ctx.packed, ctx.quant_state = packed, quant_state
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        grad_x = None
+        if ctx.needs_input_grad[0]:
+            weight = dequantize_nf4(ctx.packed, ctx.quant_state, grad_out.dtype)
+            grad_x = torch.matmul(grad_out, weight)
+        return grad_x, None, None, None
+
+
+def _prepare(module, x):
+    """The part of bitsandbytes' Linear4bit.forward before the matmul: (x, bias, input dtype), or
+    None when the layer must take the original path (nf4.py:115-138)."""
+    try:
+        from bitsandbytes.nn.modules import fix_4bit_weight_quant_state_from_module
+    except ImportError:
+        fix_4bit_weight_quant_state_from_module = None
+    if fix_4bit_weight_quant_state_from_module is not None:
+        fix_4bit_weight_quant_state_from_module(module)
+    quant_state = getattr(module.weight, "quant_state", None)
+    if (not x.is_cuda or not supported(quant_state) or module.weight.requires_grad
+            or (module.bias is not None and module.bias.requires_grad)):
+        return None
+    if not getattr(module, "compute_type_is_set", True):
+        module.set_compute_type(x)
+        module.compute_type_is_set = True
+    inp_dtype = x.dtype
+    compute_dtype = getattr(module, "compute_dtype", None)
+    if compute_dtype is not None:
+        x = x.to(compute_dtype)
+    if x.dtype not in (torch.float16, torch.float32, torch.bfloat16):
+        return None
+    bias = module.bias
+    if bias is not None:
+        if bias.dtype != x.dtype:
+            bias.data = bias.data.to(x.dtype)
+        bias = bias.to(x.dtype)
+    return x, bias, inp_dtype
+
+
+_ORIGINAL = {}
+
+
+def linear4bit(module, x, keep_compute_dtype=False):
+    """bitsandbytes' Linear4bit.forward on our kernels. With keep_compute_dtype the output stays
+    in the compute dtype instead of being cast back to the input dtype (nf4.py:141-149)."""
+    prepared = _prepare(module, x)
+    if prepared is None:
+        original = _ORIGINAL.get("forward")
+        if original is None:
+            raise RuntimeError("linear4bit: unsupported layer and no original forward to fall back to")
+        return original(module, x)
+    x, bias, inp_dtype = prepared
+    out = NF4Linear.apply(x, module.weight, module.weight.quant_state, bias)
+    return out if keep_compute_dtype else out.to(inp_dtype)
+
+
+def patch_linear4bit():
+    """Routes bitsandbytes' Linear4bit.forward through linear4bit (nf4.py:155-166)."""
+    import bitsandbytes.nn.modules as bnb_modules
+
+    cls = bnb_modules.Linear4bit
+    if "forward" in _ORIGINAL:
+        return
+    _ORIGINAL["forward"] = cls.forward
+
+    def forward(self, x):
+        return linear4bit(self, x)
+
+    cls.forward = forward
+
+
+def project(layer, x):
+    """An MLP projection that keeps its output in the compute dtype when it is a plain 4-bit
+    layer; anything else runs as it is (nf4.py:169-176)."""
+    try:
+        import bitsandbytes.nn.modules as bnb_modules
+        plain = (bnb_modules.Linear4bit, bnb_modules.LinearNF4)
+    except ImportError:
+        plain = ()
+    if type(layer) in plain:
+        return linear4bit(layer, x, keep_compute_dtype=True)
+    return layer(x)

@@ -1,0 +1,206 @@
+"""A Qwen2.5-shaped QLoRA training step built from this package's ops.
+
+The model is the Qwen2 decoder (RMSNorm -> q/k/v -> RoPE -> causal GQA attention -> o ->
+residual -> RMSNorm -> gate/up -> SwiGLU -> down -> residual) with every linear a frozen NF4
+(blocksize 64, double-quantised scales) base plus a trainable LoRA adapter, a final RMSNorm and a
+frozen bf16 lm_head feeding the fused linear cross-entropy. Weights are random (N(0, 0.02)
+before quantisation; LoRA A Kaiming-uniform, B N(0, 0.01)); there is no checkpoint to load.
+Attention is torch's scaled_dot_product_attention (the reference never patches attention).
+
+Per-rank data parallelism lives in dp.py; this module is single-device.
+"""
+
+import math
+from dataclasses import dataclass, replace
+
+import torch
+import torch.nn.functional as F
+
+from .cross_entropy import fused_causal_lm_loss
+from .lora import DropoutCast, ScaledAdd
+from .nf4 import NF4Linear, quantize_nf4
+from .rmsnorm import rmsnorm
+from .rope import CudaRoPE
+from .swiglu import swiglu
+
+
+@dataclass(frozen=True)
+class QwenShape:
+    name: str
+    hidden: int
+    intermediate: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    vocab: int
+    tie_embeddings: bool
+    theta: float = 1e6
+    eps: float = 1e-6
+    lora_r: int = 16
+    lora_alpha: int = 32
+    lora_dropout: float = 0.05
+
+
+PRESETS = {
+    # Qwen2.5-0.5B shapes, r=16
+    "0.5b": QwenShape("qwen2.5-0.5b", 896, 4864, 24, 14, 2, 64, 151936, True),
+    # Qwen2.5-1.5B shapes, r=16
+    "1.5b": QwenShape("qwen2.5-1.5b", 1536, 8960, 28, 12, 2, 128, 151936, True),
+    # Qwen2.5-7B shapes, r=64 alpha=128
+    "7b": QwenShape("qwen2.5-7b", 3584, 18944, 28, 28, 4, 128, 152064, False,
+                    lora_r=64, lora_alpha=128),
+}
+
+
+def preset(name, **overrides):
+    return replace(PRESETS[name], **overrides)
+
+
+class LoRANF4Linear(torch.nn.Module):
+    """y = x @ deq(W).T + b + (alpha/r) * dropout(x) @ A.T @ B.T with W frozen in NF4."""
+
+    def __init__(self, in_features, out_features, bias, shape, device, gen):
+        super().__init__()
+        w = torch.empty(out_features, in_features, device=device, dtype=torch.bfloat16)
+        w.normal_(0.0, 0.02, generator=gen)
+        self.packed, self.quant_state = quantize_nf4(w)
+        del w
+        self.bias = None
+        if bias:
+            b = torch.empty(out_features, device=device, dtype=torch.bfloat16)
+            self.bias = b.normal_(0.0, 0.02, generator=gen)
+        r = shape.lora_r
+        a = torch.empty(r, in_features, device=device, dtype=torch.float32)
+        bound = 1.0 / math.sqrt(in_features)    # kaiming_uniform_(a=sqrt(5)), as nn.Linear/peft
+        a.uniform_(-bound, bound, generator=gen)
+        b = torch.empty(out_features, r, device=device, dtype=torch.float32)
+        b.normal_(0.0, 0.01, generator=gen)
+        self.lora_A = torch.nn.Parameter(a)
+        self.lora_B = torch.nn.Parameter(b)
+        self.scaling = shape.lora_alpha / r
+        self.p = shape.lora_dropout
+        self.in_features, self.out_features = in_features, out_features
+
+    def forward(self, x, seed):
+        base = NF4Linear.apply(x, self.packed, self.quant_state, self.bias)
+        p = self.p if self.training else 0.0
+        xd = DropoutCast.apply(x, p, seed, x.dtype) if p > 0 else x
+        lo = F.linear(F.linear(xd, self.lora_A.to(x.dtype)), self.lora_B.to(x.dtype))
+        return ScaledAdd.apply(base, lo, self.scaling)
+
+
+_PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+class DecoderLayer(torch.nn.Module):
+    def __init__(self, shape, device, gen):
+        super().__init__()
+        s = shape
+        H, I, D = s.hidden, s.intermediate, s.head_dim
+        self.shape = s
+        self.ln1 = torch.ones(H, device=device, dtype=torch.bfloat16)
+        self.ln2 = torch.ones(H, device=device, dtype=torch.bfloat16)
+        self.q = LoRANF4Linear(H, s.heads * D, True, s, device, gen)
+        self.k = LoRANF4Linear(H, s.kv_heads * D, True, s, device, gen)
+        self.v = LoRANF4Linear(H, s.kv_heads * D, True, s, device, gen)
+        self.o = LoRANF4Linear(s.heads * D, H, False, s, device, gen)
+        self.gate = LoRANF4Linear(H, I, False, s, device, gen)
+        self.up = LoRANF4Linear(H, I, False, s, device, gen)
+        self.down = LoRANF4Linear(I, H, False, s, device, gen)
+
+    def forward(self, h, cos, sin, seed):
+        s = self.shape
+        B, S, _ = h.shape
+        x = rmsnorm(h, self.ln1, s.eps)
+        q = self.q(x, seed + 0).view(B, S, s.heads, s.head_dim).transpose(1, 2)
+        k = self.k(x, seed + 1).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        v = self.v(x, seed + 2).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        q, k = CudaRoPE.apply(q, k, cos, sin)
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
+        h = h + self.o(a, seed + 3)
+        x = rmsnorm(h, self.ln2, s.eps)
+        m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
+        return h + self.down(m, seed + 6)
+
+
+class QwenQLoRA(torch.nn.Module):
+    """The full model: embedding -> layers -> final norm -> fused linear CE."""
+
+    def __init__(self, shape, device="cuda", seed=0, checkpoint=True):
+        super().__init__()
+        self.shape = shape
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        emb = torch.empty(shape.vocab, shape.hidden, device=dev, dtype=torch.bfloat16)
+        self.embed = emb.normal_(0.0, 0.02, generator=gen)
+        self.layers = torch.nn.ModuleList(DecoderLayer(shape, dev, gen)
+                                          for _ in range(shape.layers))
+        self.norm = torch.ones(shape.hidden, device=dev, dtype=torch.bfloat16)
+        if shape.tie_embeddings:
+            self.lm_head = self.embed
+        else:
+            head = torch.empty(shape.vocab, shape.hidden, device=dev, dtype=torch.bfloat16)
+            self.lm_head = head.normal_(0.0, 0.02, generator=gen)
+        self.checkpoint = checkpoint
+        self._rope = {}
+        self.step_seed = 0
+
+    def rope_tables(self, seq, device):
+        key = (seq, device)
+        if key not in self._rope:
+            D = self.shape.head_dim
+            inv = 1.0 / (self.shape.theta ** (torch.arange(0, D, 2, dtype=torch.float32,
+                                                           device=device) / D))
+            pos = torch.arange(seq, dtype=torch.float32, device=device)
+            emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)[None]
+            self._rope[key] = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16))
+        return self._rope[key]
+
+    def forward(self, input_ids, labels, num_items_in_batch=None):
+        B, S = input_ids.shape
+        cos, sin = self.rope_tables(S, input_ids.device)
+        h = F.embedding(input_ids, self.embed)
+        for i, layer in enumerate(self.layers):
+            # per (step, layer) seeds: a checkpoint recompute replays the same dropout masks
+            seed = (self.step_seed * 1_000_003 + i * 7919) & 0x7FFFFFFF
+            if self.checkpoint and self.training:
+                h = torch.utils.checkpoint.checkpoint(layer, h, cos, sin, seed,
+                                                      use_reentrant=False)
+            else:
+                h = layer(h, cos, sin, seed)
+        h = rmsnorm(h, self.norm, self.shape.eps)
+        return fused_causal_lm_loss(h, self.lm_head, labels, num_items_in_batch=num_items_in_batch)
+
+    def adapter_parameters(self):
+        return [p for p in self.parameters() if p.requires_grad]
+
+
+def synthetic_batch(shape, batch, seq, device, seed, ignore_frac=0.05):
+    """Token ids uniform in [0, vocab), labels = ids with ~ignore_frac set to -100 (shifted
+    inside the loss, as ForCausalLMLoss does)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    ids = torch.randint(0, shape.vocab, (batch, seq), device=device, generator=gen)
+    labels = ids.clone()
+    labels[torch.rand(batch, seq, device=device, generator=gen) < ignore_frac] = -100
+    return ids, labels
+
+
+def make_optimizer(model, lr=1e-4):
+    """AdamW on the adapters only (the NF4 base, norms and head are frozen buffers)."""
+    return torch.optim.AdamW(model.adapter_parameters(), lr=lr, betas=(0.9, 0.999),
+                             weight_decay=0.0, fused=True)
+
+
+def train_step(model, opt, input_ids, labels, grad_sync=None, num_items_in_batch=None):
+    """One optimizer step; returns the loss tensor (on the device, not synchronised)."""
+    model.train()
+    loss, _ = model(input_ids, labels, num_items_in_batch=num_items_in_batch)
+    loss.backward()
+    if grad_sync is not None:
+        grad_sync()
+    opt.step()
+    opt.zero_grad(set_to_none=False)
+    model.step_seed += 1
+    return loss.detach()

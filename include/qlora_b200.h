@@ -1,0 +1,160 @@
+/* qlora_b200 — C-ABI of the B200 (sm_100a) kernel suite for the Qwen2.5 QLoRA training step.
+ *
+ * Every entry point takes plain device pointers, element counts, strides in elements, dtype
+ * tags and a cudaStream_t, launches on that stream and returns a status (QB_OK = 0). A nonzero
+ * status leaves a message for qb_last_error() on the calling thread. The caller owns all memory;
+ * no entry point allocates device memory except where its comment says so. No entry point
+ * synchronises the stream.
+ *
+ * Each declaration names the reference function (imoshka2009-lab/hackathon, `solution/`) whose
+ * kernel it replaces, by file:line.
+ */
+#ifndef QLORA_B200_H
+#define QLORA_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define QB_OK 0
+#define QB_ERR_INVALID 1     /* bad argument: shape, stride, dtype, alignment, null pointer */
+#define QB_ERR_CUDA 2        /* a CUDA call or launch failed */
+#define QB_ERR_UNSUPPORTED 3 /* valid input this build has no kernel for */
+#define QB_ERR_TIMEOUT 4     /* a bounded device-side wait gave up */
+
+/* dtype tags (the same numbers as solution/_common.py:19-25 round_mode) */
+#define QB_F32 0
+#define QB_F16 1
+#define QB_BF16 2
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* qb_last_error(void);
+/* Version of this ABI; bumped when a signature changes. */
+int qb_abi_version(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * NF4 with double-quantised absmax (bitsandbytes layout)
+ */
+
+/* Dequantise n_weights NF4 weights into `out` (out_dtype F32/F16/BF16).
+ * Replaces solution/nf4.py:25-49 (nf4_dequant_kernel) and :71-92 (dequantize_nf4).
+ * packed: n_weights/2 bytes, weight 2i in the high nibble of byte i, 2i+1 in the low nibble.
+ * nested=1: absmax is uint8 [ceil(n/blocksize)] codes into code2[256] (fp32), second-level
+ *   scales absmax2 fp32 [ceil(nblocks/blocksize2)] and the fp32 `offset`:
+ *   scale = code2[absmax[b]] * absmax2[b / blocksize2] + offset   (a rounded multiply, then a
+ *   rounded add: no fused multiply-add), w = lut16[nibble] * scale, then rounded to out_dtype.
+ * nested=0: absmax is fp32 [nblocks]; code2, absmax2 and offset are ignored.
+ * blocksize (and blocksize2 when nested) must be even; n_weights must be even. */
+int qb_nf4_dequant(const uint8_t* packed, int64_t n_weights, const void* absmax, int nested,
+                   const float* code2, const float* absmax2, float offset, int blocksize,
+                   int blocksize2, const float* lut16, void* out, int out_dtype,
+                   cudaStream_t stream);
+
+/* First-level NF4 quantisation of w (w_dtype F32/F16/BF16, n_weights even): per block of
+ * `blocksize` weights absmax[b] = max|w|, each weight -> index of the nearest lut16 entry to
+ * w/absmax, packed two per byte (high nibble first). The input producer of the format
+ * qb_nf4_dequant reads (bitsandbytes quantize_4bit, used at solution/test_kernels.py:48-49). */
+int qb_nf4_quantize(const void* w, int w_dtype, int64_t n_weights, int blocksize,
+                    const float* lut16, uint8_t* packed, float* absmax, cudaStream_t stream);
+
+/* Second-level (double) quantisation of the fp32 block scales: offset = mean(absmax) (written
+ * to *offset_dev), then per block of blocksize2 scales absmax2[j] = max|absmax - offset| and
+ * absmax_q[b] = index of the code2 entry nearest to (absmax[b] - offset) / absmax2[j].
+ * code2 must be sorted ascending. `workspace` is caller-owned device memory of
+ * qb_nf4_double_quant_workspace(n_blocks) bytes. */
+int64_t qb_nf4_double_quant_workspace(int64_t n_blocks);
+int qb_nf4_double_quant(const float* absmax, int64_t n_blocks, int blocksize2,
+                        const float* code2, uint8_t* absmax_q, float* absmax2,
+                        float* offset_dev, void* workspace, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * RMSNorm (Qwen2RMSNorm), frozen weight
+ */
+
+/* y = w * round_x(x * rstd), rstd = 1/sqrt(mean(x^2) + eps) per row, stored to rstd[rows].
+ * round_x rounds through x's dtype when x is F16/BF16 (no-op for F32). Row strides in elements;
+ * the last dimension is contiguous. Replaces solution/rmsnorm.py:25-39 (rmsnorm_fwd_kernel). */
+int qb_rmsnorm_fwd(const void* x, int x_dtype, int64_t x_row_stride, const void* w, int w_dtype,
+                   void* y, int y_dtype, int64_t y_row_stride, float* rstd, int64_t rows,
+                   int64_t cols, float eps, cudaStream_t stream);
+
+/* dx = rstd * (g - x * rstd^2 * mean(g * x)), g = dy * w. No weight gradient (frozen).
+ * Replaces solution/rmsnorm.py:43-55 (rmsnorm_bwd_kernel). */
+int qb_rmsnorm_bwd(const void* dy, int dy_dtype, int64_t dy_row_stride, const void* x,
+                   int x_dtype, int64_t x_row_stride, const void* w, int w_dtype,
+                   const float* rstd, void* dx, int dx_dtype, int64_t dx_row_stride,
+                   int64_t rows, int64_t cols, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * RoPE on q and k in one launch
+ */
+
+/* Rotate-half RoPE. q [B,HQ,S,D] and k [B,HK,S,D] with arbitrary element strides
+ * (q_strides = {b,h,s}; the last dimension is contiguous), cos/sin [B or broadcast, S, D] with
+ * strides cs_stride_b (0 to broadcast) and cs_stride_s. Halves (x1,x2), (c1,c2), (s1,s2):
+ *   forward : o1 = x1*c1 - x2*s1, o2 = x2*c2 + x1*s2
+ *   backward: d1 = g1*c1 + g2*s2, d2 = g2*c2 - g1*s1
+ * q/k share in_dtype, q_out/k_out share out_dtype; cos and sin share cs_dtype.
+ * Replaces solution/rope.py:25-62 (rope_qk_kernel) and :65-75 (_launch). */
+int qb_rope_qk(const void* q, const void* k, void* q_out, void* k_out, const void* cos_,
+               const void* sin_, int in_dtype, int out_dtype, int cs_dtype, int64_t B,
+               int64_t HQ, int64_t HK, int64_t S, int64_t D, const int64_t* q_strides,
+               const int64_t* k_strides, const int64_t* qo_strides, const int64_t* ko_strides,
+               int64_t cs_stride_b, int64_t cs_stride_s, int backward, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * SwiGLU
+ */
+
+/* out = silu(gate) * up over n contiguous elements (fp32 math).
+ * Replaces solution/swiglu.py:15-22 (example_swiglu_fwd_kernel). */
+int qb_swiglu_fwd(const void* gate, const void* up, void* out, int dtype, int64_t n,
+                  cudaStream_t stream);
+/* dup = g*silu(gate); dgate = g*up*sig*(1 + gate*(1-sig)).
+ * Replaces solution/swiglu.py:25-37 (example_swiglu_bwd_kernel). */
+int qb_swiglu_bwd(const void* grad, const void* gate, const void* up, void* dgate, void* dup,
+                  int dtype, int64_t n, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * LoRA dropout + cast, scaled add
+ */
+
+/* out[r,c] = in[r,c] * keep * scale, keep = (u > p) with u the Philox-4x32-10 uniform of
+ * (seed, int32(r*cols + c)) — the stream of Triton's tl.rand, so masks match the reference
+ * bit for bit. With p <= 0: out = in * scale (a cast when scale = 1).
+ * Replaces solution/lora.py:29-46 (lora_dropout_scale_kernel) and :74-81 (_dropout_scale). */
+int qb_dropout_scale(const void* in, int in_dtype, int64_t in_row_stride, void* out,
+                     int out_dtype, int64_t out_row_stride, int64_t rows, int64_t cols,
+                     uint64_t seed, float p, float scale, cudaStream_t stream);
+
+/* out = base + lo * scaling (fp32 math). Replaces solution/lora.py:49-60
+ * (lora_scaled_add_kernel). */
+int qb_scaled_add(const void* base, int base_dtype, int64_t base_row_stride, const void* lo,
+                  int lo_dtype, int64_t lo_row_stride, void* out, int out_dtype,
+                  int64_t out_row_stride, int64_t rows, int64_t cols, float scaling,
+                  cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Cross-entropy over rows of materialised logits (the chunked path)
+ */
+
+/* Per row of logits [rows, vocab] (row_stride in elements): lse, loss = lse - z[label]
+ * (0 when label == -100 or < 0), entropy = lse - sum(softmax*z), argmax (first index of the
+ * max) into pred (int64, may be NULL) and correct (int32: argmax == label and labelled; may be
+ * NULL). With write_grad the row is overwritten in place by (softmax - onehot) * grad_scale
+ * for labelled rows and 0 for the others.
+ * Replaces solution/cross_entropy.py:48-90 (fused_ce_kernel) and solution/fused_ce.py:42-96
+ * (ce_row_kernel, grad_scale = 1). */
+int qb_ce_rows(void* logits, int logits_dtype, int64_t row_stride, const int64_t* target,
+               int64_t rows, int64_t vocab, float* loss, float* entropy, int64_t* pred,
+               int32_t* correct, float grad_scale, int write_grad, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QLORA_B200_H */

@@ -1,0 +1,146 @@
+"""The reference's eager PyTorch path of the QLoRA step, timed on the host CPU — TEST
+INFRASTRUCTURE ONLY (bench.py's `cpu_baseline` and `--impl reference` legs).
+
+The reference is Python + Triton; its only CPU-runnable form of the step is the eager code its
+tests compare against: the Qwen2 decoder layer (solution/test_rmsnorm.py:9-14 RMSNorm,
+test_rope.py:9-17 RoPE, test_kernels.py:24-25 SwiGLU), bitsandbytes-style linears that rebuild
+the bf16 weight from NF4 in forward and again in backward (solution/nf4.py:95-112, the dequant
+here is the C restatement oracle/nf4_ref.c), peft LoRA with dropout, and ForCausalLMLoss over
+the lm_head (test_cross_entropy.py:9-30).
+
+A full 7B step on a CPU takes hours, so this times a bounded SAMPLE: one decoder layer of the
+configured shape on `tokens` tokens (forward, checkpoint recompute, backward) and the head + CE
+on the same rows, and scales to the model: step_time = layers * layer_time + head_time, so
+tokens/s = tokens / step_time. Attention is timed at the sample's sequence length (shorter than
+the configured one), which flatters the CPU; the JSON line says so.
+"""
+
+import os
+import time
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import c_ref, nf4_ref, ops_ref
+
+
+class _DequantLinear(torch.autograd.Function):
+    """F.linear with the weight rebuilt from NF4 in forward and again in backward."""
+
+    @staticmethod
+    def forward(ctx, x, mod):
+        w = mod.dequant()
+        ctx.mod = mod
+        return F.linear(x, w, mod.bias)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g @ ctx.mod.dequant(), None
+
+
+class CpuNF4LoRALinear(torch.nn.Module):
+    def __init__(self, in_f, out_f, bias, r, alpha, p, rng, threads):
+        super().__init__()
+        n = in_f * out_f
+        self.shape = (out_f, in_f)
+        self.packed = rng.integers(0, 256, n // 2, dtype=np.uint8)
+        self.absmax_q = rng.integers(0, 256, n // 64, dtype=np.uint8)
+        from hackathon_b200.nf4 import signed_dynamic_code
+        self.code2 = signed_dynamic_code().numpy()
+        self.absmax2 = (rng.random((n // 64 + 255) // 256) * 0.05 + 0.01).astype(np.float32)
+        self.offset = 0.03
+        self.threads = threads
+        self.bias = (torch.randn(out_f) * 0.02).to(torch.bfloat16) if bias else None
+        self.A = torch.nn.Parameter(torch.empty(r, in_f).uniform_(-in_f ** -0.5, in_f ** -0.5))
+        self.B = torch.nn.Parameter(torch.randn(out_f, r) * 0.01)
+        self.scaling = alpha / r
+        self.p = p
+
+    def dequant(self):
+        bits = c_ref.dequant_nf4_bf16(self.packed, self.shape[0] * self.shape[1], self.absmax_q,
+                                      self.code2, self.absmax2, self.offset, 64, 256,
+                                      threads=self.threads)
+        return torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).view(self.shape)
+
+    def forward(self, x):
+        base = _DequantLinear.apply(x, self)
+        xd = F.dropout(x, self.p, training=True) if self.p > 0 else x
+        lo = F.linear(F.linear(xd, self.A.to(x.dtype)), self.B.to(x.dtype))
+        return base + lo * self.scaling
+
+
+class CpuDecoderLayer(torch.nn.Module):
+    def __init__(self, shape, rng, threads):
+        super().__init__()
+        s = shape
+        H, I, D = s.hidden, s.intermediate, s.head_dim
+        mk = lambda i, o, b: CpuNF4LoRALinear(i, o, b, s.lora_r, s.lora_alpha, s.lora_dropout,
+                                             rng, threads)
+        self.s = s
+        self.q, self.k, self.v = mk(H, s.heads * D, True), mk(H, s.kv_heads * D, True), \
+            mk(H, s.kv_heads * D, True)
+        self.o = mk(s.heads * D, H, False)
+        self.gate, self.up, self.down = mk(H, I, False), mk(H, I, False), mk(I, H, False)
+        self.ln1 = torch.ones(H, dtype=torch.bfloat16)
+        self.ln2 = torch.ones(H, dtype=torch.bfloat16)
+
+    def forward(self, h, cos, sin):
+        s = self.s
+        B, S, _ = h.shape
+        x = ops_ref.rmsnorm_ref(h, self.ln1, s.eps)
+        q = self.q(x).view(B, S, s.heads, s.head_dim).transpose(1, 2)
+        k = self.k(x).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        v = self.v(x).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        q, k = ops_ref.rope_ref(q, k, cos, sin)
+        rep = s.heads // s.kv_heads
+        a = F.scaled_dot_product_attention(q, k.repeat_interleave(rep, 1),
+                                           v.repeat_interleave(rep, 1), is_causal=True)
+        h = h + self.o(a.transpose(1, 2).reshape(B, S, -1))
+        x = ops_ref.rmsnorm_ref(h, self.ln2, s.eps)
+        m = ops_ref.swiglu_ref(self.gate(x), self.up(x)).to(x.dtype)
+        return h + self.down(m)
+
+
+def time_sample(shape, tokens=128, threads=None, repeats=1, seed=0):
+    """(tokens/s scaled to the whole model, description dict) of the eager CPU path."""
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(seed)
+    torch.manual_seed(seed)
+    layer = CpuDecoderLayer(shape, rng, threads)
+    cos, sin = ops_ref.qwen_cos_sin(1, tokens, shape.head_dim, shape.theta, torch.bfloat16)
+    h0 = (torch.randn(1, tokens, shape.hidden) * 0.5).to(torch.bfloat16)
+    head = (torch.randn(shape.vocab, shape.hidden) * 0.02).to(torch.bfloat16)
+    labels = torch.randint(0, shape.vocab, (1, tokens))
+
+    def layer_step():
+        with torch.no_grad():            # the checkpoint's first forward
+            layer(h0, cos, sin)
+        h = h0.clone().requires_grad_()
+        out = layer(h, cos, sin)         # recompute in backward
+        out.float().sum().backward()
+
+    def head_step():
+        hn = h0.clone().float().requires_grad_()
+        loss = ops_ref.ce_ref(hn, head, labels, matmul_dtype=torch.bfloat16)[0]
+        loss.backward()
+
+    layer_step()  # warm-up (allocations, thread pools)
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        layer_step()
+    t_layer = (time.perf_counter() - t0) / repeats
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        head_step()
+    t_head = (time.perf_counter() - t0) / repeats
+    step = shape.layers * t_layer + t_head
+    desc = {
+        "sample": (f"1 decoder layer ({shape.name} shapes) fwd + checkpoint recompute + bwd on "
+                   f"{tokens} tokens (seq {tokens}), NF4 rebuilt by the C oracle per forward "
+                   f"and backward, x{shape.layers} layers, + lm_head/CE fwd+bwd on the same "
+                   f"rows; attention at seq {tokens}"),
+        "layer_s": round(t_layer, 4), "head_s": round(t_head, 4),
+    }
+    return tokens / step, threads, desc

@@ -1,0 +1,108 @@
+"""The C-ABI library on the CPU: it loads, exports every entry point include/*.h declares, the
+ctypes binding covers them, and the ops refuse non-CUDA tensors (there is no CPU path)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+
+def _declared():
+    names = set()
+    inc = os.path.join(ROOT, "include")
+    for f in os.listdir(inc):
+        if f.endswith(".h"):
+            src = open(os.path.join(inc, f)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(qb_[a-z0-9_]+)\s*\(", src))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from hackathon_b200 import _lib
+    lib = _lib.load()
+    declared = _declared()
+    assert declared, "no declarations found"
+    for name in sorted(declared):
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        ctypes.cast(getattr(lib, name), ctypes.c_void_p)
+    assert declared <= set(_lib.exported_symbols()), declared - set(_lib.exported_symbols())
+    assert lib.qb_abi_version() >= 1
+
+
+def test_error_message_plumbing_without_gpu():
+    """Argument checks run before any CUDA call, so they work here."""
+    from hackathon_b200 import _lib
+    lib = _lib.load()
+    rc = lib.qb_nf4_dequant(None, 3, None, 0, None, None, 0.0, 64, 256, None, None, 2, None)
+    assert rc == 1
+    assert b"even" in lib.qb_last_error()
+    rc = lib.qb_rmsnorm_fwd(None, 0, 0, None, 0, None, 0, 0, None, 4, 0, 1e-6, None)
+    assert rc == 1 and b"bad shape" in lib.qb_last_error()
+    with pytest.raises(RuntimeError, match="qb_swiglu_fwd failed"):
+        _lib.call("qb_swiglu_fwd", None, None, None, 2, -1, None)
+
+
+@pytest.mark.parametrize("op", ["rmsnorm", "rope", "swiglu", "dropout", "dequant"])
+def test_ops_refuse_cpu_tensors(op):
+    import hackathon_b200 as hb
+    from hackathon_b200 import lora, nf4, rmsnorm, rope, swiglu
+    x = torch.randn(2, 4, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        if op == "rmsnorm":
+            rmsnorm.rmsnorm(x, torch.ones(8), 1e-6)
+        elif op == "rope":
+            rope.TritonRoPE.apply(x[None], x[None], x, x)
+        elif op == "swiglu":
+            swiglu.swiglu(x, x)
+        elif op == "dropout":
+            lora.DropoutCast.apply(x, 0.1, 1, torch.float32)
+        else:
+            st = nf4.QuantState(absmax=torch.ones(1), shape=(2, 4), blocksize=64)
+            nf4.dequantize_nf4(torch.zeros(4, dtype=torch.uint8), st)
+    assert hb.PATCHES == ("rmsnorm", "rope", "cross_entropy", "lora")
+
+
+def test_quant_state_admission():
+    from hackathon_b200.nf4 import QuantState, supported
+    s2 = QuantState(absmax=torch.ones(1), blocksize=256, quant_type="dynamic")
+    assert supported(QuantState(absmax=torch.ones(1), shape=(4, 64), blocksize=64, state2=s2))
+    assert not supported(QuantState(absmax=torch.ones(1), shape=(4, 64), blocksize=63))
+    assert not supported(QuantState(absmax=torch.ones(1), shape=(4, 4, 4), blocksize=64))
+    assert not supported(QuantState(absmax=torch.ones(1), shape=(4, 64), blocksize=64,
+                                    quant_type="fp4"))
+    assert not supported(None)
+
+
+def test_shift_labels_and_chunked_step_host_logic():
+    from hackathon_b200.cross_entropy import ChunkedStep, shift_labels_of
+    labels = torch.tensor([[1, 2, 3], [4, -100, 6]])
+    assert shift_labels_of(labels).tolist() == [[2, 3, -100], [-100, 6, -100]]
+    target = shift_labels_of(labels)
+    pred = torch.tensor([[2, 0, 0], [0, 6, 1]])
+    st = ChunkedStep(torch.zeros(2, 3), torch.zeros(2, 3), pred, target)
+    assert int(st.labelled) == 3 and int(st.correct) == 2
+
+
+def test_rope_supported_guard():
+    from hackathon_b200.rope import _supported
+    q = torch.randn(1, 2, 3, 8)
+    assert not _supported(q, q, q[0], q[0], 1)   # CPU tensors go to the original
+
+
+def test_apply_is_idempotent_without_gpu():
+    import hackathon_b200 as hb
+    from transformers.models.qwen2 import modeling_qwen2 as m
+    hb.apply()
+    first = m.Qwen2RMSNorm.forward
+    hb.apply()
+    assert m.Qwen2RMSNorm.forward is first
+    # patched forward hands CPU tensors to the original implementation
+    norm = m.Qwen2RMSNorm(8)
+    x = torch.randn(2, 8)
+    want = norm.weight * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6))
+    torch.testing.assert_close(norm(x), want)

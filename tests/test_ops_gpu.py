@@ -1,0 +1,371 @@
+"""Parity of the CUDA ops (called through the C-ABI) with the reference: against the fixtures the
+reference's kernels produced, and against the pinned CPU oracle on seeded inputs, at the
+reference's test shapes and at BASELINE shapes. Tolerances follow the reference's tests
+(solution/_testing.py:12 TOL, test_*.py) and the stated bars: NF4 bit-exact; RMSNorm / RoPE /
+SwiGLU within atol 1e-2 / rtol 1.6e-2 in bf16."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import nf4_ref, ops_ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-5, torch.float16: 2e-3, torch.bfloat16: 1.6e-2}
+BF16_ATOL = 1e-2
+
+
+def _t(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+# ----------------------------------------------------------------------------------- NF4
+
+def _state_from_golden(g, i, dev):
+    from hackathon_b200.nf4 import QuantState
+    rows, cols, bs, nested, bs2 = (int(v) for v in g[f"nf4_{i}_meta"])
+    if nested:
+        s2 = QuantState(absmax=_t(g[f"nf4_{i}_absmax2"], dev), code=_t(g["nf4_code2"], dev),
+                        blocksize=bs2, quant_type="dynamic")
+        return QuantState(absmax=_t(g[f"nf4_{i}_absmax_q"], dev), shape=(rows, cols),
+                          blocksize=bs, offset=float(g[f"nf4_{i}_offset"][0]), state2=s2)
+    return QuantState(absmax=_t(g[f"nf4_{i}_absmax"], dev), shape=(rows, cols), blocksize=bs)
+
+
+def test_nf4_dequant_bit_exact_vs_reference_fixtures(cuda):
+    from hackathon_b200.nf4 import dequantize_nf4
+    g = golden("nf4")
+    for i in range(5):
+        st = _state_from_golden(g, i, cuda)
+        packed = _t(g[f"nf4_{i}_packed"], cuda).reshape(-1, 1)
+        ref32 = g[f"nf4_{i}_f32"]
+        out32 = dequantize_nf4(packed, st, torch.float32).cpu().numpy()
+        out16 = dequantize_nf4(packed, st, torch.float16).cpu().numpy()
+        outbf = dequantize_nf4(packed, st, torch.bfloat16).cpu().view(torch.int16).numpy()
+        assert np.array_equal(out32.view(np.uint32), ref32.view(np.uint32)), i
+        assert np.array_equal(out16.view(np.uint16), g[f"nf4_{i}_f16"].view(np.uint16)), i
+        assert np.array_equal(outbf.view(np.uint16), nf4_ref.f32_to_bf16_bits(ref32)), i
+
+
+def _oracle_rows(packed_u8, q, absmax2, code2, offset, cols, rows_idx, bs=64, bs2=256):
+    """Oracle bf16 bits of whole rows of a nested-NF4 matrix."""
+    return np.stack([nf4_ref.dequant_nf4(packed_u8, cols, q, True, code2, absmax2, offset, bs,
+                                         bs2, out="bf16", start=r * cols) for r in rows_idx])
+
+
+@pytest.mark.parametrize("shape", [(3584, 3584), (512, 3584), (18944, 3584), (3584, 18944)])
+def test_nf4_quantize_dequant_baseline_shapes(cuda, shape):
+    """Cfg2 shapes: GPU quantiser -> GPU dequant (bf16), rows checked bit for bit against the
+    oracle, and the whole matrix against the quantisation error bound."""
+    from hackathon_b200.nf4 import dequantize_nf4, quantize_nf4
+    gen = torch.Generator(device=cuda).manual_seed(0)
+    w = (torch.randn(shape, generator=gen, device=cuda) * 0.02).to(torch.bfloat16)
+    packed, st = quantize_nf4(w)
+    out = dequantize_nf4(packed, st, torch.bfloat16)
+    rows = [0, 1, shape[0] // 2, shape[0] - 1]
+    want = _oracle_rows(packed.cpu().numpy().reshape(-1), st.absmax.cpu().numpy(),
+                        st.state2.absmax.cpu().numpy(), st.state2.code.cpu().numpy(),
+                        st.offset, shape[1], rows)
+    got = out[rows].cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, want)
+    blocks = w.float().abs().reshape(-1, 64).amax(1).repeat_interleave(64).view(shape)
+    assert torch.all((out.float() - w.float()).abs() <= 0.17 * blocks + 1e-6)
+
+
+def test_nf4_quantiser_matches_oracle(cuda):
+    from hackathon_b200.nf4 import quantize_nf4, signed_dynamic_code
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((192, 640)) * 0.03).astype(np.float32)
+    packed, st = quantize_nf4(_t(w, cuda), compress_statistics=False)
+    ref_packed, ref_absmax = nf4_ref.quantize_nf4(w, 64)
+    assert np.array_equal(packed.cpu().numpy().reshape(-1), ref_packed)
+    assert np.array_equal(st.absmax.cpu().numpy(), ref_absmax)
+    packed2, st2 = quantize_nf4(_t(w, cuda), compress_statistics=True)
+    q, a2, off = nf4_ref.double_quant(ref_absmax, signed_dynamic_code().numpy(), 256)
+    assert abs(st2.offset - float(off)) <= 1e-6 * abs(float(off))
+    np.testing.assert_allclose(st2.state2.absmax.cpu().numpy(), a2, rtol=1e-5)
+    assert (st2.absmax.cpu().numpy() != q).mean() < 0.01
+
+
+@pytest.mark.parametrize("bs,n", [(2, 10), (6, 36), (64, 64 * 7 + 2), (32, 1024)])
+def test_nf4_dequant_generic_blocksizes(cuda, bs, n):
+    """Block sizes the word path does not take (any even size) and ragged lengths."""
+    from hackathon_b200.nf4 import QuantState, dequantize_nf4
+    rng = np.random.default_rng(bs)
+    w = (rng.standard_normal(n) * 0.05).astype(np.float32)
+    packed, absmax = nf4_ref.quantize_nf4(w, bs)
+    st = QuantState(absmax=_t(absmax, cuda), shape=(1, n), blocksize=bs)
+    out = dequantize_nf4(_t(packed, cuda), st, torch.float32).cpu().numpy().reshape(-1)
+    ref = nf4_ref.dequant_nf4(packed, n, absmax, False, None, None, 0.0, bs, 2, out="f32")
+    assert np.array_equal(out.view(np.uint32), ref.view(np.uint32))
+
+
+def test_nf4_rejects_bad_blocksize(cuda):
+    from hackathon_b200.nf4 import QuantState, dequantize_nf4
+    st = QuantState(absmax=torch.ones(4, device=cuda), shape=(2, 8), blocksize=3)
+    with pytest.raises(RuntimeError, match="blocksize"):
+        dequantize_nf4(torch.zeros(8, dtype=torch.uint8, device=cuda), st, torch.float16)
+
+
+def test_nf4_linear_forward_backward(cuda):
+    from hackathon_b200.nf4 import NF4Linear, dequantize_nf4, quantize_nf4
+    torch.manual_seed(0)
+    w = (torch.randn(256, 512, device=cuda) * 0.02).to(torch.bfloat16)
+    packed, st = quantize_nf4(w)
+    bias = torch.randn(256, device=cuda, dtype=torch.bfloat16)
+    x = torch.randn(4, 33, 512, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    y = NF4Linear.apply(x, packed, st, bias)
+    wd = dequantize_nf4(packed, st, torch.bfloat16)
+    xr = x.detach().clone().requires_grad_()
+    yr = torch.nn.functional.linear(xr.float(), wd.float(), bias.float())
+    torch.testing.assert_close(y.float(), yr, rtol=1.6e-2, atol=2e-2)
+    g = torch.randn_like(y)
+    y.backward(g)
+    yr.backward(g.float())
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=1.6e-2, atol=2e-2)
+
+
+# ----------------------------------------------------------------------------------- RMSNorm
+
+@pytest.mark.parametrize("i", range(6))
+def test_rmsnorm_vs_reference_fixtures(cuda, i):
+    from hackathon_b200.rmsnorm import rmsnorm
+    g = golden("rmsnorm")
+    x = _t(g[f"rms_{i}_x"], cuda).requires_grad_()
+    w = _t(g[f"rms_{i}_w"], cuda)
+    y = rmsnorm(x, w, 1e-6)
+    ref = _t(g[f"rms_{i}_y"], cuda)
+    assert y.dtype == ref.dtype
+    tol = TOL[x.dtype]
+    torch.testing.assert_close(y, ref, rtol=tol, atol=tol)
+    y.backward(_t(g[f"rms_{i}_g"], cuda))
+    assert x.grad.dtype == x.dtype
+    torch.testing.assert_close(x.grad, _t(g[f"rms_{i}_dx"], cuda), rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("x_dtype,w_dtype", [(torch.float32, torch.float32),
+                                             (torch.float16, torch.float32),
+                                             (torch.float16, torch.float16),
+                                             (torch.bfloat16, torch.bfloat16),
+                                             (torch.bfloat16, torch.float32)])
+@pytest.mark.parametrize("hidden", [1536, 1000, 3584, 896, 1001])
+def test_rmsnorm_vs_oracle(cuda, x_dtype, w_dtype, hidden):
+    from hackathon_b200.rmsnorm import rmsnorm
+    torch.manual_seed(0)
+    weight = (1 + 0.1 * torch.randn(hidden)).to(w_dtype)
+    x = torch.randn(4, 512, hidden, dtype=x_dtype)
+    dy = torch.randn(4, 512, hidden)
+    xr = x.clone().requires_grad_()
+    yr = ops_ref.rmsnorm_ref(xr, weight, 1e-6)
+    yr.backward(dy.to(yr.dtype))
+    xg = x.to(cuda).requires_grad_()
+    y = rmsnorm(xg, weight.to(cuda), 1e-6)
+    assert y.dtype == yr.dtype and y.shape == yr.shape
+    tol = TOL[x_dtype]
+    atol = BF16_ATOL if x_dtype == torch.bfloat16 else tol
+    torch.testing.assert_close(y.cpu(), yr.detach(), rtol=tol, atol=atol)
+    y.backward(dy.to(cuda).to(y.dtype))
+    torch.testing.assert_close(xg.grad.cpu(), xr.grad, rtol=tol, atol=atol)
+
+
+def test_rmsnorm_strided_rows(cuda):
+    """A row stride larger than the row (a column slice of a wider buffer)."""
+    from hackathon_b200.rmsnorm import rmsnorm
+    torch.manual_seed(1)
+    buf = torch.randn(64, 2048, device=cuda, dtype=torch.bfloat16)
+    x = buf[:, :1536]
+    w = torch.randn(1536, device=cuda, dtype=torch.bfloat16)
+    y = rmsnorm(x, w, 1e-6)
+    yr = ops_ref.rmsnorm_ref(x.cpu(), w.cpu(), 1e-6)
+    torch.testing.assert_close(y.cpu(), yr, rtol=1.6e-2, atol=BF16_ATOL)
+
+
+# ----------------------------------------------------------------------------------- RoPE
+
+@pytest.mark.parametrize("i", range(8))
+def test_rope_vs_reference_fixtures(cuda, i):
+    from hackathon_b200.rope import TritonRoPE
+    g = golden("rope")
+    half, equal, _ = (int(v) for v in g[f"rope_{i}_meta"])
+    t = {k: _t(g[f"rope_{i}_{k}"], cuda) for k in
+         ("q", "k", "cos", "sin", "qo", "ko", "gq", "gk", "dq", "dk")}
+    # rebuild the (B,S,H,D) buffers seen as (B,H,S,D), as the attention does
+    q = t["q"].transpose(1, 2).contiguous().transpose(1, 2).requires_grad_()
+    k = t["k"].transpose(1, 2).contiguous().transpose(1, 2).requires_grad_()
+    qo, ko = TritonRoPE.apply(q, k, t["cos"], t["sin"])
+    tol = (2e-3 if half else 1e-5) * (1 if equal else 4)
+    torch.testing.assert_close(qo, t["qo"], rtol=tol, atol=tol)
+    torch.testing.assert_close(ko, t["ko"], rtol=tol, atol=tol)
+    assert qo.stride() == q.stride()
+    torch.autograd.backward((qo, ko), (t["gq"], t["gk"]))
+    torch.testing.assert_close(q.grad, t["dq"], rtol=tol, atol=tol)
+    torch.testing.assert_close(k.grad, t["dk"], rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(4, 512, 12, 2, 128), (2, 256, 14, 2, 64),
+                                   (1, 4096, 28, 4, 128), (2, 33, 3, 1, 10)])
+def test_rope_vs_oracle(cuda, dtype, shape):
+    from hackathon_b200.rope import TritonRoPE
+    B, S, HQ, HK, D = shape
+    torch.manual_seed(0)
+    q = torch.randn(B, S, HQ, D, dtype=dtype).transpose(1, 2)
+    k = torch.randn(B, S, HK, D, dtype=dtype).transpose(1, 2)
+    cos, sin = ops_ref.qwen_cos_sin(1, S, D, dtype=dtype)
+    qr, kr = q.clone().requires_grad_(), k.clone().requires_grad_()
+    oq_r, ok_r = ops_ref.rope_ref(qr, kr, cos, sin)
+    gq, gk = torch.randn_like(oq_r), torch.randn_like(ok_r)
+    torch.autograd.backward((oq_r, ok_r), (gq, gk))
+    qg = q.to(cuda).requires_grad_()
+    kg = k.to(cuda).requires_grad_()
+    oq, ok = TritonRoPE.apply(qg, kg, cos.to(cuda), sin.to(cuda))
+    torch.autograd.backward((oq, ok), (gq.to(cuda), gk.to(cuda)))
+    tol = TOL[dtype]
+    atol = BF16_ATOL if dtype == torch.bfloat16 else tol
+    for a, b in ((oq, oq_r), (ok, ok_r), (qg.grad, qr.grad), (kg.grad, kr.grad)):
+        torch.testing.assert_close(a.cpu(), b.detach(), rtol=tol, atol=atol)
+
+
+# ----------------------------------------------------------------------------------- SwiGLU
+
+@pytest.mark.parametrize("i", range(2))
+def test_swiglu_vs_reference_fixtures(cuda, i):
+    from hackathon_b200.swiglu import swiglu
+    g = golden("swiglu")
+    gate = _t(g[f"swiglu_{i}_gate"], cuda).requires_grad_()
+    up = _t(g[f"swiglu_{i}_up"], cuda).requires_grad_()
+    y = swiglu(gate, up)
+    tol = TOL[gate.dtype]
+    torch.testing.assert_close(y, _t(g[f"swiglu_{i}_y"], cuda), rtol=tol, atol=tol)
+    y.backward(_t(g[f"swiglu_{i}_grad"], cuda))
+    torch.testing.assert_close(gate.grad, _t(g[f"swiglu_{i}_dgate"], cuda), rtol=tol, atol=tol)
+    torch.testing.assert_close(up.grad, _t(g[f"swiglu_{i}_dup"], cuda), rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(4, 512, 8960), (3, 77, 1001), (1, 2048, 18944)])
+def test_swiglu_vs_oracle(cuda, dtype, shape):
+    from hackathon_b200.swiglu import swiglu
+    torch.manual_seed(0)
+    gate = torch.randn(shape, device=cuda, dtype=dtype, requires_grad=True)
+    up = torch.randn(shape, device=cuda, dtype=dtype, requires_grad=True)
+    grad = torch.randn(shape, device=cuda, dtype=dtype)
+    gr = gate.detach().float().requires_grad_()
+    ur = up.detach().float().requires_grad_()
+    ref = ops_ref.swiglu_ref(gr, ur)
+    ref.backward(grad.float())
+    out = swiglu(gate, up)
+    out.backward(grad)
+    tol = TOL[dtype]
+    atol = BF16_ATOL if dtype == torch.bfloat16 else tol
+    torch.testing.assert_close(out.float(), ref, rtol=tol, atol=atol)
+    torch.testing.assert_close(gate.grad.float(), gr.grad, rtol=tol, atol=atol)
+    torch.testing.assert_close(up.grad.float(), ur.grad, rtol=tol, atol=atol)
+
+
+# ----------------------------------------------------------------------------------- LoRA
+
+def test_dropout_masks_equal_reference_bits(cuda):
+    from hackathon_b200.lora import DropoutCast
+    g = golden("lora")
+    x = _t(g["drop_x"], cuda)
+    for i in range(4):
+        seed, p_micro = (int(v) for v in g[f"drop_{i}_meta"])
+        p = p_micro / 1e6
+        keep = np.unpackbits(g[f"drop_{i}_keep"])[: x.numel()].reshape(x.shape).astype(bool)
+        xg = x.clone().requires_grad_()
+        y = DropoutCast.apply(xg, p, seed, torch.float32)
+        assert np.array_equal((y != 0).cpu().numpy(), keep), i
+        if f"drop_{i}_y" in g:
+            assert np.array_equal(y.detach().cpu().numpy().view(np.uint32),
+                                  g[f"drop_{i}_y"].view(np.uint32))
+        y.backward(torch.ones_like(y))
+        dk = np.unpackbits(g[f"drop_{i}_dx_keep"])[: x.numel()].reshape(x.shape).astype(bool)
+        assert np.array_equal((xg.grad != 0).cpu().numpy(), dk), i
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32, torch.bfloat16])
+def test_dropout_cast_no_dropout_is_a_cast(cuda, out_dtype):
+    from hackathon_b200.lora import DropoutCast
+    x = torch.randn(3, 7, 1536, device=cuda, requires_grad=True)
+    y = DropoutCast.apply(x, 0.0, 0, out_dtype)
+    assert y.dtype == out_dtype
+    torch.testing.assert_close(y, x.detach().to(out_dtype), atol=0, rtol=0)
+    g = torch.randn_like(y)
+    y.backward(g)
+    assert x.grad.dtype == x.dtype
+    torch.testing.assert_close(x.grad, g.float(), atol=0, rtol=0)
+
+
+def test_dropout_rate_scale_and_backward(cuda):
+    from hackathon_b200.lora import DropoutCast
+    p = 0.05
+    x = torch.randn(2048, 1536, device=cuda, requires_grad=True)
+    y = DropoutCast.apply(x, p, 1234, torch.float32)
+    kept = y != 0
+    rate = 1 - kept.float().mean().item()
+    assert abs(rate - p) < 0.01, rate
+    torch.testing.assert_close(y[kept], x.detach()[kept] / (1 - p))
+    y.backward(torch.ones_like(y))
+    torch.testing.assert_close(x.grad, kept.float() / (1 - p))
+    y3 = DropoutCast.apply(x.detach(), p, 4321, torch.float32)
+    assert not torch.equal(y3 != 0, kept)
+
+
+def test_dropout_mask_at_step_shape_matches_oracle(cuda):
+    """[16384, 3584] bf16 (the 7B step's q/k/v input): rows spread over the tensor, bit-exact."""
+    from hackathon_b200.lora import DropoutCast
+    rows, cols, p, seed = 16384, 3584, 0.05, 987654321
+    x = torch.ones(rows, cols, device=cuda, dtype=torch.bfloat16)
+    y = DropoutCast.apply(x, p, seed, torch.bfloat16)
+    for r in (0, 1, 8191, rows - 1):
+        want = nf4_ref.philox_uniform(seed, r * cols + np.arange(cols)) > np.float32(p)
+        assert np.array_equal((y[r] != 0).cpu().numpy(), want), r
+
+
+def test_dropout_flat_index_wraps_like_int32(cuda):
+    """rows*cols > 2^31: the reference's int32 flat index wraps; so must ours."""
+    from hackathon_b200 import _lib
+    rows, cols, p, seed = 270_000, 8192, 0.5, 99
+    src = torch.ones(1, cols, device=cuda, dtype=torch.bfloat16)
+    out = torch.empty(rows, cols, device=cuda, dtype=torch.bfloat16)
+    _lib.call("qb_dropout_scale", src.data_ptr(), _lib.BF16, 0, out.data_ptr(), _lib.BF16, cols,
+              rows, cols, seed, p, 2.0, _lib.stream(cuda))
+    for r in (262_143, 262_144, rows - 1):   # 262144 * 8192 = 2^31
+        want = nf4_ref.philox_uniform(seed, r * cols + np.arange(cols)) > np.float32(p)
+        assert np.array_equal((out[r] != 0).cpu().numpy(), want), r
+
+
+@pytest.mark.parametrize("out_features", [1536, 256])
+def test_scaled_add_matches_peft(cuda, out_features):
+    from hackathon_b200.lora import ScaledAdd
+    torch.manual_seed(0)
+    base = torch.randn(2, 5, out_features, device=cuda, requires_grad=True)
+    lo = torch.randn(2, 5, out_features, device=cuda, dtype=torch.float16, requires_grad=True)
+    base_ref = base.detach().clone().requires_grad_()
+    lo_ref = lo.detach().clone().requires_grad_()
+    out_ref = ops_ref.scaled_add_ref(base_ref, lo_ref, 2.0)
+    out = ScaledAdd.apply(base, lo, 2.0)
+    assert out.dtype == out_ref.dtype
+    torch.testing.assert_close(out, out_ref, atol=1e-6, rtol=1e-6)
+    g = torch.randn_like(out_ref)
+    out_ref.backward(g)
+    out.backward(g)
+    torch.testing.assert_close(base.grad, base_ref.grad)
+    assert lo.grad.dtype == lo_ref.grad.dtype
+    torch.testing.assert_close(lo.grad, lo_ref.grad, atol=2e-3, rtol=2e-3)
+
+
+def test_scaled_add_vs_reference_fixture(cuda):
+    from hackathon_b200.lora import ScaledAdd
+    g = golden("lora")
+    base = _t(g["sadd_base"], cuda).requires_grad_()
+    lo = _t(g["sadd_lo"], cuda, torch.float16).requires_grad_()
+    y = ScaledAdd.apply(base, lo, 2.0)
+    torch.testing.assert_close(y, _t(g["sadd_y"], cuda), rtol=1e-6, atol=1e-6)
+    y.backward(_t(g["sadd_g"], cuda))
+    torch.testing.assert_close(base.grad, _t(g["sadd_dbase"], cuda))
+    torch.testing.assert_close(lo.grad.float(), _t(g["sadd_dlo"], cuda), rtol=2e-3, atol=2e-3)
