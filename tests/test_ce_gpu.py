@@ -21,10 +21,14 @@ def test_fused_causal_lm_loss_vs_reference_fixtures(cuda, i):
     labels = torch.from_numpy(g[f"ce_v{vocab}_labels"]).to(cuda)
     items = int(g[f"ce_{i}_num_items"][0])
     num_items = None if items < 0 else torch.tensor(items, device=cuda)
-    with torch.backends.cuda.matmul.flags(allow_tf32=False):
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False   # fp32 logits, as the fixture's CPU matmul
+    try:
         loss, step = fused_causal_lm_loss(hidden, weight, labels, num_items_in_batch=num_items,
                                           chunk_rows=7)
         (loss * 1024.0).backward()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
     torch.testing.assert_close(loss.cpu(), torch.tensor(g[f"ce_{i}_loss"][0]), rtol=1e-4, atol=1e-5)
     torch.testing.assert_close(step.token_loss.cpu(), torch.from_numpy(g[f"ce_{i}_token_loss"]),
                                rtol=1e-4, atol=1e-4)
@@ -131,7 +135,7 @@ def test_ce_rows_kernel_edge_cases(cuda):
     target = torch.tensor([5, 1000, -100, 0], device=cuda)
     want_lse = torch.logsumexp(logits.cpu(), -1)
     loss, ent, correct = ce_rows(logits.clone(), target, write_grad=False)
-    assert correct.tolist() == [1, 1, 0, 0]
+    assert correct.tolist() == [1, 1, 0, 1]   # row 3 is all zeros: argmax 0 == label 0
     assert loss[2].item() == 0.0
     torch.testing.assert_close(loss[0].cpu(), want_lse[0] - 3.0, rtol=1e-5, atol=1e-5)
     g = logits.clone()
