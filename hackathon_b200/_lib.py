@@ -32,6 +32,8 @@ _SIGNATURES = {
     "qb_nf4_quantize": [_p, _i32, _i64, _i32, _p, _p, _p, _p],
     "qb_nf4_double_quant_workspace": [_i64],
     "qb_nf4_double_quant": [_p, _i64, _i32, _p, _p, _p, _p, _p, _p],
+    "qb_nf4_double_quant_noalloc_max_blocks": [],
+    "qb_nf4_double_quant_noalloc": [_p, _i64, _i32, _p, _p, _p, _p, _p],
     "qb_rmsnorm_fwd": [_p, _i32, _i64, _p, _i32, _p, _i32, _i64, _p, _i64, _i64, _f32, _p],
     "qb_rmsnorm_bwd": [_p, _i32, _i64, _p, _i32, _i64, _p, _i32, _p, _p, _i32, _i64, _i64, _i64,
                        _p],
@@ -43,7 +45,8 @@ _SIGNATURES = {
     "qb_scaled_add": [_p, _i32, _i64, _p, _i32, _i64, _p, _i32, _i64, _i64, _i64, _f32, _p],
     "qb_ce_rows": [_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p, _p, _f32, _i32, _p],
 }
-_RESTYPE = {"qb_last_error": ctypes.c_char_p, "qb_nf4_double_quant_workspace": ctypes.c_int64}
+_RESTYPE = {"qb_last_error": ctypes.c_char_p, "qb_nf4_double_quant_workspace": ctypes.c_int64,
+            "qb_nf4_double_quant_noalloc_max_blocks": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib = None

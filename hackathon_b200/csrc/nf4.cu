@@ -11,6 +11,8 @@
 // The fast path gives each thread one 4-byte word (8 weights) per step, so a warp reads 128
 // contiguous bytes and writes 512 (bf16/fp16) or 1024 (fp32) contiguous bytes per step: every
 // load and store instruction is fully coalesced; the lookup tables sit in shared memory.
+#include <mutex>
+
 #include "qb_common.cuh"
 
 namespace {
@@ -257,6 +259,67 @@ extern "C" int qb_nf4_quantize(const void* w, int w_dtype, int64_t n_weights, in
         static_cast<const T*>(w), n_weights, blocksize, lut16, packed, absmax, n_blocks);
   });
   return qb::check_launch("nf4_quantize");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Double quant without any allocation, for callers that cannot allocate device memory.
+//
+// The partial sums live in this file-scope device array instead of a caller-provided workspace.
+// Every GPU that loads the library holds these 4 KiB until the process exits. Host code must
+// not pass `g_dq_scratch` to a kernel (on the host it names a stand-in, not device memory): the
+// device address is looked up once per device with cudaGetSymbolAddress and cached. Every slot a
+// call uses is written by its first kernel before its second kernel reads it, so nothing needs
+// clearing between calls; calls whose kernels overlap on the GPU (different streams, or
+// different host threads on one device) race on the array.
+constexpr int kStaticPartials = 512;
+static __device__ __align__(256) double g_dq_scratch[kStaticPartials];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+int static_scratch(double** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "nf4_double_quant_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return qb::fail(QB_ERR_UNSUPPORTED, "nf4_double_quant_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_dq_scratch);
+    if (e != cudaSuccess || !p)
+      return qb::fail(QB_ERR_CUDA, "nf4_double_quant_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = static_cast<double*>(g_scratch_addr[dev]);
+  return QB_OK;
+}
+}  // namespace
+
+extern "C" int64_t qb_nf4_double_quant_noalloc_max_blocks(void) {
+  return static_cast<int64_t>(kStaticPartials) * 4096;
+}
+
+extern "C" int qb_nf4_double_quant_noalloc(const float* absmax, int64_t n_blocks, int blocksize2,
+                                           const float* code2, uint8_t* absmax_q, float* absmax2,
+                                           float* offset_dev, cudaStream_t stream) {
+  if (n_blocks <= 0) return qb::fail(QB_ERR_INVALID, "nf4_double_quant_noalloc: no blocks");
+  if (blocksize2 <= 0 || blocksize2 % 2) return qb::fail(QB_ERR_INVALID, "nf4_double_quant_noalloc: blocksize2 must be even");
+  const int64_t parts = (n_blocks + 4095) / 4096;  // the partition qb_nf4_double_quant uses
+  if (parts > kStaticPartials)
+    return qb::fail(QB_ERR_INVALID,
+                    "nf4_double_quant_noalloc: %lld scale blocks exceed the static scratch "
+                    "limit of %lld (use qb_nf4_double_quant with a workspace)",
+                    (long long)n_blocks, (long long)kStaticPartials * 4096);
+  double* partial = nullptr;
+  if (int s = static_scratch(&partial)) return s;
+  dq_partial_sum_kernel<<<static_cast<unsigned>(parts), kThreads, 0, stream>>>(absmax, n_blocks, partial);
+  dq_mean_kernel<<<1, 32, 0, stream>>>(partial, static_cast<int>(parts), n_blocks, offset_dev);
+  const int64_t grid = (n_blocks + blocksize2 - 1) / blocksize2;
+  dq_quantize_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+      absmax, n_blocks, blocksize2, code2, offset_dev, absmax_q, absmax2);
+  return qb::check_launch("nf4_double_quant_noalloc");
 }
 
 extern "C" int64_t qb_nf4_double_quant_workspace(int64_t) {

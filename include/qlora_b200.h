@@ -71,6 +71,21 @@ int qb_nf4_double_quant(const float* absmax, int64_t n_blocks, int blocksize2,
                         const float* code2, uint8_t* absmax_q, float* absmax2,
                         float* offset_dev, void* workspace, cudaStream_t stream);
 
+/* qb_nf4_double_quant for callers that cannot allocate device memory — code running where
+ * cudaMalloc is off limits (inside a caching allocator's own hooks, a plugin host that owns all
+ * device memory, a process that has pinned its memory budget). No counterpart in the reference.
+ * Same arguments and results as qb_nf4_double_quant, minus the workspace: the partial sums go
+ * to a 4 KiB array compiled into the library (static device memory every GPU that loads the
+ * library keeps until exit), so n_blocks is limited to qb_nf4_double_quant_noalloc_max_blocks()
+ * (2,097,152 scale blocks = 134M weights at blocksize 64); larger inputs return QB_ERR_INVALID.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress): make
+ * that first call before any stream capture. Calls share the array, so calls that overlap on the
+ * GPU race; each call writes every slot it reads, so nothing needs clearing. */
+int64_t qb_nf4_double_quant_noalloc_max_blocks(void);
+int qb_nf4_double_quant_noalloc(const float* absmax, int64_t n_blocks, int blocksize2,
+                                const float* code2, uint8_t* absmax_q, float* absmax2,
+                                float* offset_dev, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * RMSNorm (Qwen2RMSNorm), frozen weight
  */
