@@ -44,6 +44,8 @@ _SIGNATURES = {
     "qb_dropout_scale": [_p, _i32, _i64, _p, _i32, _i64, _i64, _i64, _u64, _f32, _f32, _p],
     "qb_scaled_add": [_p, _i32, _i64, _p, _i32, _i64, _p, _i32, _i64, _i64, _i64, _f32, _p],
     "qb_ce_rows": [_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p, _p, _f32, _i32, _p],
+    "qb_device_error": [_p],
+    "qb_gemm_bf16": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p],
 }
 _RESTYPE = {"qb_last_error": ctypes.c_char_p, "qb_nf4_double_quant_workspace": ctypes.c_int64,
             "qb_nf4_double_quant_noalloc_max_blocks": ctypes.c_int64}

@@ -168,6 +168,24 @@ int qb_ce_rows(void* logits, int logits_dtype, int64_t row_stride, const int64_t
                int64_t rows, int64_t vocab, float* loss, float* entropy, int64_t* pred,
                int32_t* correct, float grad_scale, int write_grad, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Tensor-core (tcgen05 / TMEM / TMA) GEMM
+ */
+
+/* C[M,N] = A[M,K] * B[N,K]^T (+ bias[N] fp32), bf16 operands, fp32 accumulation, C in F32 or
+ * BF16 (row stride ldc). a_mn_major = 0: A is [M,K] with row stride lda; 1: A is stored [K,M]
+ * (row stride lda). Same for B ([N,K] or stored [K,N]). Leading dimensions must make rows
+ * 16-byte aligned. Replaces the cuBLAS calls of the reference's chunked CE
+ * (solution/cross_entropy.py:117 logits = h @ W.T, :123 grad_h = dz @ W) and of its 4-bit
+ * linear (solution/nf4.py:104 F.linear, :111 grad_out @ W). */
+int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
+                 int b_mn_major, void* C, int64_t ldc, int c_dtype, const float* bias, int64_t M,
+                 int64_t N, int64_t K, cudaStream_t stream);
+
+/* Reads and clears this device's tensor-core error flag (synchronises `stream`): QB_OK, or
+ * QB_ERR_TIMEOUT when a kernel gave up one of its bounded waits (its output is then invalid). */
+int qb_device_error(cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
