@@ -46,9 +46,18 @@ _SIGNATURES = {
     "qb_ce_rows": [_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p, _p, _f32, _i32, _p],
     "qb_device_error": [_p],
     "qb_gemm_bf16": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p],
+    "qb_nf4_linear_fwd": [_p, _i64, _p, _p, _p, _p, _f32, _i32, _p, _i64, _i64, _i64, _p, _p,
+                          _i64, _p, _i64, _i64, _p, _i64, _p],
+    "qb_nf4_linear_dgrad": [_p, _i64, _p, _p, _p, _p, _f32, _i32, _p, _i64, _i64, _i64, _p,
+                            _i64, _p, _i64, _i64, _p, _i64, _p],
+    "qb_linear_ce_vocab_tiles": [_i64],
+    "qb_linear_ce_stats": [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p],
+    "qb_ce_reduce": [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p],
+    "qb_linear_ce_grad": [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p],
 }
 _RESTYPE = {"qb_last_error": ctypes.c_char_p, "qb_nf4_double_quant_workspace": ctypes.c_int64,
-            "qb_nf4_double_quant_noalloc_max_blocks": ctypes.c_int64}
+            "qb_nf4_double_quant_noalloc_max_blocks": ctypes.c_int64,
+            "qb_linear_ce_vocab_tiles": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib = None

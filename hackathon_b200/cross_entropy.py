@@ -24,6 +24,49 @@ GRAD_GAIN = 65536.0
 STEP_ATTR = "_soup_chunked_step"
 
 
+def linear_ce_tc(h2, w, tgt, token_loss, entropy, pred, grad_h, scale_dev, chunk_rows):
+    """The tcgen05 path for bf16 hidden states and head: per chunk of rows, pass 1 (logits in
+    TMEM -> per-tile row statistics), the reduction, and with grad_h pass 2 (logits in TMEM ->
+    dZ bf16) followed by dH = dZ @ W into grad_h (fp32). Logits never reach HBM."""
+    from .gemm import gemm
+    n, hdim = h2.shape
+    vocab = w.shape[0]
+    dev = h2.device
+    s = _lib.stream(dev)
+    n_vt = int(_lib.load().qb_linear_ce_vocab_tiles(vocab))
+    rows_max = min(chunk_rows, n)
+    partials = torch.empty((n_vt, rows_max, 4), dtype=torch.float32, device=dev)
+    z_label = torch.empty(rows_max, dtype=torch.float32, device=dev)
+    lse = torch.empty(rows_max, dtype=torch.float32, device=dev)
+    ldz = (vocab + 7) // 8 * 8      # 16-byte rows for the dH GEMM's TMA
+    dz = torch.empty((rows_max, ldz), dtype=torch.bfloat16, device=dev) \
+        if grad_h is not None else None
+    for start in range(0, n, chunk_rows):
+        stop = min(start + chunk_rows, n)
+        rows = stop - start
+        h = h2[start:stop]
+        t = tgt[start:stop]
+        _lib.call("qb_linear_ce_stats", h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
+                  t.data_ptr(), rows, vocab, hdim, partials.data_ptr(), z_label.data_ptr(), s,
+                  work=(0, 2 * rows * vocab * hdim))
+        _lib.call("qb_ce_reduce", partials.data_ptr(), n_vt, rows, vocab, t.data_ptr(),
+                  z_label.data_ptr(), token_loss[start:stop].data_ptr(),
+                  entropy[start:stop].data_ptr(), pred[start:stop].data_ptr(), None,
+                  lse.data_ptr(), s, work=(n_vt * rows * 16 + rows * 32, 0))
+        if grad_h is not None:
+            _lib.call("qb_linear_ce_grad", h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
+                      t.data_ptr(), rows, vocab, hdim, lse.data_ptr(), scale_dev.data_ptr(),
+                      dz.data_ptr(), dz.stride(0), s, work=(0, 2 * rows * vocab * hdim))
+            gemm(dz[:rows, :vocab], w.t(), out=grad_h[start:stop], out_dtype=torch.float32)
+
+
+def tc_path_ok(h2, w, matmul_dtype):
+    return (matmul_dtype == torch.bfloat16 and h2.is_cuda and w.is_cuda
+            and h2.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+            and h2.shape[1] % 8 == 0 and w.stride(-1) == 1 and h2.stride(-1) == 1
+            and w.stride(0) % 8 == 0 and h2.stride(0) % 8 == 0)
+
+
 def ce_rows_inplace(logits, target, token_loss, entropy, pred, grad_scale, write_grad):
     """Runs the row kernel on a [rows, vocab] logits chunk (rewritten in place with the scaled
     gradient when write_grad)."""
@@ -47,14 +90,28 @@ class FusedLinearCrossEntropy(torch.autograd.Function):
         n_rows = h2.shape[0]
         dev = hidden.device
         with_grad = ctx.needs_input_grad[0]
-        denom = float(denominator)
-        grad_scale = GRAD_GAIN / denom if denom else 0.0
 
         token_loss = torch.empty(n_rows, dtype=torch.float32, device=dev)
         entropy = torch.empty(n_rows, dtype=torch.float32, device=dev)
         pred = torch.empty(n_rows, dtype=torch.int64, device=dev)
         grad_h = torch.empty((n_rows, shape[-1]), dtype=torch.float32, device=dev) \
             if with_grad else None
+        w_mm = weight if weight.dtype == matmul_dtype else weight.to(matmul_dtype)
+        h_mm = h2 if h2.dtype == matmul_dtype else h2.to(matmul_dtype)
+        if tc_path_ok(h_mm, w_mm, matmul_dtype):
+            # the gradient scale stays on the device: no host sync on the denominator
+            d = torch.as_tensor(denominator, dtype=torch.float32, device=dev).reshape(1)
+            scale_dev = torch.where(d != 0, GRAD_GAIN / d, torch.zeros_like(d))
+            linear_ce_tc(h_mm, w_mm, tgt, token_loss, entropy, pred, grad_h, scale_dev,
+                         chunk_rows)
+            loss = token_loss.sum() / denominator
+            ctx.save_for_backward(grad_h)
+            ctx.shape, ctx.dtype = shape, hidden.dtype
+            ctx.mark_non_differentiable(token_loss, entropy, pred)
+            return (loss, token_loss.view(shape[:-1]), entropy.view(shape[:-1]),
+                    pred.view(shape[:-1]))
+        denom = float(denominator)
+        grad_scale = GRAD_GAIN / denom if denom else 0.0
         with torch.autocast(device_type=dev.type, enabled=False):
             w = weight if weight.dtype == matmul_dtype else weight.to(matmul_dtype)
             for start in range(0, n_rows, chunk_rows):

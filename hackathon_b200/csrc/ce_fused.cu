@@ -1,0 +1,232 @@
+// Fused linear cross-entropy on the tcgen05 GEMM: the [rows x vocab] logits live only in TMEM.
+//
+// (solution/cross_entropy.py:48-138 and fused_ce.py:42-158 compute the same quantities from a
+// materialised logits chunk.) Here, per chunk of rows:
+//   pass 1  qb_linear_ce_stats: logits tile = H W^T (128 rows x 256 vocab) in TMEM; the
+//           epilogue reduces each row of the tile to (max m, sum e^(z-m), sum e^(z-m) z, first
+//           argmax) — one float4 per (vocab tile, row) — and picks z[label] from the tile that
+//           holds it. Logits never reach HBM.
+//   reduce  qb_ce_reduce: merges the per-tile partials of every row into lse, loss =
+//           lse - z[label], entropy = lse - t/s, argmax, correct.
+//   pass 2  qb_linear_ce_grad: the logits tile again, epilogue dZ = (e^(z - lse) - onehot) *
+//           scale in bf16 (scale = GRAD_GAIN / denominator read on the device; 0 for unlabelled
+//           rows) — the gradient, not the logits.
+//   then    dH = dZ W (qb_gemm_bf16 with W read MN-major), fp32.
+// Executed flops: 3 x 2 N H V against the algorithmic 4 N H V (logits + dH).
+#include <cfloat>
+
+#include "tc_gemm.cuh"
+
+namespace {
+
+constexpr int kBN = 256;
+
+struct EpiGrad {
+  __nv_bfloat16* dz;       // [rows, ldz]
+  int64_t ldz;
+  const int64_t* target;
+  const float* lse;        // [rows]
+  const float* scale_dev;  // device scalar: GRAD_GAIN / denominator
+  int rows, vocab;
+  bool vec;
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
+    const int r = m0 + row;
+    const bool live = r < rows;
+    const int64_t label = live ? __ldg(target + r) : -1;
+    const float l = live ? __ldg(lse + r) : 0.f;
+    const float sc = (live && label >= 0) ? __ldg(scale_dev) : 0.f;
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      float v[32];
+      tc::tmem_ld32(taddr + ch * 32, v);
+      const int n = n0 + ch * 32;
+      if (!live || n >= vocab) continue;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        v[i] = (__expf(v[i] - l) - (n + i == label ? 1.f : 0.f)) * sc;
+      __nv_bfloat16* dst = dz + static_cast<int64_t>(r) * ldz + n;
+      if (vec && n + 32 <= vocab) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) qb::store8<__nv_bfloat16>(dst + i, v + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < vocab) dst[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
+};
+
+// Per row of the tile: (max m, sum e^(z-m), sum e^(z-m) z, first argmax) over the tile's
+// columns; z[label] when the label falls in this tile. One running max per 32-column chunk: when
+// a chunk raises it, the sums so far are rescaled once.
+struct EpiStats {
+  float4* partials;
+  float* z_label;
+  const int64_t* target;
+  int rows, vocab;
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
+    const int r = m0 + row;
+    const int64_t label = r < rows ? __ldg(target + r) : -1;
+    float m = -INFINITY, s = 0.f, t = 0.f;
+    int idx = 0x7fffffff;
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      float v[32];
+      tc::tmem_ld32(taddr + ch * 32, v);
+      const int n = n0 + ch * 32;
+      float cm = -INFINITY;
+      int cidx = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (n + i >= vocab) v[i] = -INFINITY;
+        if (v[i] > cm) { cm = v[i]; cidx = n + i; }
+        if (n + i == label && r < rows) z_label[r] = v[i];
+      }
+      if (cm == -INFINITY) continue;
+      if (cm > m) {                     // new running max: rescale what was summed so far
+        const float f = __expf(m - cm); // 0 when m == -inf
+        s *= f;
+        t *= f;
+        m = cm;
+        idx = cidx;
+      }
+      float cs = 0.f, ct = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float e = __expf(v[i] - m);
+        cs += e;
+        ct += (v[i] == -INFINITY) ? 0.f : e * v[i];
+      }
+      s += cs;
+      t += ct;
+    }
+    if (r < rows)
+      partials[static_cast<int64_t>(n0 / BN) * rows + r] = make_float4(m, s, t, __int_as_float(idx));
+  }
+};
+
+// One warp per row: merge the row's partials, finish the statistics.
+__global__ void ce_reduce_kernel(const float4* __restrict__ partials, int n_vt, int rows,
+                                 const int64_t* __restrict__ target,
+                                 const float* __restrict__ z_label, float* __restrict__ loss,
+                                 float* __restrict__ entropy, int64_t* __restrict__ pred,
+                                 int32_t* __restrict__ correct, float* __restrict__ lse_out,
+                                 int vocab) {
+  const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float m = -INFINITY, s = 0.f, t = 0.f;
+  int idx = 0x7fffffff;
+  for (int j = lane; j < n_vt; j += 32) {
+    const float4 p = partials[static_cast<int64_t>(j) * rows + r];
+    const int pidx = __float_as_int(p.w);
+    if (p.x == -INFINITY) continue;
+    if (p.x > m || (p.x == m && pidx < idx)) idx = pidx;
+    const float mm = fmaxf(m, p.x);
+    const float fa = __expf(m - mm), fb = __expf(p.x - mm);
+    s = s * fa + p.y * fb;
+    t = t * fa + p.z * fb;
+    m = mm;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float ot = __shfl_xor_sync(0xffffffffu, t, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (om == -INFINITY) continue;
+    if (om > m || (om == m && oi < idx)) idx = oi;
+    const float mm = fmaxf(m, om);
+    const float fa = __expf(m - mm), fb = __expf(om - mm);
+    s = s * fa + os * fb;
+    t = t * fa + ot * fb;
+    m = mm;
+  }
+  if (lane == 0) {
+    const float lse = m + logf(s);
+    const int64_t label = target[r];
+    const bool labelled = label >= 0 && label < vocab;
+    loss[r] = labelled ? lse - z_label[r] : 0.f;
+    entropy[r] = lse - t / s;
+    if (pred) pred[r] = idx;
+    if (correct) correct[r] = (labelled && idx == label) ? 1 : 0;
+    if (lse_out) lse_out[r] = lse;
+  }
+}
+
+int maps(CUtensorMap* mh, CUtensorMap* mw, const void* hidden, int64_t ldh, const void* weight,
+         int64_t ldw, int64_t rows, int64_t vocab, int64_t hdim) {
+  if (int s = tc_host::encode_2d(mh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, hidden, hdim, rows,
+                                 ldh * 2, 64, tcg::BM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return s;
+  return tc_host::encode_2d(mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, weight, hdim, vocab, ldw * 2, 64,
+                            kBN, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int check(int64_t rows, int64_t vocab, int64_t hdim, const void* a, const void* b,
+          const char* what) {
+  if (rows < 0 || vocab <= 0 || hdim <= 0 || rows > (1 << 30) || vocab > (1 << 30) || hdim > (1 << 30))
+    return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
+  if (rows > 0 && (!a || !b)) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  return QB_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t qb_linear_ce_vocab_tiles(int64_t vocab) { return (vocab + kBN - 1) / kBN; }
+
+extern "C" int qb_linear_ce_stats(const void* hidden, int64_t ldh, const void* weight,
+                                  int64_t ldw, const int64_t* target, int64_t rows,
+                                  int64_t vocab, int64_t hdim, void* partials, float* z_label,
+                                  cudaStream_t stream) {
+  if (int s = check(rows, vocab, hdim, hidden, weight, "linear_ce_stats")) return s;
+  if (rows == 0) return QB_OK;
+  if (!target || !partials || !z_label) return qb::fail(QB_ERR_INVALID, "linear_ce_stats: null pointer");
+  CUtensorMap mh, mw;
+  if (int s = maps(&mh, &mw, hidden, ldh, weight, ldw, rows, vocab, hdim)) return s;
+  tcg::Problem pb{static_cast<int>(rows), static_cast<int>(vocab), static_cast<int>((hdim + 63) / 64),
+                  0, static_cast<int>((rows + 127) / 128), static_cast<int>((vocab + kBN - 1) / kBN)};
+  EpiStats epi{static_cast<float4*>(partials), z_label, target, static_cast<int>(rows),
+                static_cast<int>(vocab)};
+  return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
+      mh, mw, mh, mw, pb, tcg::Nf4Operand{}, epi, stream, "linear_ce_stats");
+}
+
+extern "C" int qb_ce_reduce(const void* partials, int64_t n_vtiles, int64_t rows, int64_t vocab,
+                            const int64_t* target, const float* z_label, float* loss,
+                            float* entropy, int64_t* pred, int32_t* correct, float* lse,
+                            cudaStream_t stream) {
+  if (rows < 0 || n_vtiles <= 0 || rows > (1 << 30)) return qb::fail(QB_ERR_INVALID, "ce_reduce: bad shape");
+  if (rows == 0) return QB_OK;
+  if (!partials || !target || !z_label || !loss || !entropy)
+    return qb::fail(QB_ERR_INVALID, "ce_reduce: null pointer");
+  const int warps = 8;
+  const unsigned grid = static_cast<unsigned>((rows + warps - 1) / warps);
+  ce_reduce_kernel<<<grid, warps * 32, 0, stream>>>(
+      static_cast<const float4*>(partials), static_cast<int>(n_vtiles), static_cast<int>(rows),
+      target, z_label, loss, entropy, pred, correct, lse, static_cast<int>(vocab));
+  return qb::check_launch("ce_reduce");
+}
+
+extern "C" int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight,
+                                 int64_t ldw, const int64_t* target, int64_t rows, int64_t vocab,
+                                 int64_t hdim, const float* lse, const float* scale_dev,
+                                 void* dz, int64_t ldz, cudaStream_t stream) {
+  if (int s = check(rows, vocab, hdim, hidden, weight, "linear_ce_grad")) return s;
+  if (rows == 0) return QB_OK;
+  if (!target || !lse || !scale_dev || !dz) return qb::fail(QB_ERR_INVALID, "linear_ce_grad: null pointer");
+  CUtensorMap mh, mw;
+  if (int s = maps(&mh, &mw, hidden, ldh, weight, ldw, rows, vocab, hdim)) return s;
+  tcg::Problem pb{static_cast<int>(rows), static_cast<int>(vocab), static_cast<int>((hdim + 63) / 64),
+                  0, static_cast<int>((rows + 127) / 128), static_cast<int>((vocab + kBN - 1) / kBN)};
+  const bool vec = qb::aligned16(dz) && (ldz * 2) % 16 == 0;
+  EpiGrad epi{static_cast<__nv_bfloat16*>(dz), ldz, target, lse, scale_dev,
+              static_cast<int>(rows), static_cast<int>(vocab), vec};
+  return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
+      mh, mw, mh, mw, pb, tcg::Nf4Operand{}, epi, stream, "linear_ce_grad");
+}

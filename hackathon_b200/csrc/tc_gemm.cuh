@@ -4,7 +4,7 @@
 //
 // with K split into two segments (segment 1 is optional), each with its own operand sources:
 //   A: TMA, K-major or MN-major                    (activations, LoRA weights)
-//      NF4, K-major or MN-major: packed codes arrive by TMA, four dequant warps rebuild the bf16
+//      NF4, K-major or MN-major: packed codes arrive by TMA, eight dequant warps rebuild the bf16
 //      tile in registers (bit-exact with qb_nf4_dequant) and write it to shared memory in the
 //      swizzled layout the MMA reads — no bf16 weight ever reaches HBM
 //   B: TMA, K-major or MN-major
@@ -15,7 +15,7 @@
 //   warp 0      TMA producer (one thread)        -> full[s]
 //   warp 1      TMEM allocator + MMA issuer      full[s] (+ afull[s]) -> MMAs -> empty[s], tfull[b]
 //   warps 2-5   epilogue: TMEM -> registers -> the epilogue functor; tempty[b]
-//   warps 6-9   NF4 dequant (only when an A source is NF4): full[s] -> A tile -> afull[s]
+//   warps 6-13  NF4 dequant (only when an A source is NF4): full[s] -> A tile -> afull[s]
 // Accumulators are double-buffered in TMEM (2 x BN columns), so the epilogue of one tile runs
 // under the MMAs of the next. Every wait is bounded (tc::mbar_wait): a wait that gives up
 // raises the device error flag and every role drains out; TMEM is always released.
@@ -32,6 +32,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kEpiWarp0 = 2;
 constexpr int kDeqWarp0 = 6;
+constexpr int kDeqThreads = 256;  // 8 dequant warps: two per scheduler
 
 struct Nf4Operand {
   const uint8_t* absmax_q;  // uint8 codes of the block scales [rows * blocks_per_row]
@@ -58,7 +59,7 @@ struct Cfg {
   static constexpr int C_BYTES = NF4 ? 4096 : 0;
   static constexpr int STAGE = A_BYTES + B_BYTES + C_BYTES;
   static constexpr int STAGES = (NF4 ? 208 : 196) * 1024 / STAGE;
-  static constexpr int THREADS = NF4 ? 320 : 192;
+  static constexpr int THREADS = NF4 ? 192 + kDeqThreads : 192;
   static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
   static constexpr int EXTRA = 1024 /*align*/ + 512 /*barriers*/ + (NF4 ? (256 + 16) * 4 : 0);
   static constexpr int SMEM = STAGES * STAGE + EXTRA;
@@ -67,35 +68,63 @@ struct Cfg {
 constexpr bool is_nf4(int s) { return s == kNf4K || s == kNf4MN; }
 constexpr bool is_mn(int s) { return s == kTmaMN || s == kNf4MN; }
 
-// One dequant thread rebuilds 64 consecutive weights (32 packed bytes, one scale block) into one
-// 128-byte swizzled smem row: chunk c (8 weights) lands at chunk position c ^ swz.
-__device__ __forceinline__ void dequant_row64(const uint8_t* codes, float scale,
-                                              const float* lut, uint8_t* row, int swz) {
-  const uint4 c0 = *reinterpret_cast<const uint4*>(codes);
-  const uint4 c1 = *reinterpret_cast<const uint4*>(codes + 16);
-  const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+// One dequant thread rebuilds 32 consecutive weights (16 packed bytes, all in one scale block)
+// as four 16-byte chunks of a 128-byte swizzled smem row: chunk c lands at chunk position
+// c ^ swz. Byte j of the codes holds weights 2j (high nibble) and 2j+1 (low nibble).
+//
+// Per code byte: both nibble indices come pre-multiplied by 4 (one shift + mask per 4 bytes,
+// one byte permute per index), the two table values are multiplied by the scale in one packed
+// f32x2 multiply (two IEEE round-to-nearest products, as two scalar multiplies would give) and
+// rounded to bf16 in one cvt.
+__device__ __forceinline__ uint32_t nf4_pair(const float* lut, uint32_t hi4, uint32_t lo4, int b,
+                                             uint64_t scale2) {
+  const uint32_t ih = __byte_perm(hi4, 0u, 0x4440u | b);
+  const uint32_t il = __byte_perm(lo4, 0u, 0x4440u | b);
+  const float vh = *reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(lut) + ih);
+  const float vl = *reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(lut) + il);
+  uint64_t v, p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(vh), "f"(vl));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(scale2));
+  float ph, pl;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(ph), "=f"(pl) : "l"(p));
+  __nv_bfloat162 r = __floats2bfloat162_rn(ph, pl);   // weight 2j (high nibble) in the low half
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+__device__ __forceinline__ void dequant32(const uint8_t* codes, float scale, const float* lut,
+                                          uint8_t* row, int c0, int swz) {
+  const uint4 cw = *reinterpret_cast<const uint4*>(codes);
+  const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+  uint64_t scale2;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(scale2) : "f"(scale));
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const uint32_t x = w[c];
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t x = w[j];
+    const uint32_t hi4 = (x >> 2) & 0x3C3C3C3Cu;   // byte b: 4 * high nibble
+    const uint32_t lo4 = (x << 2) & 0x3C3C3C3Cu;   // byte b: 4 * low nibble
     uint32_t o[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const float hi = __fmul_rn(lut[(x >> (8 * b + 4)) & 15u], scale);  // weight 2j first
-      const float lo = __fmul_rn(lut[(x >> (8 * b)) & 15u], scale);
-      __nv_bfloat162 p = __floats2bfloat162_rn(hi, lo);
-      o[b] = *reinterpret_cast<uint32_t*>(&p);
-    }
-    *reinterpret_cast<uint4*>(row + ((c ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    for (int b = 0; b < 4; ++b) o[b] = nf4_pair(lut, hi4, lo4, b, scale2);
+    *reinterpret_cast<uint4*>(row + (((c0 + j) ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
-__device__ __forceinline__ float nf4_scale(const Nf4Operand& q, const float* s_code2, int row,
-                                           int blk_in_row) {
-  if (row >= q.rows || blk_in_row >= q.blocks_per_row) return 0.f;
+// The raw ingredients of one block scale (code of the first-level absmax, second-level scale),
+// loaded a couple of k-steps before they are needed; code < 0 marks an out-of-range block.
+struct ScaleRaw {
+  int code;
+  float a2;
+};
+
+__device__ __forceinline__ ScaleRaw scale_raw(const Nf4Operand& q, int row, int blk_in_row) {
+  if (row >= q.rows || blk_in_row >= q.blocks_per_row) return ScaleRaw{-1, 0.f};
   const int64_t blk = static_cast<int64_t>(row) * q.blocks_per_row + blk_in_row;
-  const uint8_t code = __ldg(q.absmax_q + blk);
-  const float a2 = __ldg(q.absmax2 + blk / q.blocksize2);
-  return __fadd_rn(__fmul_rn(s_code2[code], a2), q.offset);
+  return ScaleRaw{static_cast<int>(__ldg(q.absmax_q + blk)), __ldg(q.absmax2 + blk / q.blocksize2)};
+}
+
+// scale = code2[code] * absmax2 + offset: a rounded multiply, then a rounded add (no FMA).
+__device__ __forceinline__ float scale_of(const ScaleRaw& r, const float* s_code2, float offset) {
+  return r.code < 0 ? 0.f : __fadd_rn(__fmul_rn(s_code2[r.code], r.a2), offset);
 }
 
 template <int A0, int B0, int A1, int B1, int BN, class Epi>
@@ -127,7 +156,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
-      tc::mbar_init(&afull[s], 128);
+      tc::mbar_init(&afull[s], kDeqThreads);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
@@ -265,37 +294,49 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
     }
   } else if (kNF4) {
     // ---------------------------------------------------------------- NF4 dequant
-    // These warps step through every k-block (arriving on afull for TMA-fed blocks too), so
-    // afull's phases stay in lock step with full's.
-    const int d = threadIdx.x - kDeqWarp0 * 32;  // 0..127
+    // 256 threads, 32 weights each per k-block. These warps step through every k-block
+    // (arriving on afull for TMA-fed blocks too), so afull's phases stay in lock step with
+    // full's. Scale ingredients are loaded two k-blocks ahead of their use.
+    const int d = threadIdx.x - kDeqWarp0 * 32;  // 0..255
+    // K-major (A row = weight row): thread -> (row, half of the 64 k)
+    const int kr_row = d >> 1, k_half = d & 1;
+    // MN-major (A = W^T, k rows are weight rows): thread -> (k row, quarter of the 128 m)
+    const int mn_kr = d >> 2, mn_q = d & 3;
+    int off_codes, off_row, c0, swz;
+    if (A0 == kNf4K || A1 == kNf4K) {
+      off_codes = kr_row * 32 + k_half * 16;
+      off_row = kr_row * 128;
+      c0 = k_half * 4;
+      swz = kr_row & 7;
+    } else {
+      off_codes = mn_kr * 64 + mn_q * 16;
+      off_row = (mn_q >> 1) * 8192 + mn_kr * 128;
+      c0 = (mn_q & 1) * 4;
+      swz = mn_kr & 7;
+    }
+    auto raw_for = [&](int m0, int kb) -> ScaleRaw {
+      if (kb >= pb.nk0) return ScaleRaw{-1, 0.f};   // segment 1 is TMA-fed
+      if (A0 == kNf4K) return scale_raw(nf4, m0 + kr_row, kb);
+      return scale_raw(nf4, kb * BK + mn_kr, (m0 >> 6) + (mn_q >> 1));
+    };
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok && !tc::failed(err); tile += gridDim.x) {
       const int m0 = (tile % pb.num_m) * BM;
+      ScaleRaw r0 = raw_for(m0, 0), r1 = raw_for(m0, 1);
       for (int kb = 0; kb < nk; ++kb) {
         const bool seg1 = kb >= pb.nk0;
         const int asrc = seg1 ? A1 : A0;
-        const int k = seg1 ? kb - pb.nk0 : kb;
-        float scale = 0.f;
-        int swz = 0, off_codes = 0, off_row = 0;
-        if (asrc == kNf4K) {          // A row = weight row (out); 64 k = one scale block
-          scale = nf4_scale(nf4, s_code2, m0 + d, k);
-          off_codes = d * 32;
-          off_row = d * 128;
-          swz = d & 7;
-        } else if (asrc == kNf4MN) {  // A = W^T: k rows are weight rows, two 64-column blocks
-          const int kr = d >> 1, h = d & 1;
-          scale = nf4_scale(nf4, s_code2, k * BK + kr, (m0 >> 6) + h);
-          off_codes = kr * 64 + h * 32;
-          off_row = h * 8192 + kr * 128;
-          swz = kr & 7;
-        }
+        const ScaleRaw cur = r0;
+        r0 = r1;
+        r1 = raw_for(m0, kb + 2);
         if (!tc::mbar_wait(&full[stage], phase, err, 6)) { ok = false; break; }
         if (is_nf4(asrc)) {
           uint8_t* sA = smem + stage * C::STAGE;
           const uint8_t* sC = sA + C::A_BYTES + C::B_BYTES;
-          dequant_row64(sC + off_codes, scale, s_lut, sA + off_row, swz);
+          dequant32(sC + off_codes, scale_of(cur, s_code2, nf4.offset), s_lut, sA + off_row, c0,
+                    swz);
           tc::fence_proxy_async_smem();
         }
         tc::mbar_arrive(&afull[stage]);

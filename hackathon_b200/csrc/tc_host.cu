@@ -31,6 +31,10 @@ int current_device() {
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
               uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
               CUtensorMapSwizzle swizzle) {
+  // The encoder is a driver call and needs a current context on this thread. Threads the
+  // caller's runtime never made a context current on (autograd's backward worker of device 0,
+  // for one) get the runtime's current device's primary context here.
+  cudaFree(nullptr);
   {
     std::lock_guard<std::mutex> lock(g_mu);
     if (!g_encode) {

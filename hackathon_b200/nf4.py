@@ -180,23 +180,85 @@ def dequantize_nf4(packed, quant_state, dtype=torch.float16, out=None):
     return out
 
 
+def fused_ok(x, quant_state):
+    """True when the tcgen05 NF4 GEMM takes this call: bf16 activations on CUDA, a 2-D nested
+    NF4 state with blocksize 64 and feature counts that are multiples of 128."""
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and supported(quant_state)):
+        return False
+    out_f, in_f = quant_state.shape
+    return (quant_state.nested and quant_state.blocksize == 64 and in_f % 128 == 0
+            and out_f % 64 == 0)
+
+
+def _nf4_args(packed, qs):
+    lut = nf4_table(packed.device)
+    return (packed.data_ptr(), qs.absmax.data_ptr(), qs.state2.code.data_ptr(),
+            qs.state2.absmax.data_ptr(), float(qs.offset), int(qs.state2.blocksize),
+            lut.data_ptr())
+
+
+def _rows2d(t):
+    t2 = t.reshape(-1, t.shape[-1])
+    return t2 if t2.stride(-1) == 1 else t2.contiguous()
+
+
+def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None):
+    """y = x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T) on the fused tcgen05 kernel: the NF4
+    weight is rebuilt in registers inside the GEMM. x [..., in] bf16 -> y [..., out] bf16."""
+    out_f, in_f = qs.shape
+    x2 = _rows2d(x)
+    T = x2.shape[0]
+    y = torch.empty((T, out_f), dtype=torch.bfloat16, device=x.device)
+    r = 0 if u is None else u.shape[-1]
+    u2 = None if u is None else _rows2d(u)
+    lb = None if lora_b_scaled is None else lora_b_scaled.contiguous()
+    b = None if bias is None else bias.to(torch.bfloat16).contiguous()
+    _lib.call("qb_nf4_linear_fwd", x2.data_ptr(), x2.stride(0), *_nf4_args(packed, qs), T, in_f,
+              out_f, _lib.ptr(b), _lib.ptr(u2), u2.stride(0) if u2 is not None else 0,
+              _lib.ptr(lb), lb.stride(0) if lb is not None else 0, r, y.data_ptr(), y.stride(0),
+              _lib.stream(x.device), work=(0, 2 * T * out_f * (in_f + r)))
+    return y.view(*x.shape[:-1], out_f)
+
+
+def nf4_linear_dgrad(dy, packed, qs, v=None, lora_a=None):
+    """dx = dy @ deq(W) (+ v @ lora_a) on the fused tcgen05 kernel (W read transposed from the
+    packed codes). dy [..., out] bf16 -> dx [..., in] bf16."""
+    out_f, in_f = qs.shape
+    d2 = _rows2d(dy)
+    T = d2.shape[0]
+    dx = torch.empty((T, in_f), dtype=torch.bfloat16, device=dy.device)
+    r = 0 if v is None else v.shape[-1]
+    v2 = None if v is None else _rows2d(v)
+    la = None if lora_a is None else lora_a.contiguous()
+    _lib.call("qb_nf4_linear_dgrad", d2.data_ptr(), d2.stride(0), *_nf4_args(packed, qs), T,
+              in_f, out_f, _lib.ptr(v2), v2.stride(0) if v2 is not None else 0, _lib.ptr(la),
+              la.stride(0) if la is not None else 0, r, dx.data_ptr(), dx.stride(0),
+              _lib.stream(dy.device), work=(0, 2 * T * in_f * (out_f + r)))
+    return dx.view(*dy.shape[:-1], in_f)
+
+
 class NF4Linear(torch.autograd.Function):
     """y = x @ W.T + b, W rebuilt from NF4 in forward and again in backward (nothing dense is kept
     between them). W and b are frozen: the backward returns dX only (nf4.py:95-112)."""
 
     @staticmethod
     def forward(ctx, x, packed, quant_state, bias):
-        weight = dequantize_nf4(packed, quant_state, x.dtype)
-        out = torch.nn.functional.linear(x, weight, bias)
         ctx.packed, ctx.quant_state = packed, quant_state
-        return out
+        ctx.fused = fused_ok(x, quant_state)
+        if ctx.fused:   # bf16: the dequant happens inside the tcgen05 GEMM
+            return nf4_linear_fwd(x, packed, quant_state, bias)
+        weight = dequantize_nf4(packed, quant_state, x.dtype)
+        return torch.nn.functional.linear(x, weight, bias)
 
     @staticmethod
     def backward(ctx, grad_out):
         grad_x = None
         if ctx.needs_input_grad[0]:
-            weight = dequantize_nf4(ctx.packed, ctx.quant_state, grad_out.dtype)
-            grad_x = torch.matmul(grad_out, weight)
+            if ctx.fused and grad_out.dtype == torch.bfloat16:
+                grad_x = nf4_linear_dgrad(grad_out, ctx.packed, ctx.quant_state)
+            else:
+                weight = dequantize_nf4(ctx.packed, ctx.quant_state, grad_out.dtype)
+                grad_x = torch.matmul(grad_out, weight)
         return grad_x, None, None, None
 
 

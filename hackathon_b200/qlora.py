@@ -57,6 +57,57 @@ def preset(name, **overrides):
     return replace(PRESETS[name], **overrides)
 
 
+class LoRANF4Proj(torch.autograd.Function):
+    """The whole QLoRA projection on the fused kernels:
+
+        forward   U  = dropout(x) A^T                                   (skinny GEMM)
+                  y  = x deq(W)^T + b + U (s B)^T                       (qb_nf4_linear_fwd)
+        backward  V  = g (s B)                                          (skinny GEMM)
+                  dx = g deq(W) + dropout^T(V A)                        (qb_nf4_linear_dgrad;
+                                                                         V A as extra K if p = 0)
+                  dA = V^T dropout(x),  dB = s g^T U                    (fp32 adapter grads)
+    The dropout mask is regenerated from the seed (Philox, no stored mask)."""
+
+    @staticmethod
+    def forward(ctx, x, lora_a, lora_b, mod, p, seed):
+        from .lora import _dropout_scale
+        from .nf4 import nf4_linear_fwd
+        x2 = x.reshape(-1, x.shape[-1])
+        scale = 1.0 / (1.0 - p) if p > 0 else 1.0
+        xd = _dropout_scale(x2, x2.dtype, seed, p, scale) if p > 0 else x2
+        a16 = lora_a.to(x.dtype)
+        sb16 = (lora_b * mod.scaling).to(x.dtype)
+        u = xd @ a16.t()
+        y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16)
+        ctx.save_for_backward(x2, u, lora_a, lora_b)
+        ctx.mod, ctx.p, ctx.seed, ctx.scale, ctx.shape = mod, p, seed, scale, x.shape
+        return y.view(*x.shape[:-1], y.shape[-1])
+
+    @staticmethod
+    def backward(ctx, g):
+        from .lora import _dropout_scale
+        from .nf4 import nf4_linear_dgrad
+        x2, u, lora_a, lora_b = ctx.saved_tensors
+        mod, p = ctx.mod, ctx.p
+        g2 = g.reshape(-1, g.shape[-1])
+        if g2.dtype != x2.dtype:
+            g2 = g2.to(x2.dtype)
+        a16 = lora_a.to(x2.dtype)
+        sb16 = (lora_b * mod.scaling).to(x2.dtype)
+        v = g2 @ sb16                                              # [T, r]
+        if p > 0:
+            dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state)
+            dxd = v @ a16
+            dx += _dropout_scale(dxd, dxd.dtype, ctx.seed, p, ctx.scale)
+            xd = _dropout_scale(x2, x2.dtype, ctx.seed, p, ctx.scale)
+        else:
+            dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, v, a16)
+            xd = x2
+        da = (v.t() @ xd).float() if ctx.needs_input_grad[1] else None
+        db = (g2.t() @ u).float() * mod.scaling if ctx.needs_input_grad[2] else None
+        return dx.view(ctx.shape), da, db, None, None, None
+
+
 class LoRANF4Linear(torch.nn.Module):
     """y = x @ deq(W).T + b + (alpha/r) * dropout(x) @ A.T @ B.T with W frozen in NF4."""
 
@@ -81,10 +132,15 @@ class LoRANF4Linear(torch.nn.Module):
         self.scaling = shape.lora_alpha / r
         self.p = shape.lora_dropout
         self.in_features, self.out_features = in_features, out_features
+        self.fused = True
 
     def forward(self, x, seed):
-        base = NF4Linear.apply(x, self.packed, self.quant_state, self.bias)
+        from .nf4 import fused_ok
         p = self.p if self.training else 0.0
+        if self.fused and fused_ok(x, self.quant_state):
+            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed)
+        # the reference's composition: NF4Linear + DropoutCast + adapter GEMMs + ScaledAdd
+        base = NF4Linear.apply(x, self.packed, self.quant_state, self.bias)
         xd = DropoutCast.apply(x, p, seed, x.dtype) if p > 0 else x
         lo = F.linear(F.linear(xd, self.lora_A.to(x.dtype)), self.lora_B.to(x.dtype))
         return ScaledAdd.apply(base, lo, self.scaling)

@@ -182,6 +182,68 @@ int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const void* B, int6
                  int b_mn_major, void* C, int64_t ldc, int c_dtype, const float* bias, int64_t M,
                  int64_t N, int64_t K, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * NF4 x LoRA projection on tcgen05, the NF4 weight rebuilt in registers inside the GEMM
+ *
+ * Weight: nested NF4 (blocksize 64, double-quantised scales) of shape [out_f, in_f], in the
+ * layout qb_nf4_dequant reads; in_f a multiple of 64 (of 128 for the dgrad), packed 16-byte
+ * aligned. Activations bf16 row-major with 16-byte-aligned rows.
+ */
+
+/* y[T, out_f] = x[T, in_f] * deq(W)^T (+ bias[out_f] bf16) (+ u[T, r] * lora_b_scaled[out_f, r]^T)
+ * in bf16 (fp32 accumulation). With r > 0, u = dropout(x) * A_lora^T and lora_b_scaled =
+ * scaling * B_lora (bf16): the LoRA term rides along as extra K, so the adapter's second GEMM and
+ * the scaled add disappear. Replaces solution/nf4.py:100-104 (dequantize_nf4 + F.linear) and, with
+ * r > 0, the lora_B(...) + ScaledAdd of solution/lora.py:172-173. */
+int qb_nf4_linear_fwd(const void* x, int64_t ldx, const uint8_t* packed, const uint8_t* absmax_q,
+                      const float* code2, const float* absmax2, float offset, int blocksize2,
+                      const float* lut16, int64_t tokens, int64_t in_f, int64_t out_f,
+                      const void* bias, const void* u, int64_t ldu, const void* lora_b_scaled,
+                      int64_t ldlb, int64_t r, void* y, int64_t ldy, cudaStream_t stream);
+
+/* dx[T, in_f] = dy[T, out_f] * deq(W) (+ v[T, r] * lora_a[r, in_f]) in bf16, W read transposed
+ * from the same packed codes. With r > 0, v = scaling * dy * B_lora (no dropout on this path).
+ * Replaces solution/nf4.py:107-112 (dequantize_nf4 + grad_out @ weight). */
+int qb_nf4_linear_dgrad(const void* dy, int64_t lddy, const uint8_t* packed,
+                        const uint8_t* absmax_q, const float* code2, const float* absmax2,
+                        float offset, int blocksize2, const float* lut16, int64_t tokens,
+                        int64_t in_f, int64_t out_f, const void* v, int64_t ldv,
+                        const void* lora_a, int64_t ldla, int64_t r, void* dx, int64_t lddx,
+                        cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Fused linear cross-entropy on tcgen05 (logits only in TMEM)
+ *
+ * Replaces, for bf16 hidden states and head, the chunk loop of solution/cross_entropy.py:115-124
+ * (cuBLAS logits, fused_ce_kernel, cuBLAS dz @ W) and of solution/fused_ce.py:132-144.
+ * hidden [rows, hdim] bf16 (row stride ldh), weight [vocab, hdim] bf16 (row stride ldw),
+ * target [rows] int64 (-100 or any value outside [0, vocab) = unlabelled).
+ */
+
+/* Number of 256-wide vocab tiles: partials hold vocab_tiles * rows float4 records. */
+int64_t qb_linear_ce_vocab_tiles(int64_t vocab);
+
+/* Pass 1: per (vocab tile, row) the tile's (max, sum exp(z - max), sum exp(z - max) * z, first
+ * argmax) into `partials` (float4 [vocab_tiles, rows]), and z[label] into z_label[rows]. */
+int qb_linear_ce_stats(const void* hidden, int64_t ldh, const void* weight, int64_t ldw,
+                       const int64_t* target, int64_t rows, int64_t vocab, int64_t hdim,
+                       void* partials, float* z_label, cudaStream_t stream);
+
+/* Merges the partials: lse, loss = lse - z[label] (0 if unlabelled), entropy = lse - sum(p*z),
+ * pred = first argmax (int64, may be NULL), correct (int32, may be NULL), lse (may be NULL).
+ * The per-row outputs of solution/cross_entropy.py:77-81 / fused_ce.py:81-87. */
+int qb_ce_reduce(const void* partials, int64_t n_vtiles, int64_t rows, int64_t vocab,
+                 const int64_t* target, const float* z_label, float* loss, float* entropy,
+                 int64_t* pred, int32_t* correct, float* lse, cudaStream_t stream);
+
+/* Pass 2: dz[rows, vocab] (bf16, row stride ldz) = (exp(z - lse) - onehot(label)) * scale, with
+ * scale = *scale_dev (a device scalar, e.g. GRAD_GAIN / denominator) for labelled rows and 0
+ * otherwise (solution/cross_entropy.py:83-90). dH = dz @ weight follows with qb_gemm_bf16. */
+int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight, int64_t ldw,
+                      const int64_t* target, int64_t rows, int64_t vocab, int64_t hdim,
+                      const float* lse, const float* scale_dev, void* dz, int64_t ldz,
+                      cudaStream_t stream);
+
 /* Reads and clears this device's tensor-core error flag (synchronises `stream`): QB_OK, or
  * QB_ERR_TIMEOUT when a kernel gave up one of its bounded waits (its output is then invalid). */
 int qb_device_error(cudaStream_t stream);

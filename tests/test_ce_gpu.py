@@ -92,10 +92,21 @@ def test_fused_ce_matches_base_fp16_autocast(cuda, vocab, with_num_items):
     torch.testing.assert_close(hidden.grad.cpu(), hidden_ref.grad, atol=5e-3, rtol=2e-2)
 
 
+def _fp32_logits(hidden2d, weight):
+    """Oracle logits: exact products of the bf16 operands, fp32 sums (no TF32)."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        return (hidden2d.float() @ weight.float().t()).cpu()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def test_fused_ce_baseline_shape_rows(cuda):
-    """H=3584, V=152064 (Cfg3 shapes), bf16 activations and head: 256 rows checked against the
-    oracle fed the same bf16 logits; loss within 1e-4 relative."""
+    """H=3584, V=152064 (Cfg3 shapes), bf16 activations and head on the tcgen05 path (logits only
+    in TMEM): 256 rows against the oracle's fp32-accumulated logits; loss within 1e-4 relative."""
     from hackathon_b200.cross_entropy import fused_causal_lm_loss
+    from hackathon_b200.gemm import device_error
     gen = torch.Generator(device=cuda).manual_seed(0)
     H, V, T = 3584, 152064, 256
     hidden = torch.randn(1, T, H, device=cuda, generator=gen).to(torch.bfloat16)
@@ -105,7 +116,8 @@ def test_fused_ce_baseline_shape_rows(cuda):
     h = hidden.detach().requires_grad_()
     loss, step = fused_causal_lm_loss(h, weight, labels)
     loss.backward()
-    logits = (hidden[0] @ weight.t()).float().cpu()   # the bf16 logits the chunked path sees
+    device_error()
+    logits = _fp32_logits(hidden[0], weight)
     hr = hidden.float().cpu().requires_grad_()
     loss_ref, ent_ref, tok_ref, correct_ref, total_ref, _ = ops_ref.ce_ref(
         hr, weight.float().cpu(), labels.cpu(), logits=logits[None])
@@ -151,3 +163,51 @@ def test_ce_rows_kernel_edge_cases(cuda):
     l2, e2, _ = ce_rows(view.contiguous(), torch.tensor([1, 2, 3], device=cuda), write_grad=False)
     torch.testing.assert_close(l1, l2)
     torch.testing.assert_close(e1, e2)
+
+
+@pytest.mark.parametrize("vocab", [1000, 4096, 9001, 32768])
+@pytest.mark.parametrize("rows,chunk", [(300, 4096), (600, 256)])
+def test_tc_linear_ce_vs_oracle(cuda, vocab, rows, chunk):
+    """The tcgen05 path at ragged vocab sizes and across row chunks: statistics against the
+    fp32-logit oracle (loss 1e-4 relative), gradient within bf16 tolerance."""
+    from hackathon_b200.cross_entropy import fused_causal_lm_loss
+    from hackathon_b200.gemm import device_error
+    gen = torch.Generator(device=cuda).manual_seed(vocab + rows)
+    H = 512
+    hidden = torch.randn(1, rows, H, device=cuda, generator=gen).to(torch.bfloat16)
+    weight = (torch.randn(vocab, H, device=cuda, generator=gen) * 0.05).to(torch.bfloat16)
+    labels = torch.randint(0, vocab, (1, rows), device=cuda, generator=gen)
+    labels[:, :7] = -100
+    h = hidden.detach().requires_grad_()
+    items = (labels[:, 1:] != -100).sum()
+    loss, step = fused_causal_lm_loss(h, weight, labels, num_items_in_batch=items,
+                                      chunk_rows=chunk)
+    (loss * 1024.0).backward()
+    device_error()
+    logits = _fp32_logits(hidden[0], weight)
+    lg = logits.clone().requires_grad_()
+    loss_ref, ent_ref, tok_ref, correct_ref, total_ref, _ = ops_ref.ce_ref(
+        None, None, labels.cpu(), items.cpu(), logits=lg[None])
+    (loss_ref * 1024.0).backward()
+    assert abs(float(loss) - float(loss_ref)) <= 1e-4 * abs(float(loss_ref))
+    torch.testing.assert_close(step.token_loss.cpu(), tok_ref, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(step.token_entropy.cpu(), ent_ref, rtol=1e-4, atol=1e-3)
+    assert int(step.labelled) == int(total_ref)
+    assert abs(int(step.correct) - int(correct_ref)) <= 1
+    dh_ref = lg.grad @ weight.float().cpu()
+    torch.testing.assert_close(h.grad[0].float().cpu(), dh_ref, rtol=2e-2, atol=2e-3)
+
+
+def test_tc_linear_ce_unlabelled_rows_have_zero_gradient(cuda):
+    from hackathon_b200.cross_entropy import fused_causal_lm_loss
+    gen = torch.Generator(device=cuda).manual_seed(7)
+    hidden = torch.randn(1, 130, 256, device=cuda, generator=gen).to(torch.bfloat16)
+    weight = torch.randn(777, 256, device=cuda, generator=gen).to(torch.bfloat16)
+    labels = torch.randint(0, 777, (1, 130), device=cuda, generator=gen)
+    labels[0, 60:] = -100     # shifted targets 59.. are unlabelled
+    h = hidden.detach().requires_grad_()
+    loss, step = fused_causal_lm_loss(h, weight, labels)
+    loss.backward()
+    assert torch.all(h.grad[0, 59:] == 0)
+    assert torch.all(step.token_loss[0, 59:] == 0)
+    assert torch.isfinite(loss)

@@ -22,6 +22,37 @@ def test_tiny_step_runs_and_loss_is_sane(cuda):
     assert abs(losses[0] - math.log(shape.vocab)) < 1.0
 
 
+@pytest.mark.parametrize("p", [0.0, 0.1])
+@pytest.mark.parametrize("shape", [(3584, 512, 300), (896, 4864, 128)])
+def test_fused_projection_matches_reference_composition(cuda, p, shape):
+    """LoRANF4Proj (fused NF4 GEMM, LoRA as extra K) against the reference's composition of the
+    same op: NF4Linear + DropoutCast + lora_B(lora_A(.)) + ScaledAdd, forward and all grads."""
+    from hackathon_b200.qlora import LoRANF4Linear, preset
+    in_f, out_f, T = shape
+    s = preset("0.5b", lora_r=64, lora_alpha=128, lora_dropout=p)
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    mod = LoRANF4Linear(in_f, out_f, True, s, cuda, gen)
+    with torch.no_grad():
+        mod.lora_B.normal_(0, 0.05, generator=gen)
+    x = torch.randn(T, in_f, device=cuda, generator=gen).to(torch.bfloat16)
+    gy = torch.randn(T, out_f, device=cuda, generator=gen).to(torch.bfloat16)
+    outs = []
+    for fused in (True, False):
+        mod.fused = fused
+        mod.lora_A.grad = mod.lora_B.grad = None
+        xi = x.clone().requires_grad_()
+        y = mod(xi, seed=1234)
+        y.backward(gy)
+        outs.append((y.detach().float(), xi.grad.float(), mod.lora_A.grad.clone(),
+                     mod.lora_B.grad.clone()))
+    (y1, dx1, da1, db1), (y0, dx0, da0, db0) = outs
+    torch.testing.assert_close(y1, y0, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(dx1, dx0, rtol=2e-2, atol=2e-2)
+    for a, b in ((da1, da0), (db1, db0)):
+        rel = (a - b).norm() / b.norm()
+        assert rel < 2e-2, float(rel)
+
+
 def test_checkpoint_replays_dropout_masks(cuda):
     """With dropout on, the gradients with and without activation checkpointing agree (the
     recompute must draw the same Philox masks)."""
