@@ -13,7 +13,7 @@
 // scaled add (solution/lora.py:49-60, :104) and the [T, out] adapter output disappear.
 // Replaces solution/nf4.py:100-112 (F.linear / grad_out @ W on a dequantised weight) and the
 // lora_B(lora_A(x)) + ScaledAdd of solution/lora.py:172-173.
-#include "tc_gemm.cuh"
+#include "tc_nf4_gemm.cuh"
 
 namespace {
 
@@ -108,23 +108,27 @@ extern "C" int qb_nf4_linear_fwd(const void* x, int64_t ldx, const uint8_t* pack
   if (!x || !y) return qb::fail(QB_ERR_INVALID, "nf4_linear_fwd: null pointer");
   if (r < 0 || (r > 0 && (!u || !lora_b_scaled)))
     return qb::fail(QB_ERR_INVALID, "nf4_linear_fwd: LoRA operands");
-  CUtensorMap mA0, mB0, mA1, mB1;
-  if (int s = map_codes(&mA0, packed, in_f, out_f, 32, tcg::BM)) return s;
+  if (r > 0 && ((ldlb * 2) % 16 || r % 8 || (reinterpret_cast<uintptr_t>(lora_b_scaled) & 15u)))
+    return qb::fail(QB_ERR_INVALID, "nf4_linear_fwd: LoRA B must have 16-byte rows and r %% 8 == 0");
+  int shift = 0;
+  while ((1 << shift) < blocksize2) ++shift;
+  if ((1 << shift) != blocksize2) return qb::fail(QB_ERR_UNSUPPORTED, "nf4_linear_fwd: blocksize2 must be a power of two");
+  CUtensorMap mC, mB0, mB1;
+  if (int s = map_codes(&mC, packed, in_f, out_f, 32, tcg::BM)) return s;
   if (int s = map_bf16(&mB0, x, in_f, tokens, ldx, 64, kBN)) return s;
   if (r > 0) {
-    if (int s = map_bf16(&mA1, lora_b_scaled, r, out_f, ldlb, 64, tcg::BM)) return s;
     if (int s = map_bf16(&mB1, u, r, tokens, ldu, 64, kBN)) return s;
   } else {
-    mA1 = mA0;
     mB1 = mB0;
   }
-  tcg::Problem pb{static_cast<int>(out_f), static_cast<int>(tokens), static_cast<int>(in_f / 64),
-                  static_cast<int>((r + 63) / 64), static_cast<int>((out_f + 127) / 128),
-                  static_cast<int>((tokens + kBN - 1) / kBN)};
+  tcn::NfProblem pb{static_cast<int>(out_f), static_cast<int>(tokens), static_cast<int>(in_f / 64),
+                    static_cast<int>((r + 63) / 64), static_cast<int>((out_f + 127) / 128),
+                    static_cast<int>((tokens + kBN - 1) / kBN), shift};
+  tcn::LoraA lora{static_cast<const __nv_bfloat16*>(lora_b_scaled), ldlb, static_cast<int>(r)};
   EpiStoreT epi{static_cast<__nv_bfloat16*>(y), ldy, static_cast<const __nv_bfloat16*>(bias),
                 static_cast<int>(out_f), static_cast<int>(tokens)};
-  return tcg::launch<tcg::kNf4K, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
-      mA0, mB0, mA1, mB1, pb, operand(w, in_f, out_f), epi, stream, "nf4_linear_fwd");
+  return tcn::launch_nf4<tcg::kNf4K>(mC, mB0, mB1, pb, operand(w, in_f, out_f), lora, epi, stream,
+                                     "nf4_linear_fwd");
 }
 
 extern "C" int qb_nf4_linear_dgrad(const void* dy, int64_t lddy, const uint8_t* packed,
@@ -142,21 +146,25 @@ extern "C" int qb_nf4_linear_dgrad(const void* dy, int64_t lddy, const uint8_t* 
   if (!dy || !dx) return qb::fail(QB_ERR_INVALID, "nf4_linear_dgrad: null pointer");
   if (r < 0 || (r > 0 && (!v || !lora_a)))
     return qb::fail(QB_ERR_INVALID, "nf4_linear_dgrad: LoRA operands");
-  CUtensorMap mA0, mB0, mA1, mB1;
-  if (int s = map_codes(&mA0, packed, in_f, out_f, 64, 64)) return s;
+  if (r > 0 && ((ldla * 2) % 16 || r % 8 || (reinterpret_cast<uintptr_t>(lora_a) & 15u)))
+    return qb::fail(QB_ERR_INVALID, "nf4_linear_dgrad: LoRA A must have 16-byte rows and r %% 8 == 0");
+  int shift = 0;
+  while ((1 << shift) < blocksize2) ++shift;
+  if ((1 << shift) != blocksize2) return qb::fail(QB_ERR_UNSUPPORTED, "nf4_linear_dgrad: blocksize2 must be a power of two");
+  CUtensorMap mC, mB0, mB1;
+  if (int s = map_codes(&mC, packed, in_f, out_f, 64, 64)) return s;
   if (int s = map_bf16(&mB0, dy, out_f, tokens, lddy, 64, kBN)) return s;
   if (r > 0) {
-    if (int s = map_bf16(&mA1, lora_a, in_f, r, ldla, 64, 64)) return s;   // read MN-major
     if (int s = map_bf16(&mB1, v, r, tokens, ldv, 64, kBN)) return s;
   } else {
-    mA1 = mA0;
     mB1 = mB0;
   }
-  tcg::Problem pb{static_cast<int>(in_f), static_cast<int>(tokens),
-                  static_cast<int>((out_f + 63) / 64), static_cast<int>((r + 63) / 64),
-                  static_cast<int>(in_f / 128), static_cast<int>((tokens + kBN - 1) / kBN)};
+  tcn::NfProblem pb{static_cast<int>(in_f), static_cast<int>(tokens),
+                    static_cast<int>((out_f + 63) / 64), static_cast<int>((r + 63) / 64),
+                    static_cast<int>(in_f / 128), static_cast<int>((tokens + kBN - 1) / kBN), shift};
+  tcn::LoraA lora{static_cast<const __nv_bfloat16*>(lora_a), ldla, static_cast<int>(r)};
   EpiStoreT epi{static_cast<__nv_bfloat16*>(dx), lddx, nullptr, static_cast<int>(in_f),
                 static_cast<int>(tokens)};
-  return tcg::launch<tcg::kNf4MN, tcg::kTmaK, tcg::kTmaMN, tcg::kTmaK, kBN>(
-      mA0, mB0, mA1, mB1, pb, operand(w, in_f, out_f), epi, stream, "nf4_linear_dgrad");
+  return tcn::launch_nf4<tcg::kNf4MN>(mC, mB0, mB1, pb, operand(w, in_f, out_f), lora, epi,
+                                      stream, "nf4_linear_dgrad");
 }

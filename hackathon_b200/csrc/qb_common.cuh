@@ -7,7 +7,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
-#include "../../include/qlora_b200.h"
+#include "qlora_b200.h"
 
 namespace qb {
 
