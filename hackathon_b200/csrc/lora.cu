@@ -89,7 +89,114 @@ bool rows_ok(const void* p, int64_t stride, int esize) {
   return qb::aligned16(p) && (stride * esize) % 16 == 0;
 }
 
+// Dropout that also records its mask: one warp walks a row 32 columns at a time, every lane
+// draws its element's Philox number, and the warp's ballot is the 32-bit word of mask bits.
+template <typename IT, typename OT>
+__global__ void __launch_bounds__(kThreads)
+dropout_mask_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out, int64_t outs,
+                    uint32_t* __restrict__ bits, int64_t words, int64_t rows, int64_t cols,
+                    uint32_t k0, uint32_t k1, float p, float scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  for (int64_t task = warp; task < rows * words; task += nwarps) {
+    const int64_t row = task / words, w = task % words;
+    const int64_t c = w * 32 + lane;
+    bool keep = false;
+    if (c < cols) {
+      const uint32_t off = static_cast<uint32_t>(row * cols + c);  // int32 wrap, as the reference
+      keep = uniform_of(philox_first_word(off, k0, k1)) > p;
+      const float v = qb::to_f(in[row * ins + c]);
+      out[row * outs + c] = qb::from_f<OT>(keep ? v * scale : 0.0f);
+    }
+    const uint32_t word = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) bits[row * words + w] = word;
+  }
+}
+
+// out (+)= in * bit * scale from recorded mask bits: no random numbers, one HBM pass.
+template <typename IT, typename OT, bool ACC>
+__global__ void __launch_bounds__(kThreads)
+dropout_apply_kernel(const IT* __restrict__ in, int64_t ins, const uint32_t* __restrict__ bits,
+                     int64_t words, OT* __restrict__ out, int64_t outs, int64_t rows,
+                     int64_t cols, float scale) {
+  const int64_t n8 = cols / 8;
+  const int64_t total = rows * n8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t row = i / n8, c = (i % n8) * 8;
+    const uint32_t b = (bits[row * words + c / 32] >> (c % 32)) & 0xffu;
+    float v[8];
+    qb::load8<IT>(in + row * ins + c, v);
+    if (ACC) {
+      float o[8];
+      qb::load8<OT>(out + row * outs + c, o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = o[e] + (((b >> e) & 1u) ? v[e] * scale : 0.0f);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = ((b >> e) & 1u) ? v[e] * scale : 0.0f;
+    }
+    qb::store8<OT>(out + row * outs + c, v);
+  }
+}
+
+unsigned grid_cap(int64_t work_items) {
+  int64_t g = (work_items + kThreads - 1) / kThreads;
+  if (g > 148 * 16) g = 148 * 16;
+  if (g < 1) g = 1;
+  return static_cast<unsigned>(g);
+}
+
 }  // namespace
+
+extern "C" int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stride, void* out,
+                               int out_dtype, int64_t out_row_stride, uint32_t* bits,
+                               int64_t rows, int64_t cols, uint64_t seed, float p, float scale,
+                               cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return qb::fail(QB_ERR_INVALID, "dropout_mask: bad shape");
+  if (rows == 0 || cols == 0) return QB_OK;
+  if (!in || !out || !bits) return qb::fail(QB_ERR_INVALID, "dropout_mask: null pointer");
+  if (p >= 1.0f) return qb::fail(QB_ERR_INVALID, "dropout_mask: p must be < 1");
+  const uint32_t k0 = static_cast<uint32_t>(seed & 0xffffffffu);
+  const uint32_t k1 = static_cast<uint32_t>(seed >> 32);
+  const int64_t words = (cols + 31) / 32;
+  QB_DISPATCH_FLOAT(in_dtype, IT, {
+    QB_DISPATCH_FLOAT(out_dtype, OT, {
+      dropout_mask_kernel<IT, OT><<<grid_cap(rows * words * 32), kThreads, 0, stream>>>(
+          static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out), out_row_stride, bits,
+          words, rows, cols, k0, k1, p, scale);
+    });
+  });
+  return qb::check_launch("dropout_mask");
+}
+
+extern "C" int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_stride,
+                                const uint32_t* bits, void* out, int out_dtype,
+                                int64_t out_row_stride, int64_t rows, int64_t cols, float scale,
+                                int accumulate, cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return qb::fail(QB_ERR_INVALID, "dropout_apply: bad shape");
+  if (rows == 0 || cols == 0) return QB_OK;
+  if (!in || !out || !bits) return qb::fail(QB_ERR_INVALID, "dropout_apply: null pointer");
+  if (cols % 8) return qb::fail(QB_ERR_UNSUPPORTED, "dropout_apply: cols must be a multiple of 8");
+  const int64_t words = (cols + 31) / 32;
+  QB_DISPATCH_FLOAT(in_dtype, IT, {
+    QB_DISPATCH_FLOAT(out_dtype, OT, {
+      if (!rows_ok(in, in_row_stride, sizeof(IT)) || !rows_ok(out, out_row_stride, sizeof(OT)))
+        return qb::fail(QB_ERR_INVALID, "dropout_apply: rows must be 16-byte aligned");
+      const unsigned grid = grid_cap(rows * (cols / 8));
+      if (accumulate)
+        dropout_apply_kernel<IT, OT, true><<<grid, kThreads, 0, stream>>>(
+            static_cast<const IT*>(in), in_row_stride, bits, words, static_cast<OT*>(out),
+            out_row_stride, rows, cols, scale);
+      else
+        dropout_apply_kernel<IT, OT, false><<<grid, kThreads, 0, stream>>>(
+            static_cast<const IT*>(in), in_row_stride, bits, words, static_cast<OT*>(out),
+            out_row_stride, rows, cols, scale);
+    });
+  });
+  return qb::check_launch("dropout_apply");
+}
 
 extern "C" int qb_dropout_scale(const void* in, int in_dtype, int64_t in_row_stride, void* out,
                                 int out_dtype, int64_t out_row_stride, int64_t rows, int64_t cols,

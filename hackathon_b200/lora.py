@@ -35,6 +35,33 @@ def _dropout_scale(src, out_dtype, seed, p, scale):
     return out.view(src.shape)
 
 
+def dropout_mask(x2, p, seed, scale, out_dtype=None):
+    """(dropout(x2) in out_dtype, mask bits int32 [rows, ceil(cols/32)]) — the same Philox mask
+    as DropoutCast, recorded so a recompute or a backward can reuse it without random numbers."""
+    _lib.require_cuda(x2, what="dropout_mask")
+    rows, cols = x2.shape
+    out = torch.empty((rows, cols), dtype=out_dtype or x2.dtype, device=x2.device)
+    bits = torch.empty((rows, (cols + 31) // 32), dtype=torch.int32, device=x2.device)
+    _lib.call("qb_dropout_mask", x2.data_ptr(), _lib.tag(x2.dtype), x2.stride(0), out.data_ptr(),
+              _lib.tag(out.dtype), out.stride(0), bits.data_ptr(), rows, cols,
+              int(seed) & 0xFFFFFFFFFFFFFFFF, float(p), float(scale), _lib.stream(x2.device),
+              work=(rows * cols * (x2.element_size() + out.element_size()) + bits.numel() * 4, 0))
+    return out, bits
+
+
+def dropout_apply(x2, bits, scale, out=None, accumulate=False):
+    """out = x2 * mask * scale (or out += ...) from recorded mask bits."""
+    rows, cols = x2.shape
+    if out is None:
+        out = torch.empty_like(x2)
+    _lib.call("qb_dropout_apply", x2.data_ptr(), _lib.tag(x2.dtype), x2.stride(0),
+              bits.data_ptr(), out.data_ptr(), _lib.tag(out.dtype), out.stride(0), rows, cols,
+              float(scale), int(accumulate), _lib.stream(x2.device),
+              work=(rows * cols * (x2.element_size() + out.element_size() * (2 if accumulate else 1))
+                    + bits.numel() * 4, 0))
+    return out
+
+
 class DropoutCast(torch.autograd.Function):
     """x -> dropout(x) cast to out_dtype, mask from (seed, flat index) (lora.py:84-93)."""
 

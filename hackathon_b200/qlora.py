@@ -57,6 +57,12 @@ def preset(name, **overrides):
     return replace(PRESETS[name], **overrides)
 
 
+# Dropout masks of the current step, as bits, keyed by (projection, seed): drawn in the first
+# forward, reused by the checkpoint recompute and the backward, dropped after the backward.
+# QwenQLoRA.forward clears whatever a forward without backward left behind.
+MASKS = {}
+
+
 class LoRANF4Proj(torch.autograd.Function):
     """The whole QLoRA projection on the fused kernels:
 
@@ -70,24 +76,36 @@ class LoRANF4Proj(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, lora_a, lora_b, mod, p, seed):
-        from .lora import _dropout_scale
+        from .lora import dropout_apply, dropout_mask
         from .nf4 import nf4_linear_fwd
         x2 = x.reshape(-1, x.shape[-1])
         scale = 1.0 / (1.0 - p) if p > 0 else 1.0
-        xd = _dropout_scale(x2, x2.dtype, seed, p, scale) if p > 0 else x2
+        bits = None
+        if p > 0:
+            # the mask is drawn once per step (Philox, the reference's stream) and kept as bits:
+            # the checkpoint recompute and the backward reuse it instead of redrawing
+            key = (id(mod), seed)
+            bits = MASKS.get(key)
+            if bits is None or bits.shape[0] != x2.shape[0]:
+                xd, bits = dropout_mask(x2, p, seed, scale)
+                MASKS[key] = bits
+            else:
+                xd = dropout_apply(x2, bits, scale)
+        else:
+            xd = x2
         a16 = lora_a.to(x.dtype)
         sb16 = (lora_b * mod.scaling).to(x.dtype)
         u = xd @ a16.t()
         y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16)
-        ctx.save_for_backward(x2, u, lora_a, lora_b)
+        ctx.save_for_backward(x2, u, lora_a, lora_b, bits)
         ctx.mod, ctx.p, ctx.seed, ctx.scale, ctx.shape = mod, p, seed, scale, x.shape
         return y.view(*x.shape[:-1], y.shape[-1])
 
     @staticmethod
     def backward(ctx, g):
-        from .lora import _dropout_scale
+        from .lora import dropout_apply
         from .nf4 import nf4_linear_dgrad
-        x2, u, lora_a, lora_b = ctx.saved_tensors
+        x2, u, lora_a, lora_b, bits = ctx.saved_tensors
         mod, p = ctx.mod, ctx.p
         g2 = g.reshape(-1, g.shape[-1])
         if g2.dtype != x2.dtype:
@@ -96,10 +114,10 @@ class LoRANF4Proj(torch.autograd.Function):
         sb16 = (lora_b * mod.scaling).to(x2.dtype)
         v = g2 @ sb16                                              # [T, r]
         if p > 0:
+            MASKS.pop((id(mod), ctx.seed), None)
             dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state)
-            dxd = v @ a16
-            dx += _dropout_scale(dxd, dxd.dtype, ctx.seed, p, ctx.scale)
-            xd = _dropout_scale(x2, x2.dtype, ctx.seed, p, ctx.scale)
+            dropout_apply(v @ a16, bits, ctx.scale, out=dx, accumulate=True)
+            xd = dropout_apply(x2, bits, ctx.scale)
         else:
             dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, v, a16)
             xd = x2
@@ -216,6 +234,7 @@ class QwenQLoRA(torch.nn.Module):
 
     def forward(self, input_ids, labels, num_items_in_batch=None):
         B, S = input_ids.shape
+        MASKS.clear()
         cos, sin = self.rope_tables(S, input_ids.device)
         h = F.embedding(input_ids, self.embed)
         for i, layer in enumerate(self.layers):

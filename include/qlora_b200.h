@@ -146,6 +146,20 @@ int qb_dropout_scale(const void* in, int in_dtype, int64_t in_row_stride, void* 
                      int out_dtype, int64_t out_row_stride, int64_t rows, int64_t cols,
                      uint64_t seed, float p, float scale, cudaStream_t stream);
 
+/* qb_dropout_scale that also records its mask: bits[r * words + c / 32] bit (c % 32) =
+ * keep(r, c), words = ceil(cols / 32) (the same Philox stream, so the same mask). The recorded
+ * mask lets the checkpoint recompute and the backward skip the random numbers (a variant of
+ * solution/lora.py:29-46, which regenerates the mask from the seed each time). */
+int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stride, void* out,
+                    int out_dtype, int64_t out_row_stride, uint32_t* bits, int64_t rows,
+                    int64_t cols, uint64_t seed, float p, float scale, cudaStream_t stream);
+
+/* out = in * bit * scale (accumulate = 0) or out += in * bit * scale (accumulate = 1) with the
+ * bits of qb_dropout_mask; cols a multiple of 8, 16-byte-aligned rows. */
+int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_stride, const uint32_t* bits,
+                     void* out, int out_dtype, int64_t out_row_stride, int64_t rows,
+                     int64_t cols, float scale, int accumulate, cudaStream_t stream);
+
 /* out = base + lo * scaling (fp32 math). Replaces solution/lora.py:49-60
  * (lora_scaled_add_kernel). */
 int qb_scaled_add(const void* base, int base_dtype, int64_t base_row_stride, const void* lo,

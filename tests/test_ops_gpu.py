@@ -339,6 +339,29 @@ def test_dropout_flat_index_wraps_like_int32(cuda):
         assert np.array_equal((out[r] != 0).cpu().numpy(), want), r
 
 
+@pytest.mark.parametrize("rows,cols", [(64, 1536), (300, 3584), (7, 40)])
+def test_recorded_mask_is_the_reference_stream(cuda, rows, cols):
+    """qb_dropout_mask records exactly the reference's Philox mask as bits and produces the same
+    output as the regenerating kernel; qb_dropout_apply replays it (and accumulates)."""
+    from hackathon_b200.lora import DropoutCast, dropout_apply, dropout_mask
+    p, seed = 0.1, 424242
+    scale = 1.0 / (1.0 - p)
+    x = torch.randn(rows, cols, device=cuda).to(torch.bfloat16)
+    y, bits = dropout_mask(x, p, seed, scale)
+    want = nf4_ref.dropout_keep(seed, rows, cols, p)
+    unpacked = ((bits.cpu().numpy().view(np.uint32)[:, :, None] >> np.arange(32)) & 1).reshape(
+        rows, -1)[:, :cols].astype(bool)
+    assert np.array_equal(unpacked, want)
+    assert torch.equal(y, DropoutCast.apply(x, p, seed, torch.bfloat16))
+    if cols % 8 == 0:
+        assert torch.equal(dropout_apply(x, bits, scale), y)
+        acc = torch.ones_like(x)
+        dropout_apply(x, bits, scale, out=acc, accumulate=True)
+        keep = torch.from_numpy(want).to(cuda)
+        expect = (1.0 + torch.where(keep, x.float() * scale, torch.zeros_like(x.float())))
+        assert torch.equal(acc, expect.to(torch.bfloat16))   # one rounding, as the kernel
+
+
 @pytest.mark.parametrize("out_features", [1536, 256])
 def test_scaled_add_matches_peft(cuda, out_features):
     from hackathon_b200.lora import ScaledAdd
