@@ -123,7 +123,7 @@ extern "C" int qb_nf4_linear_fwd(const void* x, int64_t ldx, const uint8_t* pack
   }
   tcn::NfProblem pb{static_cast<int>(out_f), static_cast<int>(tokens), static_cast<int>(in_f / 64),
                     static_cast<int>((r + 63) / 64), static_cast<int>((out_f + 127) / 128),
-                    static_cast<int>((tokens + kBN - 1) / kBN), shift};
+                    static_cast<int>((tokens + tcn::kTN - 1) / tcn::kTN), shift};
   tcn::LoraA lora{static_cast<const __nv_bfloat16*>(lora_b_scaled), ldlb, static_cast<int>(r)};
   EpiStoreT epi{static_cast<__nv_bfloat16*>(y), ldy, static_cast<const __nv_bfloat16*>(bias),
                 static_cast<int>(out_f), static_cast<int>(tokens)};
@@ -161,7 +161,7 @@ extern "C" int qb_nf4_linear_dgrad(const void* dy, int64_t lddy, const uint8_t* 
   }
   tcn::NfProblem pb{static_cast<int>(in_f), static_cast<int>(tokens),
                     static_cast<int>((out_f + 63) / 64), static_cast<int>((r + 63) / 64),
-                    static_cast<int>(in_f / 128), static_cast<int>((tokens + kBN - 1) / kBN), shift};
+                    static_cast<int>(in_f / 128), static_cast<int>((tokens + tcn::kTN - 1) / tcn::kTN), shift};
   tcn::LoraA lora{static_cast<const __nv_bfloat16*>(lora_a), ldla, static_cast<int>(r)};
   EpiStoreT epi{static_cast<__nv_bfloat16*>(dx), lddx, nullptr, static_cast<int>(in_f),
                 static_cast<int>(tokens)};

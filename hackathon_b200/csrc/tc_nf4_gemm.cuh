@@ -5,14 +5,18 @@
 //
 // Three shared-memory rings decouple the latencies:
 //   codes ring (8 x 4 KiB)   packed NF4 codes of one 128 x 64 A tile, TMA (warp 6)
-//   B ring     (4 x 32 KiB)  256 x 64 activation tile, TMA (warp 0)
+//   B ring     (2 x 64 KiB)  512 x 64 activation tile (two 256-row halves), TMA (warp 0)
 //   A ring     (3 x 16 KiB)  the bf16 A tile in the swizzled layout the MMA reads, written by
 //                            two groups of eight dequant warps (warps 7-22) taking alternate k-blocks
 //                            (32 weights per thread): NF4 codes x block scale for segment 0, a copy
 //                            of the LoRA matrix for segment 1
 // The codes ring runs far ahead of the dequant warps, which run up to three k-blocks ahead of
-// the MMA; with alternate k-blocks each warp has two MMA k-steps to turn one tile around. Warp 1 issues the MMAs (one thread), warps 2-5 run the epilogue from double-buffered
-// TMEM accumulators. Every wait is bounded; a wait that gives up raises the device error flag
+// the MMA; with alternate k-blocks each warp has two MMA k-steps to turn one tile around.
+// An output tile is 128 x 512: each dequantised A k-slice feeds two N=256 MMAs, which halves the
+// dequant work and its shared-memory traffic per flop (shared-memory bandwidth, not the tensor
+// pipe, bounds this kernel). The two 256-column accumulators fill all 512 TMEM columns, so the
+// epilogue (warps 2-5) drains a tile before the MMAs of the next one start. Warp 1 issues the
+// MMAs (one thread). Every wait is bounded; a wait that gives up raises the device error flag
 // and every role drains out; TMEM is always released.
 #pragma once
 
@@ -23,10 +27,12 @@ namespace tcn {
 using tcg::BK;
 using tcg::BM;
 
-constexpr int kBN = 256;
-constexpr int kStagesB = 4, kStagesA = 3, kStagesC = 8;
+constexpr int kBN = 256;            // N of one MMA
+constexpr int kNT = 2;              // MMAs per k-step: the output tile is 128 x 512
+constexpr int kTN = kBN * kNT;
+constexpr int kStagesB = 2, kStagesA = 3, kStagesC = 8;
 constexpr int kA = BM * 128;        // 16 KiB
-constexpr int kB = kBN * 128;       // 32 KiB
+constexpr int kB = kTN * 128;       // 64 KiB
 constexpr int kC = 4096;            // packed codes of one A tile
 constexpr int kThreads = 736;       // 23 warps
 constexpr int kWarpCodes = 6, kWarpDeq0 = 7;
@@ -147,13 +153,16 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
       uint32_t ph = 0;
       long issued = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !tc::failed(err); tile += gridDim.x) {
-        const int n0 = (tile / pb.num_m) * kBN;
+        const int n0 = (tile / pb.num_m) * kTN;
         for (int kb = 0; kb < nk; ++kb) {
           if (!tc::mbar_wait(&emptyB[st], ph ^ 1, err, 11)) break;
           const bool seg1 = kb >= pb.nk0;
+          const int k = (seg1 ? kb - pb.nk0 : kb) * BK;
           tc::mbar_expect_tx(&fullB[st], kB);
-          tc::tma_load_2d(ringB + st * kB, seg1 ? &mB1 : &mB0, &fullB[st],
-                          (seg1 ? kb - pb.nk0 : kb) * BK, n0);
+#pragma unroll
+          for (int j = 0; j < kNT; ++j)
+            tc::tma_load_2d(ringB + st * kB + j * (kBN * 128), seg1 ? &mB1 : &mB0, &fullB[st], k,
+                            n0 + j * kBN);
           if (++st == kStagesB) { st = 0; ph ^= 1; }
           ++issued;
         }
@@ -194,10 +203,10 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
       uint32_t pbh = 0, pah = 0;
       int t = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !tc::failed(err); tile += gridDim.x, ++t) {
-        const int buf = t & 1;
-        if (!tc::mbar_wait(&tempty[buf], ((t >> 1) & 1) ^ 1, err, 13)) break;
+        // one accumulator set (all 512 columns): wait until the epilogue drained the last tile
+        if (!tc::mbar_wait(&tempty[0], (t & 1) ^ 1, err, 13)) break;
         tc::fence_after_sync();
-        const uint32_t d = tmem_base + buf * kBN;
+        const uint32_t d = tmem_base;
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!tc::mbar_wait(&fullB[sb], pbh, err, 14) || !tc::mbar_wait(&fullA[sa], pah, err, 15)) {
@@ -212,8 +221,11 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t a = kMN ? tc::sdesc_sw128(a_s + kk * 2048, 8192, 1024)
                                    : tc::sdesc_sw128(a_s + kk * 32, 16, 1024);
-            const uint64_t b = tc::sdesc_sw128(b_s + kk * 32, 16, 1024);
-            tc::mma_bf16(d, a, b, idesc, (kb | kk) != 0);
+#pragma unroll
+            for (int j = 0; j < kNT; ++j) {
+              const uint64_t b = tc::sdesc_sw128(b_s + j * (kBN * 128) + kk * 32, 16, 1024);
+              tc::mma_bf16(d + j * kBN, a, b, idesc, (kb | kk) != 0);
+            }
           }
           tc::mma_commit(&emptyB[sb]);
           tc::mma_commit(&emptyA[sa]);
@@ -221,7 +233,7 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
           if (++sa == kStagesA) { sa = 0; pah ^= 1; }
         }
         if (!ok) break;
-        tc::mma_commit(&tfull[buf]);
+        tc::mma_commit(&tfull[0]);
       }
       tc::mma_commit(drain);
       tc::mbar_wait_quiet(drain, 0);
@@ -232,15 +244,15 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
     const int row = quarter * 32 + lane;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
-      const int buf = t & 1;
-      const bool ready = tc::mbar_wait(&tfull[buf], (t >> 1) & 1, err, 16);
+      const bool ready = tc::mbar_wait(&tfull[0], t & 1, err, 16);
       if (!__all_sync(0xffffffffu, ready)) break;
       tc::fence_after_sync();
-      const int m0 = (tile % pb.num_m) * BM, n0 = (tile / pb.num_m) * kBN;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kBN;
-      epi.template tile<kBN>(m0, n0, row, taddr);
+      const int m0 = (tile % pb.num_m) * BM, n0 = (tile / pb.num_m) * kTN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+      for (int j = 0; j < kNT; ++j) epi.template tile<kBN>(m0, n0 + j * kBN, row, taddr + j * kBN);
       tc::fence_before_sync();
-      tc::mbar_arrive(&tempty[buf]);
+      tc::mbar_arrive(&tempty[0]);
     }
   } else {
     // ------------------------------------------------------------ dequant (warps 7-22)
