@@ -43,7 +43,8 @@ WORKLOADS = {
 BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hbm",
          "qb_rope_qk": "hbm", "qb_swiglu_fwd": "hbm", "qb_swiglu_bwd": "hbm",
          "qb_dropout_scale": "hbm", "qb_scaled_add": "hbm", "qb_ce_rows": "hbm",
-         "qb_ce_reduce": "hbm", "qb_gemm_bf16": "tensor", "qb_nf4_linear_fwd": "tensor",
+         "qb_ce_reduce": "hbm", "qb_gemm_bf16": "tensor", "qb_gemm2_bf16": "tensor",
+         "qb_nf4_linear_fwd": "tensor",
          "qb_nf4_linear_dgrad": "tensor", "qb_linear_ce_stats": "tensor",
          "qb_linear_ce_grad": "tensor"}
 

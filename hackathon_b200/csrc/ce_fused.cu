@@ -194,7 +194,7 @@ extern "C" int qb_linear_ce_stats(const void* hidden, int64_t ldh, const void* w
   EpiStats epi{static_cast<float4*>(partials), z_label, target, static_cast<int>(rows),
                 static_cast<int>(vocab)};
   return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
-      mh, mw, mh, mw, pb, tcg::Nf4Operand{}, epi, stream, "linear_ce_stats");
+      mh, mw, mh, mw, pb, epi, stream, "linear_ce_stats");
 }
 
 extern "C" int qb_ce_reduce(const void* partials, int64_t n_vtiles, int64_t rows, int64_t vocab,
@@ -228,5 +228,5 @@ extern "C" int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* we
   EpiGrad epi{static_cast<__nv_bfloat16*>(dz), ldz, target, lse, scale_dev,
               static_cast<int>(rows), static_cast<int>(vocab), vec};
   return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
-      mh, mw, mh, mw, pb, tcg::Nf4Operand{}, epi, stream, "linear_ce_grad");
+      mh, mw, mh, mw, pb, epi, stream, "linear_ce_grad");
 }

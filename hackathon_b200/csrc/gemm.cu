@@ -1,9 +1,14 @@
-// Plain bf16 GEMM on the tcgen05 kernel: C[M,N] = A[M,K] * B[N,K]^T (+ bias[N]), fp32
-// accumulation, fp32 or bf16 output. A and B may each be K-major or MN-major in HBM, which covers
-// every orientation the suite needs (logits = H W^T, dH = dZ W, LoRA products).
+// Plain bf16 GEMMs on the tcgen05 kernel, fp32 accumulation, fp32 or bf16 output:
+//   qb_gemm_bf16    C[M,N] = A[M,K] * B[N,K]^T (+ bias[N])
+//   qb_gemm2_bf16   C[M,N] = A0[M,K0] * B0[N,K0]^T + A1[M,K1] * B1[N,K1]^T (+ bias[N])
+// Each operand may be K-major or MN-major in HBM (qb_gemm_bf16: every orientation the suite
+// needs — logits = H W^T, dH = dZ W, LoRA products; qb_gemm2_bf16: the two layouts of a
+// projection with its LoRA term as extra K, forward and input gradient).
 #include "tc_gemm.cuh"
 
 namespace {
+
+constexpr int kBN = 256;
 
 // Row-major store: each epilogue thread owns one output row of the tile and writes its 32
 // consecutive columns per TMEM chunk with 16-byte stores.
@@ -51,12 +56,37 @@ int map_operand(CUtensorMap* map, const void* p, int64_t ld, bool mn_major, int6
                             CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int AS, int BS, typename OutT>
-int run(const CUtensorMap& ma, const CUtensorMap& mb, const tcg::Problem& pb, OutT* c,
-        int64_t ldc, const float* bias, bool vec, cudaStream_t s) {
-  EpiStoreRow<OutT> epi{c, ldc, pb.M, pb.N, bias, vec};
-  return tcg::launch<AS, BS, tcg::kTmaK, tcg::kTmaK, 256>(ma, mb, ma, mb, pb, tcg::Nf4Operand{},
-                                                          epi, s, "gemm_bf16");
+template <int A0, int B0, int A1, int B1, typename OutT>
+int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
+        const float* bias, bool vec, cudaStream_t s, const char* what) {
+  EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias, vec};
+  return tcg::launch<A0, B0, A1, B1, kBN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
+}
+
+template <int A0, int B0, int A1, int B1>
+int run_dtype(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
+              int c_dtype, const float* bias, bool vec, cudaStream_t s, const char* what) {
+  if (c_dtype == QB_F32) return run<A0, B0, A1, B1, float>(m, pb, c, ldc, bias, vec, s, what);
+  return run<A0, B0, A1, B1, __nv_bfloat16>(m, pb, c, ldc, bias, vec, s, what);
+}
+
+int check_common(const void* C, int c_dtype, int64_t M, int64_t N, const char* what) {
+  if (M < 0 || N < 0 || M > (1 << 30) || N > (1 << 30))
+    return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
+  if (!C) return qb::fail(QB_ERR_INVALID, "%s: null output", what);
+  if (c_dtype != QB_F32 && c_dtype != QB_BF16)
+    return qb::fail(QB_ERR_INVALID, "%s: output must be F32 or BF16", what);
+  return QB_OK;
+}
+
+tcg::Problem problem(int64_t M, int64_t N, int64_t K0, int64_t K1) {
+  return tcg::Problem{static_cast<int>(M), static_cast<int>(N), static_cast<int>((K0 + 63) / 64),
+                      static_cast<int>((K1 + 63) / 64), static_cast<int>((M + 127) / 128),
+                      static_cast<int>((N + kBN - 1) / kBN)};
+}
+
+bool vec_ok(const void* C, int64_t ldc, int c_dtype) {
+  return qb::aligned16(C) && (ldc * (c_dtype == QB_F32 ? 4 : 2)) % 16 == 0;
 }
 
 }  // namespace
@@ -65,28 +95,58 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const vo
                             int64_t ldb, int b_mn_major, void* C, int64_t ldc, int c_dtype,
                             const float* bias, int64_t M, int64_t N, int64_t K,
                             cudaStream_t stream) {
-  if (M < 0 || N < 0 || K < 0 || M > (1 << 30) || N > (1 << 30) || K > (1 << 30))
-    return qb::fail(QB_ERR_INVALID, "gemm_bf16: bad shape");
+  const char* what = "gemm_bf16";
+  if (int s = check_common(C, c_dtype, M, N, what)) return s;
+  if (K < 0 || K > (1 << 30)) return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
   if (M == 0 || N == 0) return QB_OK;
-  if (K == 0) return qb::fail(QB_ERR_UNSUPPORTED, "gemm_bf16: K == 0");
-  if (!A || !B || !C) return qb::fail(QB_ERR_INVALID, "gemm_bf16: null pointer");
-  if (c_dtype != QB_F32 && c_dtype != QB_BF16)
-    return qb::fail(QB_ERR_INVALID, "gemm_bf16: output must be F32 or BF16");
-  CUtensorMap ma, mb;
-  if (int s = map_operand(&ma, A, lda, a_mn_major != 0, M, K, 128)) return s;
-  if (int s = map_operand(&mb, B, ldb, b_mn_major != 0, N, K, 256)) return s;
-  tcg::Problem pb{static_cast<int>(M), static_cast<int>(N), static_cast<int>((K + 63) / 64), 0,
-                  static_cast<int>((M + 127) / 128), static_cast<int>((N + 255) / 256)};
-  const int es = c_dtype == QB_F32 ? 4 : 2;
-  const bool vec = qb::aligned16(C) && (ldc * es) % 16 == 0;
-#define QB_GEMM_CASE(AS, BS)                                                                 \
-  if (c_dtype == QB_F32)                                                                     \
-    return run<AS, BS, float>(ma, mb, pb, static_cast<float*>(C), ldc, bias, vec, stream);  \
-  return run<AS, BS, __nv_bfloat16>(ma, mb, pb, static_cast<__nv_bfloat16*>(C), ldc, bias, \
-                                    vec, stream);
-  if (!a_mn_major && !b_mn_major) { QB_GEMM_CASE(tcg::kTmaK, tcg::kTmaK) }
-  if (!a_mn_major && b_mn_major) { QB_GEMM_CASE(tcg::kTmaK, tcg::kTmaMN) }
-  if (a_mn_major && !b_mn_major) { QB_GEMM_CASE(tcg::kTmaMN, tcg::kTmaK) }
-  QB_GEMM_CASE(tcg::kTmaMN, tcg::kTmaMN)
-#undef QB_GEMM_CASE
+  if (K == 0) return qb::fail(QB_ERR_UNSUPPORTED, "%s: K == 0", what);
+  if (!A || !B) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  CUtensorMap m[4];
+  if (int s = map_operand(&m[0], A, lda, a_mn_major != 0, M, K, tcg::BM)) return s;
+  if (int s = map_operand(&m[1], B, ldb, b_mn_major != 0, N, K, kBN)) return s;
+  m[2] = m[0];
+  m[3] = m[1];
+  const tcg::Problem pb = problem(M, N, K, 0);
+  const bool vec = vec_ok(C, ldc, c_dtype);
+  using namespace tcg;
+  if (!a_mn_major && !b_mn_major)
+    return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+  if (!a_mn_major && b_mn_major)
+    return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+  if (a_mn_major && !b_mn_major)
+    return run_dtype<kTmaMN, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+  return run_dtype<kTmaMN, kTmaMN, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+}
+
+extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,
+                             int64_t ldb0, int b0_mn_major, int64_t K0, const void* A1,
+                             int64_t lda1, int a1_mn_major, const void* B1, int64_t ldb1,
+                             int b1_mn_major, int64_t K1, void* C, int64_t ldc, int c_dtype,
+                             const float* bias, int64_t M, int64_t N, cudaStream_t stream) {
+  const char* what = "gemm2_bf16";
+  if (K1 == 0)
+    return qb_gemm_bf16(A0, lda0, a0_mn_major, B0, ldb0, b0_mn_major, C, ldc, c_dtype, bias, M,
+                        N, K0, stream);
+  if (int s = check_common(C, c_dtype, M, N, what)) return s;
+  if (K0 <= 0 || K1 < 0 || K0 > (1 << 30) || K1 > (1 << 30))
+    return qb::fail(QB_ERR_INVALID, "%s: bad K", what);
+  if (M == 0 || N == 0) return QB_OK;
+  if (!A0 || !B0 || !A1 || !B1) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  // the two layouts a projection with its adapter term takes (forward / input gradient)
+  const bool fwd = !a0_mn_major && !b0_mn_major && !a1_mn_major && !b1_mn_major;
+  const bool bwd = !a0_mn_major && b0_mn_major && !a1_mn_major && b1_mn_major;
+  if (!fwd && !bwd)
+    return qb::fail(QB_ERR_UNSUPPORTED, "%s: A operands K-major, B operands both K- or MN-major",
+                    what);
+  CUtensorMap m[4];
+  if (int s = map_operand(&m[0], A0, lda0, false, M, K0, tcg::BM)) return s;
+  if (int s = map_operand(&m[1], B0, ldb0, bwd, N, K0, kBN)) return s;
+  if (int s = map_operand(&m[2], A1, lda1, false, M, K1, tcg::BM)) return s;
+  if (int s = map_operand(&m[3], B1, ldb1, bwd, N, K1, kBN)) return s;
+  const tcg::Problem pb = problem(M, N, K0, K1);
+  const bool vec = vec_ok(C, ldc, c_dtype);
+  using namespace tcg;
+  if (fwd)
+    return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+  return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
 }

@@ -2,9 +2,9 @@
 // dequantised in registers straight into the MMA operand (no bf16 W in HBM).
 //
 // The GEMM runs "swapped": the weight is the A operand (128 weight rows or columns per tile,
-// rebuilt by four dequant warps from packed codes that TMA brings in) and the tokens are B
-// (256 per tile, by TMA), so one MMA instruction is M=128 x N=256 x K=16 and the dequant cost
-// per flop is 1/256 weight per multiply-add. The epilogue writes the tile transposed into the
+// rebuilt by the dequant warps from packed codes that TMA brings in) and the tokens are B
+// (512 per tile, by TMA, as two N=256 MMAs), so the dequant cost per flop is 1/512 weight per
+// multiply-add. The epilogue writes the tile transposed into the
 // row-major [tokens, features] output.
 //
 //   forward  Y^T[out, T]  = [ W | s*B_lora ] [ X | U ]^T (+ bias)       U = dropout(X) A_lora^T
@@ -66,8 +66,8 @@ int check_nf4(const Nf4Ptrs& w, int64_t in_f, int64_t out_f, const char* what) {
   return QB_OK;
 }
 
-tcg::Nf4Operand operand(const Nf4Ptrs& w, int64_t in_f, int64_t out_f) {
-  tcg::Nf4Operand q;
+tcn::Nf4Operand operand(const Nf4Ptrs& w, int64_t in_f, int64_t out_f) {
+  tcn::Nf4Operand q;
   q.absmax_q = w.absmax_q;
   q.absmax2 = w.absmax2;
   q.code2 = w.code2;
@@ -127,7 +127,7 @@ extern "C" int qb_nf4_linear_fwd(const void* x, int64_t ldx, const uint8_t* pack
   tcn::LoraA lora{static_cast<const __nv_bfloat16*>(lora_b_scaled), ldlb, static_cast<int>(r)};
   EpiStoreT epi{static_cast<__nv_bfloat16*>(y), ldy, static_cast<const __nv_bfloat16*>(bias),
                 static_cast<int>(out_f), static_cast<int>(tokens)};
-  return tcn::launch_nf4<tcg::kNf4K>(mC, mB0, mB1, pb, operand(w, in_f, out_f), lora, epi, stream,
+  return tcn::launch_nf4<tcn::kNf4K>(mC, mB0, mB1, pb, operand(w, in_f, out_f), lora, epi, stream,
                                      "nf4_linear_fwd");
 }
 
@@ -165,6 +165,6 @@ extern "C" int qb_nf4_linear_dgrad(const void* dy, int64_t lddy, const uint8_t* 
   tcn::LoraA lora{static_cast<const __nv_bfloat16*>(lora_a), ldla, static_cast<int>(r)};
   EpiStoreT epi{static_cast<__nv_bfloat16*>(dx), lddx, nullptr, static_cast<int>(in_f),
                 static_cast<int>(tokens)};
-  return tcn::launch_nf4<tcg::kNf4MN>(mC, mB0, mB1, pb, operand(w, in_f, out_f), lora, epi,
+  return tcn::launch_nf4<tcn::kNf4MN>(mC, mB0, mB1, pb, operand(w, in_f, out_f), lora, epi,
                                       stream, "nf4_linear_dgrad");
 }

@@ -13,11 +13,16 @@
 // The codes ring runs far ahead of the dequant warps, which run up to three k-blocks ahead of
 // the MMA; with alternate k-blocks each warp has two MMA k-steps to turn one tile around.
 // An output tile is 128 x 512: each dequantised A k-slice feeds two N=256 MMAs, which halves the
-// dequant work and its shared-memory traffic per flop (shared-memory bandwidth, not the tensor
-// pipe, bounds this kernel). The two 256-column accumulators fill all 512 TMEM columns, so the
-// epilogue (warps 2-5) drains a tile before the MMAs of the next one start. Warp 1 issues the
-// MMAs (one thread). Every wait is bounded; a wait that gives up raises the device error flag
-// and every role drains out; TMEM is always released.
+// dequant work and its shared-memory traffic per flop. The hand-off of the thread-written A
+// operand (stores, proxy fence, barrier round trip), not the tensor pipe, bounds this kernel:
+// with the dequant arithmetic removed it still runs at ~1.1 PFLOP/s, against ~1.4 for the same
+// contraction with A brought in by TMA. Long token counts therefore go through a transient
+// bf16 weight and the TMA-fed GEMM instead (the host-side dispatch); this kernel serves the
+// short ones, where reading 0.5 byte per weight instead of 2 is what counts. The two 256-column
+// accumulators fill all 512 TMEM columns, so the epilogue (warps 2-5) drains a tile before the
+// MMAs of the next one start. Warp 1 issues the MMAs (one thread). Every wait is bounded; a
+// wait that gives up raises the device error flag and every role drains out; TMEM is always
+// released.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -26,6 +31,51 @@ namespace tcn {
 
 using tcg::BK;
 using tcg::BM;
+
+enum Nf4Src : int { kNf4K = 2, kNf4MN = 3 };   // A = W (K-major) or A = W^T (MN-major)
+
+struct Nf4Operand {
+  const uint8_t* absmax_q;  // uint8 codes of the block scales [rows * blocks_per_row]
+  const float* absmax2;     // second-level scales
+  const float* code2;       // [256]
+  const float* lut;         // NF4 code book [16]
+  float offset;
+  int blocksize2;
+  int blocks_per_row;       // in_features / 64
+  int rows;                 // out_features
+  int cols;                 // in_features
+};
+
+// Per code byte: both nibble indices come pre-multiplied by 4 (one shift + mask per 4 bytes,
+// one byte permute per index), the two table values are multiplied by the scale in one packed
+// f32x2 multiply (two IEEE round-to-nearest products, as two scalar multiplies would give) and
+// rounded to bf16 in one cvt. Byte j of the codes holds weights 2j (high nibble) and 2j+1.
+__device__ __forceinline__ uint32_t nf4_pair(const float* lut, uint32_t hi4, uint32_t lo4, int b,
+                                             uint64_t scale2) {
+  const uint32_t ih = __byte_perm(hi4, 0u, 0x4440u | b);
+  const uint32_t il = __byte_perm(lo4, 0u, 0x4440u | b);
+  const float vh = *reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(lut) + ih);
+  const float vl = *reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(lut) + il);
+  uint64_t v, p;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(vh), "f"(vl));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(scale2));
+  float ph, pl;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(ph), "=f"(pl) : "l"(p));
+  __nv_bfloat162 r = __floats2bfloat162_rn(ph, pl);   // weight 2j (high nibble) in the low half
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// The raw ingredients of one block scale (code of the first-level absmax, second-level scale),
+// loaded a couple of k-steps before they are needed; code < 0 marks an out-of-range block.
+struct ScaleRaw {
+  int code;
+  float a2;
+};
+
+// scale = code2[code] * absmax2 + offset: a rounded multiply, then a rounded add (no FMA).
+__device__ __forceinline__ float scale_of(const ScaleRaw& r, const float* s_code2, float offset) {
+  return r.code < 0 ? 0.f : __fadd_rn(__fmul_rn(s_code2[r.code], r.a2), offset);
+}
 
 constexpr int kBN = 256;            // N of one MMA
 constexpr int kNT = 2;              // MMAs per k-step: the output tile is 128 x 512
@@ -84,7 +134,7 @@ __device__ __forceinline__ void dequant32(const uint8_t* codes, float scale, con
     const uint32_t lo4 = (x << 2) & 0x3C3C3C3Cu;
     uint32_t o[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) o[b] = tcg::nf4_pair(lut, hi4, lo4, b, scale2);
+    for (int b = 0; b < 4; ++b) o[b] = nf4_pair(lut, hi4, lo4, b, scale2);
     *reinterpret_cast<uint4*>(row + (((c0 + cl) ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
@@ -93,9 +143,9 @@ template <int A0, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant__ CUtensorMap mB0,
               const __grid_constant__ CUtensorMap mB1, const NfProblem pb,
-              const tcg::Nf4Operand nf4, const LoraA lora, Epi epi, int* err) {
-  static_assert(A0 == tcg::kNf4K || A0 == tcg::kNf4MN, "A0 is an NF4 source");
-  constexpr bool kMN = A0 == tcg::kNf4MN;
+              const Nf4Operand nf4, const LoraA lora, Epi epi, int* err) {
+  static_assert(A0 == kNf4K || A0 == kNf4MN, "A0 is an NF4 source");
+  constexpr bool kMN = A0 == kNf4MN;
   constexpr uint32_t kIdesc0 = tc::idesc_bf16(BM, kBN, kMN, false);
   constexpr uint32_t kIdesc1 = kIdesc0;   // segment-1 A uses the same major-ness
 
@@ -279,14 +329,14 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
       a_blk = q;
     }
     const float offset = nf4.offset;
-    auto raw_for = [&](int tile, int kb) -> tcg::ScaleRaw {
-      if (tile >= num_tiles || kb >= pb.nk0) return tcg::ScaleRaw{-1, 0.f};
+    auto raw_for = [&](int tile, int kb) -> ScaleRaw {
+      if (tile >= num_tiles || kb >= pb.nk0) return ScaleRaw{-1, 0.f};
       const int m0 = (tile % pb.num_m) * BM;
       const int row = kMN ? kb * BK + a_row : m0 + a_row;
       const int blk_in_row = kMN ? (m0 >> 6) + (a_blk >> 1) : kb;
-      if (row >= nf4.rows || blk_in_row >= nf4.blocks_per_row) return tcg::ScaleRaw{-1, 0.f};
+      if (row >= nf4.rows || blk_in_row >= nf4.blocks_per_row) return ScaleRaw{-1, 0.f};
       const int64_t blk = static_cast<int64_t>(row) * nf4.blocks_per_row + blk_in_row;
-      return tcg::ScaleRaw{static_cast<int>(__ldg(nf4.absmax_q + blk)),
+      return ScaleRaw{static_cast<int>(__ldg(nf4.absmax_q + blk)),
                            __ldg(nf4.absmax2 + (blk >> pb.bs2_shift))};
     };
     // the item (tile, kb) two k-blocks after (tile, kb): this group's next one
@@ -300,20 +350,20 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
     bool ok = true;
     int pt = blockIdx.x, pk = group;              // this group's next item to prefetch
     while (pk >= nk && pt < num_tiles) { pk -= nk; pt += gridDim.x; }
-    tcg::ScaleRaw pre = raw_for(pt, pk);
+    ScaleRaw pre = raw_for(pt, pk);
     for (int tile = blockIdx.x; tile < num_tiles && ok && !tc::failed(err); tile += gridDim.x) {
       const int m0 = (tile % pb.num_m) * BM;
       for (int kb = 0; kb < nk; ++kb, ++it) {
         const bool seg0 = kb < pb.nk0;
         if ((it % kGroups) == group) {
-          const tcg::ScaleRaw cur = pre;
+          const ScaleRaw cur = pre;
           next2(pt, pk);
           pre = raw_for(pt, pk);
           if (!tc::mbar_wait(&emptyA[sa], pah ^ 1, err, 17)) { ok = false; break; }
           uint8_t* a_dst = ringA + sa * kA + off_row;
           if (seg0) {
             if (!tc::mbar_wait(&fullC[sc], pch, err, 18)) { ok = false; break; }
-            dequant32(ringC + sc * kC + off_codes, tcg::scale_of(cur, s_code2, offset), s_lut,
+            dequant32(ringC + sc * kC + off_codes, scale_of(cur, s_code2, offset), s_lut,
                       a_dst, c0, rot, swz);
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&emptyC[sc]);
@@ -348,7 +398,7 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
 
 template <int A0, class Epi>
 int launch_nf4(const CUtensorMap& mCodes, const CUtensorMap& mB0, const CUtensorMap& mB1,
-               const NfProblem& pb, const tcg::Nf4Operand& nf4, const LoraA& lora,
+               const NfProblem& pb, const Nf4Operand& nf4, const LoraA& lora,
                const Epi& epi, cudaStream_t stream, const char* what) {
   auto kernel = tc_nf4_kernel<A0, Epi>;
   static bool configured[64] = {};

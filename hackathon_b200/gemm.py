@@ -39,6 +39,41 @@ def gemm(a, b_t, out=None, out_dtype=torch.bfloat16, bias=None):
     return out
 
 
+def gemm2(a0, b0_t, a1, b1_t, out=None, out_dtype=torch.bfloat16, bias=None):
+    """out[M, N] = a0 @ b0_t.T + a1 @ b1_t.T (+ bias) in one fp32 accumulation: the second term is
+    extra K of the same tcgen05 GEMM (C-ABI qb_gemm2_bf16). a0/a1 row-major; b0_t/b1_t both
+    row-major or both transposed views of row-major tensors."""
+    if a1 is None or a1.shape[-1] == 0:
+        return gemm(a0, b0_t, out=out, out_dtype=out_dtype, bias=bias)
+    _lib.require_cuda(a0, b0_t, a1, b1_t, what="gemm2")
+    for t in (a0, b0_t, a1, b1_t):
+        if t.dtype != torch.bfloat16:
+            raise TypeError("gemm2: bf16 operands only")
+    M, K0 = a0.shape
+    N, K0b = b0_t.shape
+    M1, K1 = a1.shape
+    N1, K1b = b1_t.shape
+    if K0 != K0b or K1 != K1b or M1 != M or N1 != N:
+        raise ValueError(f"gemm2: shapes {tuple(a0.shape)} {tuple(b0_t.shape)} "
+                         f"{tuple(a1.shape)} {tuple(b1_t.shape)} do not match")
+    a0 = a0 if a0.stride(-1) == 1 else a0.contiguous()
+    a1 = a1 if a1.stride(-1) == 1 else a1.contiguous()
+    b0_t, ldb0, b0_mn = _operand(b0_t)
+    b1_t, ldb1, b1_mn = _operand(b1_t)
+    if b0_mn != b1_mn:   # the kernel takes both B operands in one layout
+        b1_t = b1_t.t().contiguous().t() if b0_mn else b1_t.contiguous()
+        b1_t, ldb1, b1_mn = _operand(b1_t)
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a0.device)
+    if bias is not None:
+        bias = bias.float().contiguous()
+    _lib.call("qb_gemm2_bf16", a0.data_ptr(), a0.stride(0), 0, b0_t.data_ptr(), ldb0, int(b0_mn),
+              K0, a1.data_ptr(), a1.stride(0), 0, b1_t.data_ptr(), ldb1, int(b1_mn), K1,
+              out.data_ptr(), out.stride(0), _lib.tag(out.dtype), _lib.ptr(bias), M, N,
+              _lib.stream(a0.device), work=(0, 2 * M * N * (K0 + K1)))
+    return out
+
+
 def device_error():
     """Raises if a tensor-core kernel on this device gave up a bounded wait (synchronises)."""
     _lib.call("qb_device_error", _lib.stream())

@@ -202,16 +202,50 @@ def _rows2d(t):
     return t2 if t2.stride(-1) == 1 else t2.contiguous()
 
 
-def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None):
-    """y = x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T) on the fused tcgen05 kernel: the NF4
-    weight is rebuilt in registers inside the GEMM. x [..., in] bf16 -> y [..., out] bf16."""
+# Token count from which a projection runs as "rebuild W into a transient bf16 copy
+# (qb_nf4_dequant), then the TMA-fed GEMM with the LoRA term as extra K (qb_gemm2_bf16)" instead
+# of the fused kernel. The fused kernel reads 0.5 byte per weight but its thread-written operand
+# caps it near 1 PFLOP/s; the TMA-fed GEMM runs at 1.1-1.4 PFLOP/s and the rebuild costs one
+# streaming pass over the weight (tens of microseconds), so long token counts win by 10-40%.
+DEQUANT_GEMM_MIN_TOKENS = 8192
+
+_WEIGHT_WS = {}
+
+
+def _weight_workspace(device, out_f, in_f):
+    """A bf16 [out_f, in_f] scratch for the transient weight, one per (device, stream): every
+    user of it is ordered on that stream, so one buffer serves all projections in turn."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    buf = _WEIGHT_WS.get(key)
+    if buf is None or buf.numel() < out_f * in_f:
+        buf = torch.empty(out_f * in_f, dtype=torch.bfloat16, device=device)
+        _WEIGHT_WS[key] = buf
+    return buf[:out_f * in_f].view(out_f, in_f)
+
+
+def _use_dequant_gemm(tokens, path):
+    if path not in (None, "fused", "dequant"):
+        raise ValueError(f"unknown path {path!r}")
+    return path == "dequant" or (path is None and tokens >= DEQUANT_GEMM_MIN_TOKENS)
+
+
+def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=None):
+    """y = x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T), bf16 in and out, fp32 accumulation.
+    path "fused": the tcgen05 kernel that rebuilds the NF4 weight in registers inside the GEMM;
+    "dequant": W rebuilt into a transient bf16 copy, then the TMA-fed GEMM; None picks by token
+    count (DEQUANT_GEMM_MIN_TOKENS). x [..., in] -> y [..., out]."""
     out_f, in_f = qs.shape
     x2 = _rows2d(x)
     T = x2.shape[0]
-    y = torch.empty((T, out_f), dtype=torch.bfloat16, device=x.device)
     r = 0 if u is None else u.shape[-1]
     u2 = None if u is None else _rows2d(u)
     lb = None if lora_b_scaled is None else lora_b_scaled.contiguous()
+    if _use_dequant_gemm(T, path):
+        from .gemm import gemm2
+        w = dequantize_nf4(packed, qs, torch.bfloat16, out=_weight_workspace(x.device, out_f, in_f))
+        y = gemm2(x2, w, u2, lb, bias=bias)
+        return y.view(*x.shape[:-1], out_f)
+    y = torch.empty((T, out_f), dtype=torch.bfloat16, device=x.device)
     b = None if bias is None else bias.to(torch.bfloat16).contiguous()
     _lib.call("qb_nf4_linear_fwd", x2.data_ptr(), x2.stride(0), *_nf4_args(packed, qs), T, in_f,
               out_f, _lib.ptr(b), _lib.ptr(u2), u2.stride(0) if u2 is not None else 0,
@@ -220,16 +254,23 @@ def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None):
     return y.view(*x.shape[:-1], out_f)
 
 
-def nf4_linear_dgrad(dy, packed, qs, v=None, lora_a=None):
-    """dx = dy @ deq(W) (+ v @ lora_a) on the fused tcgen05 kernel (W read transposed from the
-    packed codes). dy [..., out] bf16 -> dx [..., in] bf16."""
+def nf4_linear_dgrad(dy, packed, qs, v=None, lora_a=None, path=None):
+    """dx = dy @ deq(W) (+ v @ lora_a), bf16 in and out, fp32 accumulation; `path` as in
+    nf4_linear_fwd (the fused kernel reads W transposed from the packed codes; the dequant path
+    reads the transient copy MN-major). dy [..., out] -> dx [..., in]."""
     out_f, in_f = qs.shape
     d2 = _rows2d(dy)
     T = d2.shape[0]
-    dx = torch.empty((T, in_f), dtype=torch.bfloat16, device=dy.device)
     r = 0 if v is None else v.shape[-1]
     v2 = None if v is None else _rows2d(v)
     la = None if lora_a is None else lora_a.contiguous()
+    if _use_dequant_gemm(T, path):
+        from .gemm import gemm2
+        w = dequantize_nf4(packed, qs, torch.bfloat16,
+                           out=_weight_workspace(dy.device, out_f, in_f))
+        dx = gemm2(d2, w.t(), v2, None if la is None else la.t())
+        return dx.view(*dy.shape[:-1], in_f)
+    dx = torch.empty((T, in_f), dtype=torch.bfloat16, device=dy.device)
     _lib.call("qb_nf4_linear_dgrad", d2.data_ptr(), d2.stride(0), *_nf4_args(packed, qs), T,
               in_f, out_f, _lib.ptr(v2), v2.stride(0) if v2 is not None else 0, _lib.ptr(la),
               la.stride(0) if la is not None else 0, r, dx.data_ptr(), dx.stride(0),

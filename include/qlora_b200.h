@@ -196,6 +196,20 @@ int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const void* B, int6
                  int b_mn_major, void* C, int64_t ldc, int c_dtype, const float* bias, int64_t M,
                  int64_t N, int64_t K, cudaStream_t stream);
 
+/* C[M, N] = A0[M, K0] * B0[N, K0]^T + A1[M, K1] * B1[N, K1]^T (+ bias[N] fp32), fp32
+ * accumulation in one pass (segment 1 is extra K of the same accumulator); C fp32 or bf16.
+ * K1 == 0 is qb_gemm_bf16. With K1 > 0 the A operands are K-major and the B operands are both
+ * K-major or both MN-major (QB_ERR_UNSUPPORTED otherwise). This is the long-token path of a
+ * 4-bit projection with its LoRA term on a transient bf16 copy of the weight (qb_nf4_dequant
+ * writes it): forward y = [x | u] [W | s*B_lora]^T + bias, input gradient
+ * dx = [dy | v] [W^T | A_lora^T]^T. Replaces solution/nf4.py:100-112 (F.linear / grad_out @ W
+ * on the dequantised weight) and the lora_B(...) + ScaledAdd of solution/lora.py:172-173. */
+int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0, int64_t ldb0,
+                  int b0_mn_major, int64_t K0, const void* A1, int64_t lda1, int a1_mn_major,
+                  const void* B1, int64_t ldb1, int b1_mn_major, int64_t K1, void* C,
+                  int64_t ldc, int c_dtype, const float* bias, int64_t M, int64_t N,
+                  cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * NF4 x LoRA projection on tcgen05, the NF4 weight rebuilt in registers inside the GEMM
  *

@@ -74,3 +74,61 @@ def test_gemm_rejects_misaligned_rows(cuda):
     b = torch.randn(64, 67, device=cuda).to(torch.bfloat16)
     with pytest.raises(RuntimeError, match="16"):
         gemm(a, b)
+
+
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("shape", [(384, 512, 320, 64), (129, 257, 200, 16), (1, 300, 64, 8),
+                                   (1000, 136, 2048, 100)])
+def test_gemm2_two_segments(cuda, shape, b_t):
+    """C = A0 B0^T + A1 B1^T in one accumulation (qb_gemm2_bf16): both B layouts, ragged M/N and
+    segment lengths that are not multiples of the 64-wide k-block."""
+    from hackathon_b200.gemm import device_error, gemm2
+    M, N, K0, K1 = shape
+    g = torch.Generator(device=cuda).manual_seed(4)
+
+    def pad(n):   # leading dims padded to 16-byte rows, views cut to the shape
+        return (n + 7) // 8 * 8
+
+    def b_op(k):
+        if b_t:   # transposed view of a row-major [k, N]: read MN-major
+            return torch.randn(k, pad(N), device=cuda, generator=g).to(torch.bfloat16)[:, :N].t()
+        return torch.randn(N, pad(k), device=cuda, generator=g).to(torch.bfloat16)[:, :k]
+
+    a0 = torch.randn(M, pad(K0), device=cuda, generator=g).to(torch.bfloat16)[:, :K0]
+    a1 = torch.randn(M, pad(K1), device=cuda, generator=g).to(torch.bfloat16)[:, :K1]
+    b0, b1 = b_op(K0), b_op(K1)
+    bias = torch.randn(N, device=cuda, generator=g)
+    for out_dtype in (torch.float32, torch.bfloat16):
+        out = gemm2(a0, b0, a1, b1, out_dtype=out_dtype, bias=bias)
+        device_error()
+        _check(out, _ref(a0, b0, bias) + a1.float() @ b1.float().t(), out_dtype)
+
+
+def test_gemm2_mixed_b_layouts(cuda):
+    """A row-major B1 next to a transposed-view B0 is brought to one layout on the host."""
+    from hackathon_b200.gemm import device_error, gemm2
+    g = torch.Generator(device=cuda).manual_seed(5)
+    a0 = torch.randn(256, 128, device=cuda, generator=g).to(torch.bfloat16)
+    b0 = torch.randn(128, 384, device=cuda, generator=g).to(torch.bfloat16).t()
+    a1 = torch.randn(256, 64, device=cuda, generator=g).to(torch.bfloat16)
+    b1 = torch.randn(384, 64, device=cuda, generator=g).to(torch.bfloat16)
+    out = gemm2(a0, b0, a1, b1, out_dtype=torch.float32)
+    device_error()
+    _check(out, _ref(a0, b0) + _ref(a1, b1), torch.float32)
+
+
+@pytest.mark.parametrize("shape", [(16384, 3584, 3584), (16384, 512, 3584)])
+def test_gemm2_projection_step_shape(cuda, shape):
+    """A 7B projection with its rank-64 LoRA term at the step's token count, sampled rows."""
+    from hackathon_b200.gemm import device_error, gemm2
+    M, N, K = shape
+    g = torch.Generator(device=cuda).manual_seed(6)
+    x = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).to(torch.bfloat16)
+    u = torch.randn(M, 64, device=cuda, generator=g).to(torch.bfloat16)
+    sb = (torch.randn(N, 64, device=cuda, generator=g) * 0.05).to(torch.bfloat16)
+    out = gemm2(x, w, u, sb)
+    device_error()
+    rows = torch.tensor([0, 1, 127, 128, 2047, 2048, M // 2, M - 1], device=cuda)
+    ref = x[rows].float() @ w.float().t() + u[rows].float() @ sb.float().t()
+    torch.testing.assert_close(out[rows].float(), ref, rtol=1.6e-2, atol=2e-2)

@@ -45,6 +45,14 @@ def test_error_message_plumbing_without_gpu():
     assert rc == 1 and b"bad shape" in lib.qb_last_error()
     with pytest.raises(RuntimeError, match="qb_swiglu_fwd failed"):
         _lib.call("qb_swiglu_fwd", None, None, None, 2, -1, None)
+    # two-segment GEMM: layouts other than the projection's two are refused before any launch
+    fake = 1 << 20
+    with pytest.raises(RuntimeError, match="K-major"):
+        _lib.call("qb_gemm2_bf16", fake, 64, 1, fake, 64, 0, 64, fake, 64, 0, fake, 64, 0, 64,
+                  fake, 64, 2, None, 128, 128, None)
+    with pytest.raises(RuntimeError, match="bad K"):
+        _lib.call("qb_gemm2_bf16", fake, 64, 0, fake, 64, 0, 0, fake, 64, 0, fake, 64, 0, 64,
+                  fake, 64, 2, None, 128, 128, None)
 
 
 @pytest.mark.parametrize("op", ["rmsnorm", "rope", "swiglu", "dropout", "dequant"])
