@@ -56,18 +56,19 @@ int map_operand(CUtensorMap* map, const void* p, int64_t ld, bool mn_major, int6
                             CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int A0, int B0, int A1, int B1, typename OutT>
+template <int A0, int B0, int A1, int B1, int BN, typename OutT>
 int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
         const float* bias, bool vec, cudaStream_t s, const char* what) {
   EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias, vec};
-  return tcg::launch<A0, B0, A1, B1, kBN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
+  return tcg::launch<A0, B0, A1, B1, BN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
 }
 
 template <int A0, int B0, int A1, int B1>
 int run_dtype(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
               int c_dtype, const float* bias, bool vec, cudaStream_t s, const char* what) {
-  if (c_dtype == QB_F32) return run<A0, B0, A1, B1, float>(m, pb, c, ldc, bias, vec, s, what);
-  return run<A0, B0, A1, B1, __nv_bfloat16>(m, pb, c, ldc, bias, vec, s, what);
+  if (c_dtype == QB_F32)
+    return run<A0, B0, A1, B1, kBN, float>(m, pb, c, ldc, bias, vec, s, what);
+  return run<A0, B0, A1, B1, kBN, __nv_bfloat16>(m, pb, c, ldc, bias, vec, s, what);
 }
 
 int check_common(const void* C, int c_dtype, int64_t M, int64_t N, const char* what) {
@@ -109,13 +110,13 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const vo
   const tcg::Problem pb = problem(M, N, K, 0);
   const bool vec = vec_ok(C, ldc, c_dtype);
   using namespace tcg;
-  if (!a_mn_major && !b_mn_major)
-    return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
-  if (!a_mn_major && b_mn_major)
-    return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
-  if (a_mn_major && !b_mn_major)
-    return run_dtype<kTmaMN, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
-  return run_dtype<kTmaMN, kTmaMN, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+#define QB_RUN(A0, B0) \
+  return run_dtype<A0, B0, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what)
+  if (!a_mn_major && !b_mn_major) QB_RUN(kTmaK, kTmaK);
+  if (!a_mn_major && b_mn_major) QB_RUN(kTmaK, kTmaMN);
+  if (a_mn_major && !b_mn_major) QB_RUN(kTmaMN, kTmaK);
+  QB_RUN(kTmaMN, kTmaMN);
+#undef QB_RUN
 }
 
 extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,

@@ -48,11 +48,15 @@ __device__ __forceinline__ void tile_blocks(const Problem& pb, int tile, int& mb
 
 template <int BN>
 struct Cfg {
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128, whole TMEM chunks");
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES_K = BN * 128;                // K-major B: BN rows of 128 bytes
+  static constexpr int B_BYTES_MN = ((BN + 63) / 64) * 8192; // MN-major B: whole 64-wide boxes
+  static constexpr int B_BYTES = B_BYTES_MN > B_BYTES_K ? B_BYTES_MN : B_BYTES_K;  // stage slot
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = 196 * 1024 / STAGE;
   static constexpr int TMEM_COLS = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  static constexpr int BUF_COLS = TMEM_COLS / 2;   // accumulator b starts at column b * BUF_COLS
   static constexpr int EXTRA = 1024 /*align*/ + 512 /*barriers*/;
   static constexpr int SMEM = STAGES * STAGE + EXTRA;
 };
@@ -131,7 +135,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
           const int asrc = seg1 ? A1 : A0, bsrc = seg1 ? B1 : B0;
           const CUtensorMap* ma = seg1 ? &mA1 : &mA0;
           const CUtensorMap* mb_ = seg1 ? &mB1 : &mB0;
-          tc::mbar_expect_tx(&full[stage], C::A_BYTES + C::B_BYTES);
+          tc::mbar_expect_tx(&full[stage], C::A_BYTES + (bsrc == kTmaK ? C::B_BYTES_K : C::B_BYTES_MN));
           if (asrc == kTmaK) {
             tc::tma_load_2d(sA, ma, &full[stage], k * BK, m0);
           } else {
@@ -141,8 +145,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
           if (bsrc == kTmaK) {
             tc::tma_load_2d(sB, mb_, &full[stage], k * BK, n0);
           } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
+#pragma unroll   // a partial last box (BN = 224) brings columns the MMA does not read
+            for (int j = 0; j < (BN + 63) / 64; ++j)
               tc::tma_load_2d(sB + j * 8192, mb_, &full[stage], n0 + j * 64, k * BK);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -166,7 +170,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
         const int buf = t & 1;
         if (!tc::mbar_wait(&tempty[buf], ((t >> 1) & 1) ^ 1, err, 2)) break;
         tc::fence_after_sync();
-        const uint32_t d = tmem_base + buf * BN;
+        const uint32_t d = tmem_base + buf * C::BUF_COLS;
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           const bool seg1 = kb >= pb.nk0;
@@ -207,7 +211,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       tc::fence_after_sync();
       int mb, nb;
       tile_blocks(pb, tile, mb, nb);
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::BUF_COLS;
       epi.template tile<BN>(mb * BM, nb * BN, row, taddr);
       tc::fence_before_sync();
       tc::mbar_arrive(&tempty[buf]);

@@ -132,3 +132,28 @@ def test_gemm2_projection_step_shape(cuda, shape):
     rows = torch.tensor([0, 1, 127, 128, 2047, 2048, M // 2, M - 1], device=cuda)
     ref = x[rows].float() @ w.float().t() + u[rows].float() @ sb.float().t()
     torch.testing.assert_close(out[rows].float(), ref, rtol=1.6e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("shape", [(2048, 1000, 200), (2560, 1330, 96), (4096, 1800, 136)])
+def test_gemm_ragged_bf16_both_b_layouts(cuda, shape, b_t):
+    """Multi-wave shapes with a ragged last tile in N and K, for both B layouts, single- and
+    two-segment, bf16 output."""
+    from hackathon_b200.gemm import device_error, gemm, gemm2
+    M, N, K = shape
+    g = torch.Generator(device=cuda).manual_seed(7)
+    a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    if b_t:
+        b = torch.randn(K, (N + 7) // 8 * 8, device=cuda, generator=g).to(torch.bfloat16)[:, :N].t()
+    else:
+        b = torch.randn(N, K, device=cuda, generator=g).to(torch.bfloat16)
+    out = gemm(a, b)
+    u = torch.randn(M, 64, device=cuda, generator=g).to(torch.bfloat16)
+    if b_t:
+        v = torch.randn(64, (N + 7) // 8 * 8, device=cuda, generator=g).to(torch.bfloat16)[:, :N].t()
+    else:
+        v = torch.randn(N, 64, device=cuda, generator=g).to(torch.bfloat16)
+    out2 = gemm2(a, b, u, v)
+    device_error()
+    _check(out, _ref(a, b), torch.bfloat16)
+    _check(out2, _ref(a, b) + _ref(u, v), torch.bfloat16)
