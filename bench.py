@@ -39,6 +39,11 @@ WORKLOADS = {
     "1.5b": ("configs[3]: Qwen2.5-1.5B-shaped QLoRA step, 4 x 2048 tokens per GPU", 4, 2048),
     "0.5b": ("configs[0] shapes: Qwen2.5-0.5B-shaped QLoRA step, 2 x 256 tokens per GPU", 2, 256),
 }
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernel,
+# from ncu captures of each of its launch shapes in the step, averaged over the step's launch mix
+# (profiles/tc_gemm_kernel_dram_traffic_7b_projections.md). Keyed by --config.
+TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1031.9e6}}
+
 # per-kernel roofline class: "hbm" (bytes) or "tensor" (flops)
 BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hbm",
          "qb_rope_qk": "hbm", "qb_swiglu_fwd": "hbm", "qb_swiglu_bwd": "hbm",
@@ -267,6 +272,8 @@ def main():
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--cpu-tokens", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="print every kernel of one step with its device time (torch.profiler)")
     ap.add_argument("--kernel", default=None, choices=KERNELS,
                     help="time one op of the step alone at a projection shape")
     ap.add_argument("--tokens", type=int, default=16384)
@@ -318,6 +325,26 @@ def main():
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+
+    if args.profile_step:
+        # every kernel of one step (ours, cuDNN, cuBLAS, torch) with its device time, from
+        # CUPTI via torch.profiler: launches run unserialised, as in the timed region
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step(0)
+            torch.cuda.synchronize()
+        rows = [(e.key, e.count, e.device_time_total / 1e3) for e in prof.key_averages()
+                if e.device_time_total > 0 and not e.key.startswith("cuda")]
+        total = sum(r[2] for r in rows)
+        rows.sort(key=lambda r: -r[2])
+        if rank == 0:
+            print(json.dumps({"profile_step": workload, "device_ms": round(total, 2),
+                              "launches": sum(r[1] for r in rows),
+                              "kernels": [{"name": k[:160], "launches": c, "ms": round(ms, 3),
+                                           "share": round(ms / total, 4)} for k, c, ms in rows]}))
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     # ---- timed region: K steps, inputs resident in HBM (working set >> 126 MB L2)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -379,7 +406,8 @@ def main():
             achieved = per / (avg_ms * 1e-3) / 1e9
             roofline = {"kernel": dom_name, "bound": "hbm", "achieved": round(achieved, 1),
                         "peak": pk["hbm_gbs"], "unit": "GB/s",
-                        "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None,
+                        "frac": round(achieved / pk["hbm_gbs"], 3),
+                        "traffic": TRAFFIC_PER_LAUNCH.get(args.config, {}).get(dom_name),
                         "algorithmic_bytes_per_launch": int(per),
                         "peak_source": pk["source"]}
         else:
@@ -388,7 +416,8 @@ def main():
             roofline = {"kernel": dom_name, "bound": "tensor", "achieved": round(achieved, 1),
                         "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                         "frac": round(achieved / pk["bf16_tflops_sustained"], 3),
-                        "traffic": None, "algorithmic_flops_per_launch": int(per),
+                        "traffic": TRAFFIC_PER_LAUNCH.get(args.config, {}).get(dom_name),
+                        "algorithmic_flops_per_launch": int(per),
                         "peak_source": pk["source"] + " (sustained)"}
 
     cpu = None
