@@ -176,13 +176,17 @@ def run_reference(args, rank, world):
 
 
 KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
-           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd")
+           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce")
+GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd")
 
 
 def kernel_case(args):
     """One op of the step on its own at a projection shape (--tokens x --in-features ->
     --out-features), timed with CUDA events over --steps launches after --warmup: the command the
-    ncu summaries cite. Inputs are larger than L2 at the default 16384 tokens."""
+    ncu summaries cite. Inputs are larger than L2 at the default 16384 tokens. `linear_ce` is the
+    fused linear cross-entropy (forward + dH) with hidden size --in-features and vocabulary
+    --out-features. --graph replays the --steps launches from one CUDA graph (bandwidth kernels
+    too short to time behind Python launch gaps)."""
     from hackathon_b200 import nf4 as nf4m
     from hackathon_b200.gemm import device_error, gemm, gemm2
     from hackathon_b200.lora import dropout_apply, dropout_mask
@@ -232,6 +236,14 @@ def kernel_case(args):
         gate, up = rnd(T, fo), rnd(T, fo)
         fn = lambda: swiglu(gate, up)  # noqa: E731
         nbytes = 3 * T * fo * 2
+    elif name == "linear_ce":
+        from hackathon_b200.cross_entropy import fused_causal_lm_loss
+        h = rnd(T, fi).requires_grad_()
+        wv = rnd(fo, fi, s=0.02)
+        labels = torch.randint(0, fo, (1, T), device=dev, generator=g)
+        labels[torch.rand((1, T), device=dev, generator=g) < 0.1] = -100
+        fn = lambda: fused_causal_lm_loss(h.view(1, T, fi), wv, labels)  # noqa: E731
+        flops = 4 * T * fi * fo        # algorithmic: logits + dH (executed: 6 N H V)
     else:
         x, wn = rnd(T, fi), rnd(fi)
         fn = lambda: rmsnorm(x, wn, 1e-6)  # noqa: E731
@@ -239,16 +251,31 @@ def kernel_case(args):
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
+    run = fn
+    if args.graph:
+        if name not in GRAPHABLE:
+            raise SystemExit(f"--graph: {name} builds tensor maps on the host per call")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                fn()
+        run = graph.replay
+        run()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        fn()
+    if args.graph:
+        run()
+    else:
+        for _ in range(args.steps):
+            run()
     e1.record()
     torch.cuda.synchronize()
     device_error()
     ms = e0.elapsed_time(e1) / args.steps
     pk = peaks()
-    line = {"kernel": name, "tokens": T, "in_features": fi, "out_features": fo, "ms": round(ms, 4)}
+    line = {"kernel": name, "tokens": T, "in_features": fi, "out_features": fo, "ms": round(ms, 4),
+            "graph": bool(args.graph)}
     if flops:
         tf = flops / (ms * 1e-3) / 1e12
         line.update(achieved=round(tf, 1), unit="TFLOP/s", peak=pk["bf16_tflops"],
@@ -276,6 +303,8 @@ def main():
                     help="print every kernel of one step with its device time (torch.profiler)")
     ap.add_argument("--kernel", default=None, choices=KERNELS,
                     help="time one op of the step alone at a projection shape")
+    ap.add_argument("--graph", action="store_true",
+                    help="with --kernel: replay the timed launches from one CUDA graph")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--in-features", type=int, default=3584)
     ap.add_argument("--out-features", type=int, default=3584)
