@@ -176,7 +176,7 @@ def run_reference(args, rank, world):
 
 
 KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
-           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce")
+           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce", "mask_acc")
 GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd")
 
 
@@ -236,6 +236,13 @@ def kernel_case(args):
         gate, up = rnd(T, fo), rnd(T, fo)
         fn = lambda: swiglu(gate, up)  # noqa: E731
         nbytes = 3 * T * fo * 2
+    elif name == "mask_acc":
+        # the backward LoRA input-gradient term: dx[T, in] += s * mask .* (V[T, r] A[r, in])
+        from hackathon_b200.gemm import gemm_mask_acc
+        v, a_l, dx = rnd(T, r), rnd(r, fi, s=0.05), rnd(T, fi)
+        _, bits = dropout_mask(dx, 0.05, 7, 1 / 0.95)
+        fn = lambda: gemm_mask_acc(v, a_l.t(), bits, 1 / 0.95, dx)  # noqa: E731
+        nbytes = 2 * T * fi * 2 + bits.numel() * 4 + T * r * 2 + r * fi * 2
     elif name == "linear_ce":
         from hackathon_b200.cross_entropy import fused_causal_lm_loss
         h = rnd(T, fi).requires_grad_()

@@ -11,14 +11,17 @@ namespace {
 constexpr int kBN = 256;
 
 // Row-major store: each epilogue thread owns one output row of the tile and writes its 32
-// consecutive columns per TMEM chunk with 16-byte stores.
+// consecutive columns per TMEM chunk with 16-byte stores; optionally adds a bias row and a
+// residual matrix of the output's type first (one rounding of acc + bias + residual).
 template <typename OutT>
 struct EpiStoreRow {
   OutT* c;
   int64_t ldc;
   int M, N;
   const float* bias;  // [N] or null
-  bool vec;           // 16-byte aligned rows
+  const OutT* resid;  // [M, N] (row stride ldr) or null
+  int64_t ldr;
+  bool vec;           // 16-byte aligned rows (output and residual)
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -34,13 +37,23 @@ struct EpiStoreRow {
         for (int i = 0; i < 32; ++i) v[i] += (n + i < N) ? __ldg(bias + n + i) : 0.f;
       }
       OutT* dst = c + static_cast<int64_t>(m) * ldc + n;
+      const OutT* res = resid ? resid + static_cast<int64_t>(m) * ldr + n : nullptr;
       if (vec && n + 32 <= N) {
+        if (res) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float r[8];
+            qb::load8(res + i, r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i + j] += r[j];
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 32; i += 8) qb::store8<OutT>(dst + i, v + i);
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (n + i < N) dst[i] = qb::from_f<OutT>(v[i]);
+          if (n + i < N) dst[i] = qb::from_f<OutT>(v[i] + (res ? qb::to_f(res[i]) : 0.f));
       }
     }
   }
@@ -58,17 +71,20 @@ int map_operand(CUtensorMap* map, const void* p, int64_t ld, bool mn_major, int6
 
 template <int A0, int B0, int A1, int B1, int BN, typename OutT>
 int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
-        const float* bias, bool vec, cudaStream_t s, const char* what) {
-  EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias, vec};
+        const float* bias, const void* resid, int64_t ldr, bool vec, cudaStream_t s,
+        const char* what) {
+  EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias,
+                        static_cast<const OutT*>(resid), ldr, vec};
   return tcg::launch<A0, B0, A1, B1, BN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
 }
 
 template <int A0, int B0, int A1, int B1>
 int run_dtype(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
-              int c_dtype, const float* bias, bool vec, cudaStream_t s, const char* what) {
+              int c_dtype, const float* bias, const void* resid, int64_t ldr, bool vec,
+              cudaStream_t s, const char* what) {
   if (c_dtype == QB_F32)
-    return run<A0, B0, A1, B1, kBN, float>(m, pb, c, ldc, bias, vec, s, what);
-  return run<A0, B0, A1, B1, kBN, __nv_bfloat16>(m, pb, c, ldc, bias, vec, s, what);
+    return run<A0, B0, A1, B1, kBN, float>(m, pb, c, ldc, bias, resid, ldr, vec, s, what);
+  return run<A0, B0, A1, B1, kBN, __nv_bfloat16>(m, pb, c, ldc, bias, resid, ldr, vec, s, what);
 }
 
 int check_common(const void* C, int c_dtype, int64_t M, int64_t N, const char* what) {
@@ -111,7 +127,8 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const vo
   const bool vec = vec_ok(C, ldc, c_dtype);
   using namespace tcg;
 #define QB_RUN(A0, B0) \
-  return run_dtype<A0, B0, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what)
+  return run_dtype<A0, B0, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec, stream, \
+                                         what)
   if (!a_mn_major && !b_mn_major) QB_RUN(kTmaK, kTmaK);
   if (!a_mn_major && b_mn_major) QB_RUN(kTmaK, kTmaMN);
   if (a_mn_major && !b_mn_major) QB_RUN(kTmaMN, kTmaK);
@@ -123,16 +140,24 @@ extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, cons
                              int64_t ldb0, int b0_mn_major, int64_t K0, const void* A1,
                              int64_t lda1, int a1_mn_major, const void* B1, int64_t ldb1,
                              int b1_mn_major, int64_t K1, void* C, int64_t ldc, int c_dtype,
-                             const float* bias, int64_t M, int64_t N, cudaStream_t stream) {
+                             const float* bias, const void* residual, int64_t ldr, int64_t M,
+                             int64_t N, cudaStream_t stream) {
   const char* what = "gemm2_bf16";
-  if (K1 == 0)
+  if (K1 == 0 && !residual)
     return qb_gemm_bf16(A0, lda0, a0_mn_major, B0, ldb0, b0_mn_major, C, ldc, c_dtype, bias, M,
                         N, K0, stream);
   if (int s = check_common(C, c_dtype, M, N, what)) return s;
   if (K0 <= 0 || K1 < 0 || K0 > (1 << 30) || K1 > (1 << 30))
     return qb::fail(QB_ERR_INVALID, "%s: bad K", what);
   if (M == 0 || N == 0) return QB_OK;
-  if (!A0 || !B0 || !A1 || !B1) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  if (!A0 || !B0 || (K1 > 0 && (!A1 || !B1)))
+    return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  if (residual && ldr < N) return qb::fail(QB_ERR_INVALID, "%s: residual row stride", what);
+  if (K1 == 0) {   // one segment with a residual
+    A1 = A0; B1 = B0; lda1 = lda0; ldb1 = ldb0; K1 = K0;
+    a1_mn_major = a0_mn_major; b1_mn_major = b0_mn_major;
+  }
+  const bool one = A1 == A0 && B1 == B0 && K1 == K0;
   // the two layouts a projection with its adapter term takes (forward / input gradient)
   const bool fwd = !a0_mn_major && !b0_mn_major && !a1_mn_major && !b1_mn_major;
   const bool bwd = !a0_mn_major && b0_mn_major && !a1_mn_major && b1_mn_major;
@@ -144,10 +169,14 @@ extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, cons
   if (int s = map_operand(&m[1], B0, ldb0, bwd, N, K0, kBN)) return s;
   if (int s = map_operand(&m[2], A1, lda1, false, M, K1, tcg::BM)) return s;
   if (int s = map_operand(&m[3], B1, ldb1, bwd, N, K1, kBN)) return s;
-  const tcg::Problem pb = problem(M, N, K0, K1);
-  const bool vec = vec_ok(C, ldc, c_dtype);
+  const tcg::Problem pb = problem(M, N, K0, one ? 0 : K1);
+  const int es = c_dtype == QB_F32 ? 4 : 2;
+  const bool vec = vec_ok(C, ldc, c_dtype) &&
+                   (!residual || (qb::aligned16(residual) && (ldr * es) % 16 == 0));
   using namespace tcg;
   if (fwd)
-    return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
-  return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, vec, stream, what);
+    return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, residual, ldr,
+                                                 vec, stream, what);
+  return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, residual, ldr,
+                                                 vec, stream, what);
 }

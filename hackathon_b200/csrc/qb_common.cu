@@ -28,4 +28,4 @@ int check_launch(const char* what) {
 
 extern "C" const char* qb_last_error(void) { return g_last_error; }
 
-extern "C" int qb_abi_version(void) { return 1; }
+extern "C" int qb_abi_version(void) { return 2; }

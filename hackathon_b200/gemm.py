@@ -39,38 +39,69 @@ def gemm(a, b_t, out=None, out_dtype=torch.bfloat16, bias=None):
     return out
 
 
-def gemm2(a0, b0_t, a1, b1_t, out=None, out_dtype=torch.bfloat16, bias=None):
-    """out[M, N] = a0 @ b0_t.T + a1 @ b1_t.T (+ bias) in one fp32 accumulation: the second term is
-    extra K of the same tcgen05 GEMM (C-ABI qb_gemm2_bf16). a0/a1 row-major; b0_t/b1_t both
-    row-major or both transposed views of row-major tensors."""
-    if a1 is None or a1.shape[-1] == 0:
+def gemm2(a0, b0_t, a1, b1_t, out=None, out_dtype=torch.bfloat16, bias=None, residual=None):
+    """out[M, N] = residual + a0 @ b0_t.T + a1 @ b1_t.T (+ bias) in one fp32 accumulation and one
+    rounding: the second term is extra K of the same tcgen05 GEMM (C-ABI qb_gemm2_bf16). a0/a1
+    row-major; b0_t/b1_t both row-major or both transposed views of row-major tensors; a1 may be
+    None; residual [M, N] in out_dtype with unit column stride."""
+    if (a1 is None or a1.shape[-1] == 0) and residual is None:
         return gemm(a0, b0_t, out=out, out_dtype=out_dtype, bias=bias)
-    _lib.require_cuda(a0, b0_t, a1, b1_t, what="gemm2")
-    for t in (a0, b0_t, a1, b1_t):
+    tensors = (a0, b0_t) if a1 is None else (a0, b0_t, a1, b1_t)
+    _lib.require_cuda(*tensors, what="gemm2")
+    for t in tensors:
         if t.dtype != torch.bfloat16:
             raise TypeError("gemm2: bf16 operands only")
     M, K0 = a0.shape
     N, K0b = b0_t.shape
-    M1, K1 = a1.shape
-    N1, K1b = b1_t.shape
-    if K0 != K0b or K1 != K1b or M1 != M or N1 != N:
-        raise ValueError(f"gemm2: shapes {tuple(a0.shape)} {tuple(b0_t.shape)} "
-                         f"{tuple(a1.shape)} {tuple(b1_t.shape)} do not match")
+    if K0 != K0b:
+        raise ValueError(f"gemm2: shapes {tuple(a0.shape)} {tuple(b0_t.shape)} do not match")
     a0 = a0 if a0.stride(-1) == 1 else a0.contiguous()
-    a1 = a1 if a1.stride(-1) == 1 else a1.contiguous()
     b0_t, ldb0, b0_mn = _operand(b0_t)
-    b1_t, ldb1, b1_mn = _operand(b1_t)
-    if b0_mn != b1_mn:   # the kernel takes both B operands in one layout
-        b1_t = b1_t.t().contiguous().t() if b0_mn else b1_t.contiguous()
+    K1, a1p, lda1, b1p, ldb1 = 0, None, 0, None, 0
+    if a1 is not None and a1.shape[-1] > 0:
+        M1, K1 = a1.shape
+        N1, K1b = b1_t.shape
+        if K1 != K1b or M1 != M or N1 != N:
+            raise ValueError(f"gemm2: shapes {tuple(a1.shape)} {tuple(b1_t.shape)} do not match "
+                             f"[{M}, {N}]")
+        a1 = a1 if a1.stride(-1) == 1 else a1.contiguous()
         b1_t, ldb1, b1_mn = _operand(b1_t)
+        if b0_mn != b1_mn:   # the kernel takes both B operands in one layout
+            b1_t = b1_t.t().contiguous().t() if b0_mn else b1_t.contiguous()
+            b1_t, ldb1, b1_mn = _operand(b1_t)
+        a1p, lda1, b1p = a1.data_ptr(), a1.stride(0), b1_t.data_ptr()
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a0.device)
     if bias is not None:
         bias = bias.float().contiguous()
+    ldr = 0
+    if residual is not None:
+        if residual.shape != (M, N) or residual.dtype != out.dtype or residual.stride(-1) != 1:
+            raise ValueError("gemm2: residual must be [M, N] in the output dtype, unit stride")
+        ldr = residual.stride(0)
     _lib.call("qb_gemm2_bf16", a0.data_ptr(), a0.stride(0), 0, b0_t.data_ptr(), ldb0, int(b0_mn),
-              K0, a1.data_ptr(), a1.stride(0), 0, b1_t.data_ptr(), ldb1, int(b1_mn), K1,
-              out.data_ptr(), out.stride(0), _lib.tag(out.dtype), _lib.ptr(bias), M, N,
+              K0, a1p, lda1, 0, b1p, ldb1, int(b0_mn), K1, out.data_ptr(), out.stride(0),
+              _lib.tag(out.dtype), _lib.ptr(bias), _lib.ptr(residual), ldr, M, N,
               _lib.stream(a0.device), work=(0, 2 * M * N * (K0 + K1)))
+    return out
+
+
+def gemm_mask_acc(a, b_t, bits, scale, out):
+    """out[M, N] (bf16, in place) += scale * mask .* (a @ b_t.T), mask from the dropout bit words
+    `bits` [M, ceil(N/32)] int32 (C-ABI qb_gemm_bf16_mask_acc). a row-major [M, K]; b_t row-major
+    [N, K] or the transposed view of a row-major [K, N]."""
+    _lib.require_cuda(a, b_t, bits, out, what="gemm_mask_acc")
+    if a.dtype != torch.bfloat16 or b_t.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise TypeError("gemm_mask_acc: bf16 operands and output only")
+    M, K = a.shape
+    N, K2 = b_t.shape
+    if K != K2 or out.shape != (M, N) or bits.shape[0] != M or bits.shape[1] * 32 < N:
+        raise ValueError("gemm_mask_acc: shapes do not match")
+    a = a if a.stride(-1) == 1 else a.contiguous()
+    b_t, ldb, b_mn = _operand(b_t)
+    _lib.call("qb_gemm_bf16_mask_acc", a.data_ptr(), a.stride(0), b_t.data_ptr(), ldb, int(b_mn),
+              bits.data_ptr(), bits.stride(0), float(scale), out.data_ptr(), out.stride(0), M, N,
+              K, _lib.stream(a.device), work=(0, 2 * M * N * K))
     return out
 
 

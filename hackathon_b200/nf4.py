@@ -223,27 +223,34 @@ def _weight_workspace(device, out_f, in_f):
     return buf[:out_f * in_f].view(out_f, in_f)
 
 
-def _use_dequant_gemm(tokens, path):
+def uses_dequant_path(tokens, path=None):
+    """True when a projection over `tokens` rows runs as transient bf16 weight + TMA-fed GEMM."""
     if path not in (None, "fused", "dequant"):
         raise ValueError(f"unknown path {path!r}")
     return path == "dequant" or (path is None and tokens >= DEQUANT_GEMM_MIN_TOKENS)
 
 
-def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=None):
-    """y = x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T), bf16 in and out, fp32 accumulation.
-    path "fused": the tcgen05 kernel that rebuilds the NF4 weight in registers inside the GEMM;
-    "dequant": W rebuilt into a transient bf16 copy, then the TMA-fed GEMM; None picks by token
-    count (DEQUANT_GEMM_MIN_TOKENS). x [..., in] -> y [..., out]."""
+def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=None,
+                   residual=None, weight_out=None):
+    """y = residual + x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T), bf16 in and out, fp32
+    accumulation. path "fused": the tcgen05 kernel that rebuilds the NF4 weight in registers inside
+    the GEMM; "dequant": W rebuilt into a transient bf16 copy, then the TMA-fed GEMM (bias, LoRA
+    term and residual in its one accumulation / epilogue); None picks by token count
+    (DEQUANT_GEMM_MIN_TOKENS). On the dequant path the copy goes to `weight_out` (bf16
+    [out, in]) when given — a caller keeps it for the backward — else to a shared scratch.
+    x [..., in] -> y [..., out]."""
     out_f, in_f = qs.shape
     x2 = _rows2d(x)
     T = x2.shape[0]
     r = 0 if u is None else u.shape[-1]
     u2 = None if u is None else _rows2d(u)
     lb = None if lora_b_scaled is None else lora_b_scaled.contiguous()
-    if _use_dequant_gemm(T, path):
+    res2 = None if residual is None else _rows2d(residual)
+    if uses_dequant_path(T, path):
         from .gemm import gemm2
-        w = dequantize_nf4(packed, qs, torch.bfloat16, out=_weight_workspace(x.device, out_f, in_f))
-        y = gemm2(x2, w, u2, lb, bias=bias)
+        w = weight_out if weight_out is not None else _weight_workspace(x.device, out_f, in_f)
+        dequantize_nf4(packed, qs, torch.bfloat16, out=w)
+        y = gemm2(x2, w, u2, lb, bias=bias, residual=res2)
         return y.view(*x.shape[:-1], out_f)
     y = torch.empty((T, out_f), dtype=torch.bfloat16, device=x.device)
     b = None if bias is None else bias.to(torch.bfloat16).contiguous()
@@ -251,23 +258,28 @@ def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=No
               out_f, _lib.ptr(b), _lib.ptr(u2), u2.stride(0) if u2 is not None else 0,
               _lib.ptr(lb), lb.stride(0) if lb is not None else 0, r, y.data_ptr(), y.stride(0),
               _lib.stream(x.device), work=(0, 2 * T * out_f * (in_f + r)))
+    if res2 is not None:
+        y += res2
     return y.view(*x.shape[:-1], out_f)
 
 
-def nf4_linear_dgrad(dy, packed, qs, v=None, lora_a=None, path=None):
+def nf4_linear_dgrad(dy, packed, qs, v=None, lora_a=None, path=None, weight=None):
     """dx = dy @ deq(W) (+ v @ lora_a), bf16 in and out, fp32 accumulation; `path` as in
     nf4_linear_fwd (the fused kernel reads W transposed from the packed codes; the dequant path
-    reads the transient copy MN-major). dy [..., out] -> dx [..., in]."""
+    reads the transient copy MN-major). `weight`: the bf16 copy a forward kept (skips the
+    rebuild). dy [..., out] -> dx [..., in]."""
     out_f, in_f = qs.shape
     d2 = _rows2d(dy)
     T = d2.shape[0]
     r = 0 if v is None else v.shape[-1]
     v2 = None if v is None else _rows2d(v)
     la = None if lora_a is None else lora_a.contiguous()
-    if _use_dequant_gemm(T, path):
+    if weight is not None or uses_dequant_path(T, path):
         from .gemm import gemm2
-        w = dequantize_nf4(packed, qs, torch.bfloat16,
-                           out=_weight_workspace(dy.device, out_f, in_f))
+        w = weight
+        if w is None:
+            w = dequantize_nf4(packed, qs, torch.bfloat16,
+                               out=_weight_workspace(dy.device, out_f, in_f))
         dx = gemm2(d2, w.t(), v2, None if la is None else la.t())
         return dx.view(*dy.shape[:-1], in_f)
     dx = torch.empty((T, in_f), dtype=torch.bfloat16, device=dy.device)

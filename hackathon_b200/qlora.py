@@ -64,26 +64,30 @@ MASKS = {}
 
 
 class LoRANF4Proj(torch.autograd.Function):
-    """The whole QLoRA projection on the fused kernels:
+    """The whole QLoRA projection (and the residual add it feeds) on this package's kernels:
 
-        forward   U  = dropout(x) A^T                                   (skinny GEMM)
-                  y  = x deq(W)^T + b + U (s B)^T                       (qb_nf4_linear_fwd)
+        forward   xd = dropout(x)                      (mask drawn once per step, kept as bits)
+                  U  = xd A^T                                           (skinny GEMM)
+                  y  = h + x deq(W)^T + b + U (s B)^T                   (one tcgen05 GEMM)
         backward  V  = g (s B)                                          (skinny GEMM)
-                  dx = g deq(W) + dropout^T(V A)                        (qb_nf4_linear_dgrad;
+                  dx = g deq(W)  [+= s mask .* (V A)]                   (tcgen05 GEMM, then the
+                                                                         masked-accumulate GEMM;
                                                                          V A as extra K if p = 0)
-                  dA = V^T dropout(x),  dB = s g^T U                    (fp32 adapter grads)
-    The dropout mask is regenerated from the seed (Philox, no stored mask)."""
+                  dA = V^T xd,  dB = s g^T U,  dh = g                   (fp32 adapter grads)
+    Under activation checkpointing the recompute keeps xd and, on the long-token path, the bf16
+    weight it rebuilt, so the backward of the same layer neither replays the mask on x nor
+    rebuilds W (both live only from the layer's recompute to its backward)."""
 
     @staticmethod
-    def forward(ctx, x, lora_a, lora_b, mod, p, seed):
+    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual):
         from .lora import dropout_apply, dropout_mask
-        from .nf4 import nf4_linear_fwd
+        from .nf4 import nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
         scale = 1.0 / (1.0 - p) if p > 0 else 1.0
         bits = None
         if p > 0:
             # the mask is drawn once per step (Philox, the reference's stream) and kept as bits:
-            # the checkpoint recompute and the backward reuse it instead of redrawing
+            # the checkpoint recompute reuses it instead of redrawing
             key = (id(mod), seed)
             bits = MASKS.get(key)
             if bits is None or bits.shape[0] != x2.shape[0]:
@@ -96,34 +100,45 @@ class LoRANF4Proj(torch.autograd.Function):
         a16 = lora_a.to(x.dtype)
         sb16 = (lora_b * mod.scaling).to(x.dtype)
         u = xd @ a16.t()
-        y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16)
-        ctx.save_for_backward(x2, u, lora_a, lora_b, bits)
+        w_keep = None
+        if ctx.needs_input_grad[0] and uses_dequant_path(x2.shape[0]):
+            w_keep = torch.empty((mod.out_features, mod.in_features), dtype=torch.bfloat16,
+                                 device=x.device)
+        y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16,
+                           residual=residual, weight_out=w_keep)
+        ctx.save_for_backward(xd, u, lora_a, lora_b, bits, w_keep)
         ctx.mod, ctx.p, ctx.seed, ctx.scale, ctx.shape = mod, p, seed, scale, x.shape
+        ctx.has_residual = residual is not None
         return y.view(*x.shape[:-1], y.shape[-1])
 
     @staticmethod
     def backward(ctx, g):
-        from .lora import dropout_apply
+        from .gemm import gemm_mask_acc
         from .nf4 import nf4_linear_dgrad
-        x2, u, lora_a, lora_b, bits = ctx.saved_tensors
+        xd, u, lora_a, lora_b, bits, w_keep = ctx.saved_tensors
         mod, p = ctx.mod, ctx.p
         g2 = g.reshape(-1, g.shape[-1])
-        if g2.dtype != x2.dtype:
-            g2 = g2.to(x2.dtype)
-        a16 = lora_a.to(x2.dtype)
-        sb16 = (lora_b * mod.scaling).to(x2.dtype)
+        if g2.dtype != xd.dtype:
+            g2 = g2.to(xd.dtype)
+        a16 = lora_a.to(xd.dtype)
+        sb16 = (lora_b * mod.scaling).to(xd.dtype)
         v = g2 @ sb16                                              # [T, r]
         if p > 0:
             MASKS.pop((id(mod), ctx.seed), None)
-            dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state)
-            dropout_apply(v @ a16, bits, ctx.scale, out=dx, accumulate=True)
-            xd = dropout_apply(x2, bits, ctx.scale)
+        dx = None
+        if not ctx.needs_input_grad[0]:
+            pass                      # e.g. the first layer's q/k/v: x comes from the embedding
+        elif p > 0:
+            dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, weight=w_keep)
+            gemm_mask_acc(v, a16.t(), bits, ctx.scale, dx)         # dx += s mask .* (V A)
+            dx = dx.view(ctx.shape)
         else:
-            dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, v, a16)
-            xd = x2
+            dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, v, a16, weight=w_keep)
+            dx = dx.view(ctx.shape)
         da = (v.t() @ xd).float() if ctx.needs_input_grad[1] else None
         db = (g2.t() @ u).float() * mod.scaling if ctx.needs_input_grad[2] else None
-        return dx.view(ctx.shape), da, db, None, None, None
+        dres = g if ctx.has_residual and ctx.needs_input_grad[6] else None
+        return dx, da, db, None, None, None, dres
 
 
 class LoRANF4Linear(torch.nn.Module):
@@ -152,16 +167,22 @@ class LoRANF4Linear(torch.nn.Module):
         self.in_features, self.out_features = in_features, out_features
         self.fused = True
 
-    def forward(self, x, seed):
+    def forward(self, x, seed, residual=None):
+        """residual + this projection of x (the residual add of the decoder layer rides in the
+        projection's epilogue on the fused path)."""
         from .nf4 import fused_ok
         p = self.p if self.training else 0.0
         if self.fused and fused_ok(x, self.quant_state):
-            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed)
+            if residual is not None and (residual.dtype != torch.bfloat16
+                                         or residual.shape[:-1] != x.shape[:-1]):
+                raise ValueError("residual: bf16, one row per input row")
+            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual)
         # the reference's composition: NF4Linear + DropoutCast + adapter GEMMs + ScaledAdd
         base = NF4Linear.apply(x, self.packed, self.quant_state, self.bias)
         xd = DropoutCast.apply(x, p, seed, x.dtype) if p > 0 else x
         lo = F.linear(F.linear(xd, self.lora_A.to(x.dtype)), self.lora_B.to(x.dtype))
-        return ScaledAdd.apply(base, lo, self.scaling)
+        out = ScaledAdd.apply(base, lo, self.scaling)
+        return out if residual is None else residual + out
 
 
 _PROJ = ("q", "k", "v", "o", "gate", "up", "down")
@@ -193,10 +214,10 @@ class DecoderLayer(torch.nn.Module):
         q, k = CudaRoPE.apply(q, k, cos, sin)
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
-        h = h + self.o(a, seed + 3)
+        h = self.o(a, seed + 3, residual=h)
         x = rmsnorm(h, self.ln2, s.eps)
         m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
-        return h + self.down(m, seed + 6)
+        return self.down(m, seed + 6, residual=h)
 
 
 class QwenQLoRA(torch.nn.Module):

@@ -196,19 +196,31 @@ int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const void* B, int6
                  int b_mn_major, void* C, int64_t ldc, int c_dtype, const float* bias, int64_t M,
                  int64_t N, int64_t K, cudaStream_t stream);
 
-/* C[M, N] = A0[M, K0] * B0[N, K0]^T + A1[M, K1] * B1[N, K1]^T (+ bias[N] fp32), fp32
- * accumulation in one pass (segment 1 is extra K of the same accumulator); C fp32 or bf16.
- * K1 == 0 is qb_gemm_bf16. With K1 > 0 the A operands are K-major and the B operands are both
- * K-major or both MN-major (QB_ERR_UNSUPPORTED otherwise). This is the long-token path of a
- * 4-bit projection with its LoRA term on a transient bf16 copy of the weight (qb_nf4_dequant
- * writes it): forward y = [x | u] [W | s*B_lora]^T + bias, input gradient
- * dx = [dy | v] [W^T | A_lora^T]^T. Replaces solution/nf4.py:100-112 (F.linear / grad_out @ W
- * on the dequantised weight) and the lora_B(...) + ScaledAdd of solution/lora.py:172-173. */
+/* C[M, N] = A0[M, K0] * B0[N, K0]^T + A1[M, K1] * B1[N, K1]^T (+ bias[N] fp32)
+ * (+ residual[M, N], C's type, row stride ldr), fp32 accumulation in one pass (segment 1 is extra
+ * K of the same accumulator), one rounding; C fp32 or bf16. K1 == 0 without a residual is
+ * qb_gemm_bf16. Otherwise the A operands are K-major and the B operands are both K-major or both
+ * MN-major (QB_ERR_UNSUPPORTED otherwise). This is the long-token path of a 4-bit projection with
+ * its LoRA term on a transient bf16 copy of the weight (qb_nf4_dequant writes it): forward
+ * y = h + [x | u] [W | s*B_lora]^T + bias (h: the residual stream the projection feeds), input
+ * gradient dx = [dy | v] [W^T | A_lora^T]^T. Replaces solution/nf4.py:100-112 (F.linear /
+ * grad_out @ W on the dequantised weight), the lora_B(...) + ScaledAdd of solution/lora.py:172-173
+ * and the decoder layer's residual add (transformers Qwen2DecoderLayer). */
 int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0, int64_t ldb0,
                   int b0_mn_major, int64_t K0, const void* A1, int64_t lda1, int a1_mn_major,
                   const void* B1, int64_t ldb1, int b1_mn_major, int64_t K1, void* C,
-                  int64_t ldc, int c_dtype, const float* bias, int64_t M, int64_t N,
-                  cudaStream_t stream);
+                  int64_t ldc, int c_dtype, const float* bias, const void* residual, int64_t ldr,
+                  int64_t M, int64_t N, cudaStream_t stream);
+
+/* C[M, N] (bf16, in place) += scale * mask .* (A[M, K] * B[N, K]^T): fp32 product, one rounding
+ * per element, A K-major, B K- or MN-major; mask bit (n & 31) of bits[m * ldbits + n / 32] (the
+ * words qb_dropout_mask records). The input gradient of a dropped-out LoRA branch,
+ * dx += s * mask .* ((dy s B) A), added to the base projection's dx without storing the [M, N]
+ * product. Replaces the DropoutCast backward (solution/lora.py:90-93) on lora_A's input gradient
+ * and the autograd sum of the two dx terms. */
+int qb_gemm_bf16_mask_acc(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn_major,
+                          const uint32_t* bits, int64_t ldbits, float scale, void* C, int64_t ldc,
+                          int64_t M, int64_t N, int64_t K, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
  * NF4 x LoRA projection on tcgen05, the NF4 weight rebuilt in registers inside the GEMM

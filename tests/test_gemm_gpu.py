@@ -157,3 +157,51 @@ def test_gemm_ragged_bf16_both_b_layouts(cuda, shape, b_t):
     device_error()
     _check(out, _ref(a, b), torch.bfloat16)
     _check(out2, _ref(a, b) + _ref(u, v), torch.bfloat16)
+
+
+@pytest.mark.parametrize("shape", [(300, 1000, 64), (16384, 3584, 64), (129, 200, 16)])
+@pytest.mark.parametrize("b_t", [True, False])
+def test_gemm_mask_acc(cuda, shape, b_t):
+    """C += s * mask .* (A B^T) with the dropout bit words (qb_gemm_bf16_mask_acc): against the
+    fp32 product masked on the host from the same bits, one rounding of C + s * acc."""
+    from hackathon_b200.gemm import device_error, gemm_mask_acc
+    M, N, K = shape
+    g = torch.Generator(device=cuda).manual_seed(8)
+    a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    if b_t:   # [K, N] row-major, used transposed (the LoRA A matrix [r, in])
+        b = (torch.randn(K, (N + 7) // 8 * 8, device=cuda, generator=g) * 0.1).to(torch.bfloat16)[:, :N].t()
+    else:
+        b = (torch.randn(N, K, device=cuda, generator=g) * 0.1).to(torch.bfloat16)
+    words = (N + 31) // 32
+    bits = torch.randint(-2**31, 2**31 - 1, (M, words), device=cuda, dtype=torch.int64,
+                         generator=g).to(torch.int32)
+    c0 = torch.randn(M, (N + 7) // 8 * 8, device=cuda, generator=g).to(torch.bfloat16)[:, :N]
+    c = c0.clone()
+    gemm_mask_acc(a, b, bits, 1.25, c)
+    device_error()
+    cols = torch.arange(N, device=cuda)
+    mask = ((bits.long()[:, cols // 32] >> (cols % 32)) & 1).bool()
+    ref = c0.float() + torch.where(mask, 1.25 * (a.float() @ b.float().t()), 0.0)
+    torch.testing.assert_close(c.float(), ref, rtol=1.6e-2, atol=2e-2)
+    # masked-out elements are untouched, bit for bit
+    assert torch.equal(c.view(torch.int16)[~mask], c0.contiguous().view(torch.int16)[~mask])
+
+
+@pytest.mark.parametrize("lora", [False, True])
+def test_gemm2_residual_epilogue(cuda, lora):
+    """out = residual + A0 B0^T (+ A1 B1^T) (+ bias) in one accumulation and one rounding."""
+    from hackathon_b200.gemm import device_error, gemm2
+    g = torch.Generator(device=cuda).manual_seed(9)
+    M, N, K = 1000, 640, 320
+    a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(torch.bfloat16)
+    res = torch.randn(M, N, device=cuda, generator=g).to(torch.bfloat16)
+    bias = torch.randn(N, device=cuda, generator=g)
+    u = torch.randn(M, 64, device=cuda, generator=g).to(torch.bfloat16) if lora else None
+    sb = (torch.randn(N, 64, device=cuda, generator=g) * 0.05).to(torch.bfloat16) if lora else None
+    out = gemm2(a, b, u, sb, bias=bias, residual=res)
+    device_error()
+    ref = res.float() + a.float() @ b.float().t() + bias
+    if lora:
+        ref = ref + u.float() @ sb.float().t()
+    torch.testing.assert_close(out.float(), ref, rtol=1.6e-2, atol=2e-2)

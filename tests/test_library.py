@@ -49,10 +49,16 @@ def test_error_message_plumbing_without_gpu():
     fake = 1 << 20
     with pytest.raises(RuntimeError, match="K-major"):
         _lib.call("qb_gemm2_bf16", fake, 64, 1, fake, 64, 0, 64, fake, 64, 0, fake, 64, 0, 64,
-                  fake, 64, 2, None, 128, 128, None)
+                  fake, 64, 2, None, None, 0, 128, 128, None)
     with pytest.raises(RuntimeError, match="bad K"):
         _lib.call("qb_gemm2_bf16", fake, 64, 0, fake, 64, 0, 0, fake, 64, 0, fake, 64, 0, 64,
-                  fake, 64, 2, None, 128, 128, None)
+                  fake, 64, 2, None, None, 0, 128, 128, None)
+    with pytest.raises(RuntimeError, match="residual row stride"):
+        _lib.call("qb_gemm2_bf16", fake, 64, 0, fake, 64, 0, 64, None, 0, 0, None, 0, 0, 0,
+                  fake, 128, 2, None, fake, 64, 128, 128, None)
+    with pytest.raises(RuntimeError, match="mask row stride"):
+        _lib.call("qb_gemm_bf16_mask_acc", fake, 64, fake, 64, 1, fake, 3, 1.0, fake, 128, 128,
+                  128, 64, None)
 
 
 @pytest.mark.parametrize("op", ["rmsnorm", "rope", "swiglu", "dropout", "dequant"])

@@ -53,6 +53,40 @@ def test_fused_projection_matches_reference_composition(cuda, p, shape):
         assert rel < 2e-2, float(rel)
 
 
+@pytest.mark.parametrize("p", [0.0, 0.1])
+def test_long_token_projection_with_residual_matches_composition(cuda, p):
+    """At the long-token path (transient bf16 weight kept from forward to backward, residual in
+    the GEMM epilogue, masked-accumulate GEMM for the dropped-out LoRA input gradient): forward
+    and all grads, residual grad included, against the reference's composition + a residual add."""
+    from hackathon_b200.nf4 import DEQUANT_GEMM_MIN_TOKENS
+    from hackathon_b200.qlora import LoRANF4Linear, preset
+    in_f, out_f, T = 896, 640, DEQUANT_GEMM_MIN_TOKENS
+    s = preset("0.5b", lora_r=64, lora_alpha=128, lora_dropout=p)
+    gen = torch.Generator(device=cuda).manual_seed(6)
+    mod = LoRANF4Linear(in_f, out_f, False, s, cuda, gen)
+    with torch.no_grad():
+        mod.lora_B.normal_(0, 0.05, generator=gen)
+    x = torch.randn(T, in_f, device=cuda, generator=gen).to(torch.bfloat16)
+    h = torch.randn(T, out_f, device=cuda, generator=gen).to(torch.bfloat16)
+    gy = torch.randn(T, out_f, device=cuda, generator=gen).to(torch.bfloat16)
+    outs = []
+    for fused in (True, False):
+        mod.fused = fused
+        mod.lora_A.grad = mod.lora_B.grad = None
+        xi, hi = x.clone().requires_grad_(), h.clone().requires_grad_()
+        y = mod(xi, seed=99, residual=hi)
+        y.backward(gy)
+        outs.append((y.detach().float(), xi.grad.float(), hi.grad.float(),
+                     mod.lora_A.grad.clone(), mod.lora_B.grad.clone()))
+    (y1, dx1, dh1, da1, db1), (y0, dx0, dh0, da0, db0) = outs
+    torch.testing.assert_close(y1, y0, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(dx1, dx0, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(dh1, dh0, rtol=0, atol=0)
+    for a, b in ((da1, da0), (db1, db0)):
+        rel = (a - b).norm() / b.norm()
+        assert rel < 2e-2, float(rel)
+
+
 def test_checkpoint_replays_dropout_masks(cuda):
     """With dropout on, the gradients with and without activation checkpointing agree (the
     recompute must draw the same Philox masks)."""
