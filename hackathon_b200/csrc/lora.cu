@@ -32,16 +32,40 @@ __device__ __forceinline__ uint32_t philox_first_word(uint32_t c0, uint32_t k0, 
   return c0;
 }
 
-__device__ __forceinline__ float uniform_of(uint32_t w) {
-  int32_t x = static_cast<int32_t>(w);
-  if (x < 0) x = ~x;  // -x - 1 without overflow
-  return __fmul_rn(__int2float_rn(x), 4.6566127342e-10f);
+// The reference keeps an element when uniform(w) > p, with uniform(w) = fl(fl(x) * 2^-31-ish),
+// x = w as int32 folded onto [0, 2^31) (x < 0 -> -x - 1). uniform is non-decreasing in x, so the
+// test is x > T for one integer T per call (keep_threshold, host side, same IEEE single
+// operations): the kernels compare integers and never convert to float.
+constexpr float kUniformScale = 4.6566127342e-10f;
+
+__device__ __forceinline__ bool keep_of(uint32_t w, int32_t thresh) {
+  const int32_t x = static_cast<int32_t>(w ^ static_cast<uint32_t>(static_cast<int32_t>(w) >> 31));
+  return x > thresh;
+}
+
+// Largest x in [0, 2^31) with fl(fl(x) * kUniformScale) <= p, or -1 when there is none
+// (p below every uniform: everything kept). Bisection over a non-decreasing function.
+int32_t keep_threshold(float p) {
+  auto u = [](int32_t x) {
+    volatile float f = static_cast<float>(x);   // round to nearest, as __int2float_rn
+    volatile float r = f * kUniformScale;       // round to nearest, as __fmul_rn
+    return static_cast<float>(r);
+  };
+  if (!(u(0) <= p)) return -1;
+  int32_t lo = 0, hi = 0x7fffffff;              // u(lo) <= p
+  if (u(hi) <= p) return hi;                    // nothing kept
+  while (hi - lo > 1) {                         // u(hi) > p
+    const int32_t mid = lo + (hi - lo) / 2;
+    if (u(mid) <= p) lo = mid;
+    else hi = mid;
+  }
+  return lo;
 }
 
 template <typename IT, typename OT, bool DROP, int VEC>
 __global__ void __launch_bounds__(kThreads)
 dropout_scale_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out, int64_t outs,
-                     int64_t cols, uint32_t k0, uint32_t k1, float p, float scale) {
+                     int64_t cols, uint32_t k0, uint32_t k1, int32_t thresh, float scale) {
   const int64_t row = blockIdx.x;
   const IT* src = in + row * ins;
   OT* dst = out + row * outs;
@@ -53,7 +77,7 @@ dropout_scale_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ ou
     for (int e = 0; e < VEC; ++e) {
       if (DROP) {
         const uint32_t off = static_cast<uint32_t>(row * cols + c + e);  // int32 wrap, as the reference
-        const bool keep = uniform_of(philox_first_word(off, k0, k1)) > p;
+        const bool keep = keep_of(philox_first_word(off, k0, k1), thresh);
         v[e] = keep ? v[e] * scale : 0.0f;
       } else {
         v[e] = v[e] * scale;
@@ -95,7 +119,7 @@ template <typename IT, typename OT>
 __global__ void __launch_bounds__(kThreads)
 dropout_mask_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out, int64_t outs,
                     uint32_t* __restrict__ bits, int64_t words, int64_t rows, int64_t cols,
-                    uint32_t k0, uint32_t k1, float p, float scale) {
+                    uint32_t k0, uint32_t k1, int32_t thresh, float scale) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
@@ -105,7 +129,7 @@ dropout_mask_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out
     bool keep = false;
     if (c < cols) {
       const uint32_t off = static_cast<uint32_t>(row * cols + c);  // int32 wrap, as the reference
-      keep = uniform_of(philox_first_word(off, k0, k1)) > p;
+      keep = keep_of(philox_first_word(off, k0, k1), thresh);
       const float v = qb::to_f(in[row * ins + c]);
       out[row * outs + c] = qb::from_f<OT>(keep ? v * scale : 0.0f);
     }
@@ -121,7 +145,7 @@ template <typename IT, typename OT>
 __global__ void __launch_bounds__(kThreads)
 dropout_mask8_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out, int64_t outs,
                      uint32_t* __restrict__ bits, int64_t rows, int64_t cols, uint32_t k0,
-                     uint32_t k1, float p, float scale) {
+                     uint32_t k1, int32_t thresh, float scale) {
   const int64_t n8 = cols / 8;
   const int64_t total = rows * n8;   // a multiple of 4: every group of four lanes is complete
   const int lane = threadIdx.x & 31;
@@ -135,7 +159,7 @@ dropout_mask8_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ ou
       const uint32_t off0 = static_cast<uint32_t>(row * cols + c);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const bool keep = uniform_of(philox_first_word(off0 + e, k0, k1)) > p;
+        const bool keep = keep_of(philox_first_word(off0 + e, k0, k1), thresh);
         b |= static_cast<uint32_t>(keep) << e;
         v[e] = keep ? v[e] * scale : 0.0f;
       }
@@ -195,6 +219,7 @@ extern "C" int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stri
   if (rows == 0 || cols == 0) return QB_OK;
   if (!in || !out || !bits) return qb::fail(QB_ERR_INVALID, "dropout_mask: null pointer");
   if (p >= 1.0f) return qb::fail(QB_ERR_INVALID, "dropout_mask: p must be < 1");
+  const int32_t thresh = keep_threshold(p);
   const uint32_t k0 = static_cast<uint32_t>(seed & 0xffffffffu);
   const uint32_t k1 = static_cast<uint32_t>(seed >> 32);
   const int64_t words = (cols + 31) / 32;
@@ -204,11 +229,11 @@ extern "C" int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stri
           rows_ok(out, out_row_stride, sizeof(OT))) {
         dropout_mask8_kernel<IT, OT><<<grid_cap(rows * (cols / 8)), kThreads, 0, stream>>>(
             static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out), out_row_stride,
-            bits, rows, cols, k0, k1, p, scale);
+            bits, rows, cols, k0, k1, thresh, scale);
       } else {
         dropout_mask_kernel<IT, OT><<<grid_cap(rows * words * 32), kThreads, 0, stream>>>(
             static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out), out_row_stride,
-            bits, words, rows, cols, k0, k1, p, scale);
+            bits, words, rows, cols, k0, k1, thresh, scale);
       }
     });
   });
@@ -249,6 +274,7 @@ extern "C" int qb_dropout_scale(const void* in, int in_dtype, int64_t in_row_str
   if (rows == 0 || cols == 0) return QB_OK;
   if (!in || !out) return qb::fail(QB_ERR_INVALID, "dropout_scale: null pointer");
   if (p >= 1.0f) return qb::fail(QB_ERR_INVALID, "dropout_scale: p must be < 1");
+  const int32_t thresh = keep_threshold(p);
   const uint32_t k0 = static_cast<uint32_t>(seed & 0xffffffffu);
   const uint32_t k1 = static_cast<uint32_t>(seed >> 32);
   const bool drop = p > 0.0f;
@@ -260,11 +286,11 @@ extern "C" int qb_dropout_scale(const void* in, int in_dtype, int64_t in_row_str
       auto* op = static_cast<OT*>(out);
       const unsigned grid = static_cast<unsigned>(rows);
       if (vec) {
-        if (drop) dropout_scale_kernel<IT, OT, true, 8><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, p, scale);
-        else dropout_scale_kernel<IT, OT, false, 8><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, p, scale);
+        if (drop) dropout_scale_kernel<IT, OT, true, 8><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, thresh, scale);
+        else dropout_scale_kernel<IT, OT, false, 8><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, thresh, scale);
       } else {
-        if (drop) dropout_scale_kernel<IT, OT, true, 1><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, p, scale);
-        else dropout_scale_kernel<IT, OT, false, 1><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, p, scale);
+        if (drop) dropout_scale_kernel<IT, OT, true, 1><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, thresh, scale);
+        else dropout_scale_kernel<IT, OT, false, 1><<<grid, kThreads, 0, stream>>>(ip, in_row_stride, op, out_row_stride, cols, k0, k1, thresh, scale);
       }
     });
   });
