@@ -51,7 +51,8 @@ BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hb
          "qb_ce_reduce": "hbm", "qb_gemm_bf16": "tensor", "qb_gemm2_bf16": "tensor",
          "qb_nf4_linear_fwd": "tensor",
          "qb_nf4_linear_dgrad": "tensor", "qb_linear_ce_stats": "tensor",
-         "qb_linear_ce_grad": "tensor"}
+         "qb_linear_ce_grad": "tensor", "qb_linear_ce_stats_logits": "tensor",
+         "qb_ce_grad_from_logits": "hbm", "qb_gemm_bf16_mask_acc": "hbm"}
 
 
 def peaks():

@@ -58,6 +58,8 @@ _SIGNATURES = {
                             _i64, _p, _i64, _i64, _p, _i64, _p],
     "qb_linear_ce_vocab_tiles": [_i64],
     "qb_linear_ce_stats": [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p],
+    "qb_linear_ce_stats_logits": [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p],
+    "qb_ce_grad_from_logits": [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _p],
     "qb_ce_reduce": [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p],
     "qb_linear_ce_grad": [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p],
 }

@@ -24,10 +24,18 @@ GRAD_GAIN = 65536.0
 STEP_ATTR = "_soup_chunked_step"
 
 
-def linear_ce_tc(h2, w, tgt, token_loss, entropy, pred, grad_h, scale_dev, chunk_rows):
+# With the gradient wanted, pass 1 also stores the chunk's fp32 logits (rows x vocab x 4 bytes of
+# scratch, 2.5 GB at 4096 x 152064) and dZ comes from them in one streaming pass, instead of
+# recomputing the logits GEMM (2 N H V flops) in pass 2. Same z, same arithmetic, same dZ.
+STORE_LOGITS = True
+
+
+def linear_ce_tc(h2, w, tgt, token_loss, entropy, pred, grad_h, scale_dev, chunk_rows,
+                 store_logits=None):
     """The tcgen05 path for bf16 hidden states and head: per chunk of rows, pass 1 (logits in
-    TMEM -> per-tile row statistics), the reduction, and with grad_h pass 2 (logits in TMEM ->
-    dZ bf16) followed by dH = dZ @ W into grad_h (fp32). Logits never reach HBM."""
+    TMEM -> per-tile row statistics, and the fp32 logits when `store_logits`), the reduction,
+    and with grad_h the dZ pass (from the stored logits, or a second logits GEMM with dZ in its
+    epilogue) followed by dH = dZ @ W into grad_h (fp32)."""
     from .gemm import gemm
     n, hdim = h2.shape
     vocab = w.shape[0]
@@ -41,23 +49,38 @@ def linear_ce_tc(h2, w, tgt, token_loss, entropy, pred, grad_h, scale_dev, chunk
     ldz = (vocab + 7) // 8 * 8      # 16-byte rows for the dH GEMM's TMA
     dz = torch.empty((rows_max, ldz), dtype=torch.bfloat16, device=dev) \
         if grad_h is not None else None
+    keep = (STORE_LOGITS if store_logits is None else store_logits) and grad_h is not None
+    ldl = (vocab + 3) // 4 * 4
+    logits = torch.empty((rows_max, ldl), dtype=torch.float32, device=dev) if keep else None
     for start in range(0, n, chunk_rows):
         stop = min(start + chunk_rows, n)
         rows = stop - start
         h = h2[start:stop]
         t = tgt[start:stop]
-        _lib.call("qb_linear_ce_stats", h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
-                  t.data_ptr(), rows, vocab, hdim, partials.data_ptr(), z_label.data_ptr(), s,
-                  work=(0, 2 * rows * vocab * hdim))
+        if keep:
+            _lib.call("qb_linear_ce_stats_logits", h.data_ptr(), h.stride(0), w.data_ptr(),
+                      w.stride(0), t.data_ptr(), rows, vocab, hdim, partials.data_ptr(),
+                      z_label.data_ptr(), logits.data_ptr(), ldl, s,
+                      work=(0, 2 * rows * vocab * hdim))
+        else:
+            _lib.call("qb_linear_ce_stats", h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
+                      t.data_ptr(), rows, vocab, hdim, partials.data_ptr(), z_label.data_ptr(), s,
+                      work=(0, 2 * rows * vocab * hdim))
         _lib.call("qb_ce_reduce", partials.data_ptr(), n_vt, rows, vocab, t.data_ptr(),
                   z_label.data_ptr(), token_loss[start:stop].data_ptr(),
                   entropy[start:stop].data_ptr(), pred[start:stop].data_ptr(), None,
                   lse.data_ptr(), s, work=(n_vt * rows * 16 + rows * 32, 0))
-        if grad_h is not None:
+        if grad_h is None:
+            continue
+        if keep:
+            _lib.call("qb_ce_grad_from_logits", logits.data_ptr(), ldl, t.data_ptr(), rows,
+                      vocab, lse.data_ptr(), scale_dev.data_ptr(), dz.data_ptr(), dz.stride(0),
+                      s, work=(rows * vocab * (4 + 2), 0))
+        else:
             _lib.call("qb_linear_ce_grad", h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
                       t.data_ptr(), rows, vocab, hdim, lse.data_ptr(), scale_dev.data_ptr(),
                       dz.data_ptr(), dz.stride(0), s, work=(0, 2 * rows * vocab * hdim))
-            gemm(dz[:rows, :vocab], w.t(), out=grad_h[start:stop], out_dtype=torch.float32)
+        gemm(dz[:rows, :vocab], w.t(), out=grad_h[start:stop], out_dtype=torch.float32)
 
 
 def tc_path_ok(h2, w, matmul_dtype):

@@ -62,11 +62,16 @@ struct EpiGrad {
 // Per row of the tile: (max m, sum e^(z-m), sum e^(z-m) z, first argmax) over the tile's
 // columns; z[label] when the label falls in this tile. One running max per 32-column chunk: when
 // a chunk raises it, the sums so far are rescaled once.
+// With `logits` set, the tile's fp32 logits are also stored ([rows, ldl]), so the gradient pass
+// can read them back (qb_ce_grad_from_logits) instead of recomputing the GEMM.
 struct EpiStats {
   float4* partials;
   float* z_label;
   const int64_t* target;
   int rows, vocab;
+  float* logits;   // or null
+  int64_t ldl;
+  bool lvec;       // 16-byte aligned logits rows
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -79,6 +84,18 @@ struct EpiStats {
       float v[32];
       tc::tmem_ld32(taddr + ch * 32, v);
       const int n = n0 + ch * 32;
+      if (logits && r < rows && n < vocab) {
+        float* dst = logits + static_cast<int64_t>(r) * ldl + n;
+        if (lvec && n + 32 <= vocab) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (n + i < vocab) dst[i] = v[i];
+        }
+      }
       float cm = -INFINITY;
       int cidx = 0x7fffffff;
 #pragma unroll
@@ -109,6 +126,39 @@ struct EpiStats {
       partials[static_cast<int64_t>(n0 / BN) * rows + r] = make_float4(m, s, t, __int_as_float(idx));
   }
 };
+
+// dz = (e^(z - lse) - onehot) * scale from stored fp32 logits: the same arithmetic as EpiGrad
+// on the same z, so dz is identical to the recomputing pass. One CTA per row, 16-byte loads.
+__global__ void __launch_bounds__(256)
+ce_grad_from_logits_kernel(const float* __restrict__ logits, int64_t ldl,
+                           const int64_t* __restrict__ target, const float* __restrict__ lse,
+                           const float* __restrict__ scale_dev, __nv_bfloat16* __restrict__ dz,
+                           int64_t ldz, int vocab, bool vec) {
+  const int64_t r = blockIdx.x;
+  const int64_t label = __ldg(target + r);
+  const float l = __ldg(lse + r);
+  const float sc = label >= 0 ? __ldg(scale_dev) : 0.f;
+  const float* z = logits + r * ldl;
+  __nv_bfloat16* d = dz + r * ldz;
+  if (vec) {
+    for (int n = threadIdx.x * 8; n < vocab; n += blockDim.x * 8) {
+      if (n + 8 <= vocab) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(z + n));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(z + n + 4));
+        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = (__expf(v[i] - l) - (n + i == label ? 1.f : 0.f)) * sc;
+        qb::store8<__nv_bfloat16>(d + n, v);
+      } else {
+        for (int i = n; i < vocab; ++i)
+          d[i] = __float2bfloat16_rn((__expf(z[i] - l) - (i == label ? 1.f : 0.f)) * sc);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x)
+      d[i] = __float2bfloat16_rn((__expf(z[i] - l) - (i == label ? 1.f : 0.f)) * sc);
+  }
+}
 
 // One warp per row: merge the row's partials, finish the statistics.
 __global__ void ce_reduce_kernel(const float4* __restrict__ partials, int n_vt, int rows,
@@ -176,6 +226,25 @@ int check(int64_t rows, int64_t vocab, int64_t hdim, const void* a, const void* 
   return QB_OK;
 }
 
+
+int stats(const void* hidden, int64_t ldh, const void* weight, int64_t ldw,
+          const int64_t* target, int64_t rows, int64_t vocab, int64_t hdim, void* partials,
+          float* z_label, float* logits, int64_t ldl, cudaStream_t stream, const char* what) {
+  if (int s = check(rows, vocab, hdim, hidden, weight, what)) return s;
+  if (rows == 0) return QB_OK;
+  if (!target || !partials || !z_label) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  if (logits && ldl < vocab) return qb::fail(QB_ERR_INVALID, "%s: logits row stride", what);
+  CUtensorMap mh, mw;
+  if (int s = maps(&mh, &mw, hidden, ldh, weight, ldw, rows, vocab, hdim)) return s;
+  tcg::Problem pb{static_cast<int>(rows), static_cast<int>(vocab), static_cast<int>((hdim + 63) / 64),
+                  0, static_cast<int>((rows + 127) / 128), static_cast<int>((vocab + kBN - 1) / kBN)};
+  EpiStats epi{static_cast<float4*>(partials), z_label, target, static_cast<int>(rows),
+                static_cast<int>(vocab), logits, ldl,
+                logits && qb::aligned16(logits) && (ldl * 4) % 16 == 0};
+  return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
+      mh, mw, mh, mw, pb, epi, stream, what);
+}
+
 }  // namespace
 
 extern "C" int64_t qb_linear_ce_vocab_tiles(int64_t vocab) { return (vocab + kBN - 1) / kBN; }
@@ -184,17 +253,35 @@ extern "C" int qb_linear_ce_stats(const void* hidden, int64_t ldh, const void* w
                                   int64_t ldw, const int64_t* target, int64_t rows,
                                   int64_t vocab, int64_t hdim, void* partials, float* z_label,
                                   cudaStream_t stream) {
-  if (int s = check(rows, vocab, hdim, hidden, weight, "linear_ce_stats")) return s;
+  return stats(hidden, ldh, weight, ldw, target, rows, vocab, hdim, partials, z_label, nullptr, 0,
+               stream, "linear_ce_stats");
+}
+
+extern "C" int qb_linear_ce_stats_logits(const void* hidden, int64_t ldh, const void* weight,
+                                         int64_t ldw, const int64_t* target, int64_t rows,
+                                         int64_t vocab, int64_t hdim, void* partials,
+                                         float* z_label, float* logits, int64_t ldl,
+                                         cudaStream_t stream) {
+  if (!logits) return qb::fail(QB_ERR_INVALID, "linear_ce_stats_logits: null logits");
+  return stats(hidden, ldh, weight, ldw, target, rows, vocab, hdim, partials, z_label, logits,
+               ldl, stream, "linear_ce_stats_logits");
+}
+
+extern "C" int qb_ce_grad_from_logits(const float* logits, int64_t ldl, const int64_t* target,
+                                      int64_t rows, int64_t vocab, const float* lse,
+                                      const float* scale_dev, void* dz, int64_t ldz,
+                                      cudaStream_t stream) {
+  if (rows < 0 || vocab <= 0 || rows > 0x7fffffff || vocab > (1 << 30) || ldl < vocab || ldz < vocab)
+    return qb::fail(QB_ERR_INVALID, "ce_grad_from_logits: bad shape");
   if (rows == 0) return QB_OK;
-  if (!target || !partials || !z_label) return qb::fail(QB_ERR_INVALID, "linear_ce_stats: null pointer");
-  CUtensorMap mh, mw;
-  if (int s = maps(&mh, &mw, hidden, ldh, weight, ldw, rows, vocab, hdim)) return s;
-  tcg::Problem pb{static_cast<int>(rows), static_cast<int>(vocab), static_cast<int>((hdim + 63) / 64),
-                  0, static_cast<int>((rows + 127) / 128), static_cast<int>((vocab + kBN - 1) / kBN)};
-  EpiStats epi{static_cast<float4*>(partials), z_label, target, static_cast<int>(rows),
-                static_cast<int>(vocab)};
-  return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
-      mh, mw, mh, mw, pb, epi, stream, "linear_ce_stats");
+  if (!logits || !target || !lse || !scale_dev || !dz)
+    return qb::fail(QB_ERR_INVALID, "ce_grad_from_logits: null pointer");
+  const bool vec = qb::aligned16(logits) && (ldl * 4) % 16 == 0 && qb::aligned16(dz) &&
+                   (ldz * 2) % 16 == 0;
+  ce_grad_from_logits_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(
+      logits, ldl, target, lse, scale_dev, static_cast<__nv_bfloat16*>(dz), ldz,
+      static_cast<int>(vocab), vec);
+  return qb::check_launch("ce_grad_from_logits");
 }
 
 extern "C" int qb_ce_reduce(const void* partials, int64_t n_vtiles, int64_t rows, int64_t vocab,

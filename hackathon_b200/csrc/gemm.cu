@@ -4,7 +4,9 @@
 // Each operand may be K-major or MN-major in HBM (qb_gemm_bf16: every orientation the suite
 // needs — logits = H W^T, dH = dZ W, LoRA products; qb_gemm2_bf16: the two layouts of a
 // projection with its LoRA term as extra K, forward and input gradient).
-#include "tc_gemm.cuh"
+#include <cstdlib>
+
+#include "tc_gemm_pair.cuh"
 
 namespace {
 
@@ -78,10 +80,56 @@ int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
   return tcg::launch<A0, B0, A1, B1, BN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
 }
 
+// Which launches take the 2-SM kernel. It is correct (the GPU tests run with it forced on) but
+// measured at half the one-CTA kernel's throughput, so it is off unless QB_GEMM_PAIR=1 (K-major
+// A operands only); QB_GEMM_PAIR=2 takes it where there are enough 256 x 256 pair tiles to give
+// every SM pair one.
+bool use_pair(bool a_k_major, int64_t M, int64_t N) {
+  static const int mode = [] {
+    const char* e = std::getenv("QB_GEMM_PAIR");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (!a_k_major || mode == 0) return false;
+  if (mode == 1) return true;
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  return pair_tiles >= tc_host::sm_count() / 2;
+}
+
+// B tensor maps with 128-row boxes for the pair kernel (each CTA loads half of a 256-row tile);
+// MN-major maps are already 64 x 64 boxes.
+int pair_maps(CUtensorMap (&m)[4], const void* B0, int64_t ldb0, bool b0_mn, int64_t K0,
+              const void* B1, int64_t ldb1, bool b1_mn, int64_t K1, int64_t N) {
+  if (!b0_mn)
+    if (int s = map_operand(&m[1], B0, ldb0, false, N, K0, tcp::kHalfN)) return s;
+  if (!b1_mn)
+    if (int s = map_operand(&m[3], B1, ldb1, false, N, K1, tcp::kHalfN)) return s;
+  return QB_OK;
+}
+
+template <int B0, int B1, typename OutT>
+int run_pair(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
+             const float* bias, const void* resid, int64_t ldr, bool vec, cudaStream_t s,
+             const char* what) {
+  EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias,
+                        static_cast<const OutT*>(resid), ldr, vec};
+  tcg::Problem pp = pb;
+  pp.num_m = (pb.M + 255) / 256;
+  pp.num_n = (pb.N + tcp::BN - 1) / tcp::BN;
+  return tcp::launch<B0, B1>(m[0], m[1], m[2], m[3], pp, epi, s, what);
+}
+
 template <int A0, int B0, int A1, int B1>
 int run_dtype(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
               int c_dtype, const float* bias, const void* resid, int64_t ldr, bool vec,
-              cudaStream_t s, const char* what) {
+              cudaStream_t s, const char* what, const CUtensorMap* mpair = nullptr) {
+  if constexpr (A0 == tcg::kTmaK && A1 == tcg::kTmaK) {
+    if (mpair) {
+      const CUtensorMap (&mp)[4] = *reinterpret_cast<const CUtensorMap(*)[4]>(mpair);
+      if (c_dtype == QB_F32)
+        return run_pair<B0, B1, float>(mp, pb, c, ldc, bias, resid, ldr, vec, s, what);
+      return run_pair<B0, B1, __nv_bfloat16>(mp, pb, c, ldc, bias, resid, ldr, vec, s, what);
+    }
+  }
   if (c_dtype == QB_F32)
     return run<A0, B0, A1, B1, kBN, float>(m, pb, c, ldc, bias, resid, ldr, vec, s, what);
   return run<A0, B0, A1, B1, kBN, __nv_bfloat16>(m, pb, c, ldc, bias, resid, ldr, vec, s, what);
@@ -125,15 +173,24 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const vo
   m[3] = m[1];
   const tcg::Problem pb = problem(M, N, K, 0);
   const bool vec = vec_ok(C, ldc, c_dtype);
+  CUtensorMap mp[4] = {m[0], m[1], m[2], m[3]};
+  const bool pair = use_pair(!a_mn_major, M, N);
+  if (pair) {
+    if (int s = pair_maps(mp, B, ldb, b_mn_major != 0, K, B, ldb, b_mn_major != 0, K, N)) return s;
+  }
+  const CUtensorMap* mpp = pair ? &mp[0] : nullptr;
   using namespace tcg;
-#define QB_RUN(A0, B0) \
-  return run_dtype<A0, B0, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec, stream, \
-                                         what)
-  if (!a_mn_major && !b_mn_major) QB_RUN(kTmaK, kTmaK);
-  if (!a_mn_major && b_mn_major) QB_RUN(kTmaK, kTmaMN);
-  if (a_mn_major && !b_mn_major) QB_RUN(kTmaMN, kTmaK);
-  QB_RUN(kTmaMN, kTmaMN);
-#undef QB_RUN
+  if (!a_mn_major && !b_mn_major)
+    return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec,
+                                                 stream, what, mpp);
+  if (!a_mn_major && b_mn_major)
+    return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec,
+                                                   stream, what, mpp);
+  if (a_mn_major && !b_mn_major)
+    return run_dtype<kTmaMN, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec,
+                                                  stream, what);
+  return run_dtype<kTmaMN, kTmaMN, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec,
+                                                 stream, what);
 }
 
 extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,
@@ -173,10 +230,16 @@ extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, cons
   const int es = c_dtype == QB_F32 ? 4 : 2;
   const bool vec = vec_ok(C, ldc, c_dtype) &&
                    (!residual || (qb::aligned16(residual) && (ldr * es) % 16 == 0));
+  CUtensorMap mp[4] = {m[0], m[1], m[2], m[3]};
+  const bool pair = use_pair(true, M, N);
+  if (pair) {
+    if (int s = pair_maps(mp, B0, ldb0, bwd, K0, B1, ldb1, bwd, K1, N)) return s;
+  }
+  const CUtensorMap* mpp = pair ? &mp[0] : nullptr;
   using namespace tcg;
   if (fwd)
     return run_dtype<kTmaK, kTmaK, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, residual, ldr,
-                                                 vec, stream, what);
+                                                 vec, stream, what, mpp);
   return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, residual, ldr,
-                                                 vec, stream, what);
+                                                 vec, stream, what, mpp);
 }

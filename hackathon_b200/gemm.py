@@ -101,7 +101,8 @@ def gemm_mask_acc(a, b_t, bits, scale, out):
     b_t, ldb, b_mn = _operand(b_t)
     _lib.call("qb_gemm_bf16_mask_acc", a.data_ptr(), a.stride(0), b_t.data_ptr(), ldb, int(b_mn),
               bits.data_ptr(), bits.stride(0), float(scale), out.data_ptr(), out.stride(0), M, N,
-              K, _lib.stream(a.device), work=(0, 2 * M * N * K))
+              K, _lib.stream(a.device), work=(2 * M * N * out.element_size() + bits.numel() * 4
+                                              + (M + N) * K * 2, 0))
     return out
 
 

@@ -269,6 +269,23 @@ int qb_linear_ce_stats(const void* hidden, int64_t ldh, const void* weight, int6
                        const int64_t* target, int64_t rows, int64_t vocab, int64_t hdim,
                        void* partials, float* z_label, cudaStream_t stream);
 
+/* qb_linear_ce_stats that also stores each tile's fp32 logits into `logits` ([rows, ldl],
+ * ldl >= vocab): the gradient then comes from qb_ce_grad_from_logits, one streaming pass over
+ * them, instead of a second GEMM (qb_linear_ce_grad). Costs rows * ldl * 4 bytes of caller scratch
+ * per chunk. No counterpart in the reference (its chunk logits are a bf16 matmul output,
+ * solution/cross_entropy.py:117). */
+int qb_linear_ce_stats_logits(const void* hidden, int64_t ldh, const void* weight, int64_t ldw,
+                              const int64_t* target, int64_t rows, int64_t vocab, int64_t hdim,
+                              void* partials, float* z_label, float* logits, int64_t ldl,
+                              cudaStream_t stream);
+
+/* dz[rows, vocab] (bf16, row stride ldz) = (exp(z - lse) - onehot(label)) * scale from the fp32
+ * logits qb_linear_ce_stats_logits stored: the same arithmetic on the same z as
+ * qb_linear_ce_grad, so the same dz (solution/cross_entropy.py:83-90). */
+int qb_ce_grad_from_logits(const float* logits, int64_t ldl, const int64_t* target, int64_t rows,
+                           int64_t vocab, const float* lse, const float* scale_dev, void* dz,
+                           int64_t ldz, cudaStream_t stream);
+
 /* Merges the partials: lse, loss = lse - z[label] (0 if unlabelled), entropy = lse - sum(p*z),
  * pred = first argmax (int64, may be NULL), correct (int32, may be NULL), lse (may be NULL).
  * The per-row outputs of solution/cross_entropy.py:77-81 / fused_ce.py:81-87. */

@@ -211,3 +211,30 @@ def test_tc_linear_ce_unlabelled_rows_have_zero_gradient(cuda):
     assert torch.all(h.grad[0, 59:] == 0)
     assert torch.all(step.token_loss[0, 59:] == 0)
     assert torch.isfinite(loss)
+
+
+@pytest.mark.parametrize("vocab", [1000, 9001, 32771])
+def test_tc_linear_ce_stored_logits_equal_recompute(cuda, vocab):
+    """The dZ pass from stored fp32 logits (qb_linear_ce_stats_logits + qb_ce_grad_from_logits)
+    gives the same dH, bit for bit, as the pass that recomputes the logits GEMM
+    (qb_linear_ce_grad): same z, same arithmetic. Statistics are the same launch either way."""
+    from hackathon_b200 import cross_entropy as ce
+    from hackathon_b200.gemm import device_error
+    gen = torch.Generator(device=cuda).manual_seed(vocab)
+    rows, H = 700, 384
+    h2 = torch.randn(rows, H, device=cuda, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(vocab, H, device=cuda, generator=gen) * 0.05).to(torch.bfloat16)
+    tgt = torch.randint(0, vocab, (rows,), device=cuda, generator=gen)
+    tgt[::5] = -100
+    scale = torch.tensor([1.0 / 512], device=cuda)
+    outs = []
+    for keep in (True, False):
+        tl = torch.empty(rows, device=cuda)
+        en = torch.empty(rows, device=cuda)
+        pr = torch.empty(rows, dtype=torch.int64, device=cuda)
+        gh = torch.empty(rows, H, device=cuda)
+        ce.linear_ce_tc(h2, w, tgt, tl, en, pr, gh, scale, 256, store_logits=keep)
+        device_error()
+        outs.append((tl, en, pr, gh))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
