@@ -61,6 +61,66 @@ struct EpiStoreRow {
   }
 };
 
+// Gate / up pair with SwiGLU: the tile's first BN/2 accumulator columns are gate features
+// j0..j0+BN/2-1 (j0 = n0 / 2), the last BN/2 the same up features. Each is rounded to bf16 — the
+// value the separate projections would store — and h = g * sigmoid(g) * u in fp32 (the
+// arithmetic of the SwiGLU kernel) is stored as bf16; g and u themselves only when asked for
+// (the backward's inputs).
+__device__ __forceinline__ float swiglu_sigmoid(float g) { return 1.0f / (1.0f + __expf(-g)); }
+
+struct EpiSwiGLU {
+  __nv_bfloat16* h;
+  int64_t ldh;
+  __nv_bfloat16* g;   // or null
+  __nv_bfloat16* u;   // or null
+  int64_t ldgu;
+  int M, I;
+  bool vec;
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
+    const int m = m0 + row;
+    const int j0 = n0 / 2;
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      float gv[32], uv[32];
+      tc::tmem_ld32(taddr + c * 32, gv);
+      tc::tmem_ld32(taddr + BN / 2 + c * 32, uv);
+      const int j = j0 + c * 32;
+      if (m >= M || j >= I) continue;
+      float hv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        gv[i] = __bfloat162float(__float2bfloat16_rn(gv[i]));
+        uv[i] = __bfloat162float(__float2bfloat16_rn(uv[i]));
+        hv[i] = gv[i] * swiglu_sigmoid(gv[i]) * uv[i];
+      }
+      const int64_t oh = static_cast<int64_t>(m) * ldh + j;
+      const int64_t og = static_cast<int64_t>(m) * ldgu + j;
+      if (vec && j + 32 <= I) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          qb::store8<__nv_bfloat16>(h + oh + i, hv + i);
+          if (g) {
+            qb::store8<__nv_bfloat16>(g + og + i, gv + i);
+            qb::store8<__nv_bfloat16>(u + og + i, uv + i);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (j + i >= I) break;
+          h[oh + i] = __float2bfloat16_rn(hv[i]);
+          if (g) {
+            g[og + i] = __float2bfloat16_rn(gv[i]);
+            u[og + i] = __float2bfloat16_rn(uv[i]);
+          }
+        }
+      }
+    }
+  }
+};
+
 int map_operand(CUtensorMap* map, const void* p, int64_t ld, bool mn_major, int64_t rows,
                 int64_t k, int box_rows) {
   // K-major: [rows, k] with row stride ld; MN-major: stored [k, rows] with row stride ld
@@ -242,4 +302,48 @@ extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, cons
                                                  vec, stream, what, mpp);
   return run_dtype<kTmaK, kTmaMN, kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, residual, ldr,
                                                  vec, stream, what, mpp);
+}
+
+extern "C" int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_gate,
+                                     const void* w_up, int64_t ldw, int64_t K0, const void* u1,
+                                     int64_t ldu1, const void* b1_gate, const void* b1_up,
+                                     int64_t ldb1, int64_t K1, void* h, int64_t ldh,
+                                     void* g_out, void* u_out, int64_t ldgu, int64_t M,
+                                     int64_t I, cudaStream_t stream) {
+  const char* what = "gemm_gateup_swiglu";
+  if (M < 0 || I < 0 || K0 <= 0 || K1 < 0 || M > (1 << 30) || I > (1 << 29) || K0 > (1 << 30) ||
+      K1 > (1 << 30))
+    return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
+  if (M == 0 || I == 0) return QB_OK;
+  if (!x || !w_gate || !w_up || !h || (K1 > 0 && (!u1 || !b1_gate || !b1_up)))
+    return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  if ((g_out == nullptr) != (u_out == nullptr))
+    return qb::fail(QB_ERR_INVALID, "%s: g and u outputs go together", what);
+  if (ldh < I || (g_out && ldgu < I)) return qb::fail(QB_ERR_INVALID, "%s: output row stride", what);
+  constexpr int kHalf = kBN / 2;
+  CUtensorMap m[4], mb0b, mb1b;
+  if (int s = map_operand(&m[0], x, ldx, false, M, K0, tcg::BM)) return s;
+  if (int s = map_operand(&m[1], w_gate, ldw, false, I, K0, kHalf)) return s;
+  if (int s = map_operand(&mb0b, w_up, ldw, false, I, K0, kHalf)) return s;
+  if (K1 > 0) {
+    if (int s = map_operand(&m[2], u1, ldu1, false, M, K1, tcg::BM)) return s;
+    if (int s = map_operand(&m[3], b1_gate, ldb1, false, I, K1, kHalf)) return s;
+    if (int s = map_operand(&mb1b, b1_up, ldb1, false, I, K1, kHalf)) return s;
+  } else {
+    m[2] = m[0];
+    m[3] = m[1];
+    mb1b = mb0b;
+  }
+  const int64_t halves = (I + kHalf - 1) / kHalf;
+  tcg::Problem pb{static_cast<int>(M), static_cast<int>(2 * halves * kHalf),
+                  static_cast<int>((K0 + 63) / 64), static_cast<int>((K1 + 63) / 64),
+                  static_cast<int>((M + 127) / 128), static_cast<int>(halves)};
+  const bool vec = qb::aligned16(h) && (ldh * 2) % 16 == 0 &&
+                   (!g_out || (qb::aligned16(g_out) && qb::aligned16(u_out) && (ldgu * 2) % 16 == 0));
+  EpiSwiGLU epi{static_cast<__nv_bfloat16*>(h), ldh, static_cast<__nv_bfloat16*>(g_out),
+                static_cast<__nv_bfloat16*>(u_out), ldgu, static_cast<int>(M), static_cast<int>(I),
+                vec};
+  using namespace tcg;
+  return launch<kTmaK, kTmaKDual, kTmaK, kTmaKDual, kBN>(m[0], m[1], m[2], m[3], pb, epi, stream,
+                                                         what, &mb0b, &mb1b);
 }

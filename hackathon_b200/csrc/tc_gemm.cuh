@@ -23,7 +23,11 @@
 
 namespace tcg {
 
-enum Src : int { kTmaK = 0, kTmaMN = 1 };
+// B sources: K-major or MN-major by TMA; kTmaKDual = K-major whose BN-row tile is two BN/2-row
+// halves from two tensors at the same row (the "top" map and the segment's second map): the
+// output tile's first BN/2 columns come from one weight, the last BN/2 from the other (a gate /
+// up pair computed by one GEMM).
+enum Src : int { kTmaK = 0, kTmaMN = 1, kTmaKDual = 2 };
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -67,6 +71,7 @@ template <int A0, int B0, int A1, int B1, int BN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mB0,
                const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mB1,
+               const __grid_constant__ CUtensorMap mB0b, const __grid_constant__ CUtensorMap mB1b,
                const Problem pb, Epi epi, int* err) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
@@ -135,7 +140,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
           const int asrc = seg1 ? A1 : A0, bsrc = seg1 ? B1 : B0;
           const CUtensorMap* ma = seg1 ? &mA1 : &mA0;
           const CUtensorMap* mb_ = seg1 ? &mB1 : &mB0;
-          tc::mbar_expect_tx(&full[stage], C::A_BYTES + (bsrc == kTmaK ? C::B_BYTES_K : C::B_BYTES_MN));
+          tc::mbar_expect_tx(&full[stage], C::A_BYTES + (bsrc == kTmaMN ? C::B_BYTES_MN : C::B_BYTES_K));
           if (asrc == kTmaK) {
             tc::tma_load_2d(sA, ma, &full[stage], k * BK, m0);
           } else {
@@ -144,6 +149,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
           }
           if (bsrc == kTmaK) {
             tc::tma_load_2d(sB, mb_, &full[stage], k * BK, n0);
+          } else if (bsrc == kTmaKDual) {
+            tc::tma_load_2d(sB, mb_, &full[stage], k * BK, n0 / 2);
+            tc::tma_load_2d(sB + (BN / 2) * 128, seg1 ? &mB1b : &mB0b, &full[stage], k * BK,
+                            n0 / 2);
           } else {
 #pragma unroll   // a partial last box (BN = 224) brings columns the MMA does not read
             for (int j = 0; j < (BN + 63) / 64; ++j)
@@ -232,7 +241,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
 template <int A0, int B0, int A1, int B1, int BN, class Epi>
 int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA1,
            const CUtensorMap& mB1, const Problem& pb, const Epi& epi, cudaStream_t stream,
-           const char* what) {
+           const char* what, const CUtensorMap* mB0b = nullptr,
+           const CUtensorMap* mB1b = nullptr) {
+  static_assert(B0 != kTmaKDual || BN % 2 == 0, "dual B splits the tile in halves");
   using C = Cfg<BN>;
   auto kernel = tc_gemm_kernel<A0, B0, A1, B1, BN, Epi>;
   static bool configured[64] = {};  // per instantiation and device
@@ -250,7 +261,10 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
   if (tiles == 0) return QB_OK;
   int grid = tc_host::sm_count();
   if (grid > tiles) grid = tiles;
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(mA0, mB0, mA1, mB1, pb, epi, err);
+  if ((B0 == kTmaKDual && !mB0b) || (B1 == kTmaKDual && !mB1b))
+    return qb::fail(QB_ERR_INVALID, "%s: dual B needs its second tensor map", what);
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
+                                              mB1b ? *mB1b : mB1, pb, epi, err);
   return qb::check_launch(what);
 }
 

@@ -12,12 +12,16 @@
 // Roles per CTA (one CTA per SM, persistent over the pair's tiles):
 //   warp 0      TMA producer: its halves of A and B; completion counted on the LEADER's full[s]
 //   warp 1      TMEM allocation (both CTAs); the leader's lane 0 issues the MMAs and commits each
-//               completion to the same barrier in both CTAs (empty[s], tfull[b])
+//               completion to the barrier of both CTAs (empty[s], tfull[b]) one after the other
 //   warps 2-5   epilogue of this CTA's 128 rows; arrive on the leader's tempty[b]
 // 6 stages of 32 KiB, accumulators double-buffered (2 x 256 TMEM columns). Every wait is bounded;
 // a wait that gives up raises the device error flag, every role drains out, and the two CTAs meet
-// at a cluster barrier before TMEM is released. No load multicasts (only the MMA-completion
-// arrive goes to both CTAs).
+// at a cluster barrier before TMEM is released. Nothing multicasts.
+//
+// Measured (16384 tokens, 7B projection shapes): correct, at ~0.72-0.77 PFLOP/s against the
+// one-CTA kernel's 1.33-1.42, with the tensor pipe busy 36 % of active cycles. Neither a
+// multicast completion commit nor CTA-scope waits changed that; the launcher keeps this kernel
+// off unless asked for.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -140,6 +144,10 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && leader) {
+      auto both = [&](uint64_t* bar) {          // commit to this barrier in both CTAs
+        tc::mma_commit_pair_to(tc::mapa(bar, 0));
+        tc::mma_commit_pair_to(tc::mapa(bar, 1));
+      };
       int s = 0;
       uint32_t ph = 0;
       int t = 0;
@@ -164,11 +172,11 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
                                    : tc::sdesc_sw128(sB + kk * 32, 16, 1024);
             tc::mma_bf16_pair(d, a, b, idesc, (kb | kk) != 0);
           }
-          tc::mma_commit_pair_both(&empty[s]);
+          both(&empty[s]);
           if (++s == kStages) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
-        tc::mma_commit_pair_both(&tfull[buf]);
+        both(&tfull[buf]);
       }
       tc::mma_commit_pair_to(tc::mapa(drain, 0));
       tc::mbar_wait_quiet(drain, 0);

@@ -86,6 +86,37 @@ def gemm2(a0, b0_t, a1, b1_t, out=None, out_dtype=torch.bfloat16, bias=None, res
     return out
 
 
+def gemm_gateup_swiglu(x, w_gate, w_up, lora_u=None, b1_gate=None, b1_up=None, save_gu=False):
+    """h = silu(g) * u for the gate/up pair in one tcgen05 GEMM (C-ABI qb_gemm_gateup_swiglu):
+    g = x @ w_gate.T (+ lora_u @ b1_gate.T), u = x @ w_up.T (+ lora_u @ b1_up.T), rounded to bf16
+    before the SwiGLU. Returns h, or (h, g, u) with save_gu. All bf16, row-major."""
+    _lib.require_cuda(x, w_gate, w_up, what="gemm_gateup_swiglu")
+    M, K0 = x.shape
+    I, K0w = w_gate.shape
+    if w_up.shape != w_gate.shape or K0w != K0 or w_up.stride(0) != w_gate.stride(0):
+        raise ValueError("gemm_gateup_swiglu: gate and up weights must match x and each other")
+    for t in (x, w_gate, w_up):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise TypeError("gemm_gateup_swiglu: bf16 row-major operands")
+    K1, up_, ldu1, bg, bu, ldb1 = 0, None, 0, None, None, 0
+    if lora_u is not None:
+        K1 = lora_u.shape[1]
+        if lora_u.shape[0] != M or b1_gate.shape != (I, K1) or b1_up.shape != (I, K1) or \
+                b1_up.stride(0) != b1_gate.stride(0):
+            raise ValueError("gemm_gateup_swiglu: LoRA operands do not match")
+        up_, ldu1, bg, bu, ldb1 = (lora_u.data_ptr(), lora_u.stride(0), b1_gate.data_ptr(),
+                                   b1_up.data_ptr(), b1_gate.stride(0))
+    h = torch.empty((M, I), dtype=torch.bfloat16, device=x.device)
+    g = u = None
+    if save_gu:
+        g, u = torch.empty_like(h), torch.empty_like(h)
+    _lib.call("qb_gemm_gateup_swiglu", x.data_ptr(), x.stride(0), w_gate.data_ptr(),
+              w_up.data_ptr(), w_gate.stride(0), K0, up_, ldu1, bg, bu, ldb1, K1, h.data_ptr(),
+              h.stride(0), _lib.ptr(g), _lib.ptr(u), I, M, I, _lib.stream(x.device),
+              work=(0, 2 * M * 2 * I * (K0 + K1)))
+    return (h, g, u) if save_gu else h
+
+
 def gemm_mask_acc(a, b_t, bits, scale, out):
     """out[M, N] (bf16, in place) += scale * mask .* (a @ b_t.T), mask from the dropout bit words
     `bits` [M, ceil(N/32)] int32 (C-ABI qb_gemm_bf16_mask_acc). a row-major [M, K]; b_t row-major

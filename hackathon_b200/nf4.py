@@ -212,10 +212,11 @@ DEQUANT_GEMM_MIN_TOKENS = 8192
 _WEIGHT_WS = {}
 
 
-def _weight_workspace(device, out_f, in_f):
-    """A bf16 [out_f, in_f] scratch for the transient weight, one per (device, stream): every
-    user of it is ordered on that stream, so one buffer serves all projections in turn."""
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+def _weight_workspace(device, out_f, in_f, slot=0):
+    """A bf16 [out_f, in_f] scratch for the transient weight, one per (device, stream, slot):
+    every user of it is ordered on that stream, so one buffer serves all projections in turn
+    (slot 1 for an op that needs two weights at once)."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream, slot)
     buf = _WEIGHT_WS.get(key)
     if buf is None or buf.numel() < out_f * in_f:
         buf = torch.empty(out_f * in_f, dtype=torch.bfloat16, device=device)

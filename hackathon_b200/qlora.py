@@ -63,6 +63,119 @@ def preset(name, **overrides):
 MASKS = {}
 
 
+def _dropped(x2, mod, p, seed):
+    """(dropout(x2) * scale, mask bits or None, scale) with the step's mask for (mod, seed): drawn
+    once (Philox, the reference's stream) and replayed from the bits afterwards."""
+    from .lora import dropout_apply, dropout_mask
+    if p <= 0:
+        return x2, None, 1.0
+    scale = 1.0 / (1.0 - p)
+    key = (id(mod), seed)
+    bits = MASKS.get(key)
+    if bits is None or bits.shape[0] != x2.shape[0]:
+        xd, bits = dropout_mask(x2, p, seed, scale)
+        MASKS[key] = bits
+    else:
+        xd = dropout_apply(x2, bits, scale)
+    return xd, bits, scale
+
+
+class GateUpSwiGLU(torch.autograd.Function):
+    """The MLP's gate and up projections and the SwiGLU between them, long-token path:
+
+        forward   xd_g, xd_u = dropout(x) (each projection's own mask); U_* = xd_* A_*^T
+                  h = silu(x W_g^T + U_g (s B_g)^T) * (x W_u^T + U_u (s B_u)^T)
+                                        (one tcgen05 GEMM, SwiGLU in its epilogue; g and u are
+                                         stored only when a backward will read them)
+        backward  dg, du = SwiGLU'(dh; g, u)
+                  dx = dg W_g + du W_u  (+= s mask_* .* (V_* A_*))      V_* = d* (s B_*)
+                  dA_* = V_*^T xd_*, dB_* = s d*^T U_*
+    The recompute keeps the two rebuilt bf16 weights for the backward of the same layer."""
+
+    @staticmethod
+    def forward(ctx, x, a_g, b_g, a_u, b_u, gate, up, p, seed_g, seed_u, save_gu):
+        from .gemm import gemm_gateup_swiglu
+        from .nf4 import _weight_workspace, dequantize_nf4
+        x2 = x.reshape(-1, x.shape[-1])
+        T, H = x2.shape
+        I, r = gate.out_features, a_g.shape[0]
+        xd_g, bits_g, scale = _dropped(x2, gate, p, seed_g)
+        xd_u, bits_u, _ = _dropped(x2, up, p, seed_u)
+        a16_g, a16_u = a_g.to(x.dtype), a_u.to(x.dtype)
+        u_g, u_u = xd_g @ a16_g.t(), xd_u @ a16_u.t()
+        lora_u = torch.cat([u_g, u_u], dim=1)                        # [T, 2r]
+        b1_g = torch.zeros((I, 2 * r), dtype=x.dtype, device=x.device)
+        b1_u = torch.zeros_like(b1_g)
+        b1_g[:, :r] = b_g * gate.scaling
+        b1_u[:, r:] = b_u * up.scaling
+        # Under activation checkpointing both passes must save the same tensors (the recompute's
+        # are unpacked in the first pass's slots): what the first pass would keep for the
+        # backward is an empty placeholder there, never None.
+        keep_w = save_gu and ctx.needs_input_grad[0]
+        ws = []
+        for slot, mod in enumerate((gate, up)):
+            w = torch.empty((I, H), dtype=torch.bfloat16, device=x.device) if keep_w \
+                else _weight_workspace(x.device, I, H, slot)
+            ws.append(dequantize_nf4(mod.packed, mod.quant_state, torch.bfloat16, out=w))
+        empty = torch.empty(0, dtype=torch.bfloat16, device=x.device)
+        kept = (ws[0], ws[1]) if keep_w else \
+            ((empty, empty) if ctx.needs_input_grad[0] else (None, None))
+        if save_gu:
+            h, g, u = gemm_gateup_swiglu(x2, ws[0], ws[1], lora_u, b1_g, b1_u, save_gu=True)
+        else:
+            # the activation checkpoint's first pass: what it saves is discarded and the
+            # recompute's tensors are unpacked in the same slots, so empty placeholders do
+            h = gemm_gateup_swiglu(x2, ws[0], ws[1], lora_u, b1_g, b1_u)
+            g = u = empty
+        ctx.save_for_backward(xd_g, xd_u, u_g, u_u, a_g, b_g, a_u, b_u, bits_g, bits_u,
+                              kept[0], kept[1], g, u)
+        ctx.gate, ctx.up, ctx.p, ctx.scale = gate, up, p, scale
+        ctx.seeds, ctx.shape = (seed_g, seed_u), x.shape
+        return h.view(*x.shape[:-1], I)
+
+    @staticmethod
+    def backward(ctx, dh):
+        from . import _lib
+        from .gemm import gemm2, gemm_mask_acc
+        from .nf4 import _weight_workspace, dequantize_nf4
+        (xd_g, xd_u, u_g, u_u, a_g, b_g, a_u, b_u, bits_g, bits_u, w_g, w_u, g, u) = \
+            ctx.saved_tensors
+        if g.numel() == 0:
+            raise RuntimeError("GateUpSwiGLU: backward through a forward that kept no g/u")
+        gate, up, p = ctx.gate, ctx.up, ctx.p
+        dh2 = dh.reshape(-1, dh.shape[-1]).to(g.dtype).contiguous()
+        dg, du = torch.empty_like(g), torch.empty_like(u)
+        _lib.call("qb_swiglu_bwd", dh2.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(),
+                  du.data_ptr(), _lib.tag(g.dtype), g.numel(), _lib.stream(g.device),
+                  work=(5 * g.numel() * g.element_size(), 0))
+        a16_g, a16_u = a_g.to(g.dtype), a_u.to(g.dtype)
+        v_g = dg @ (b_g * gate.scaling).to(g.dtype)                    # [T, r]
+        v_u = du @ (b_u * up.scaling).to(g.dtype)
+        for mod, seed in zip((gate, up), ctx.seeds):
+            MASKS.pop((id(mod), seed), None)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            I, H = dg.shape[1], xd_g.shape[1]
+            if w_g is None or w_g.numel() == 0:
+                w_g = dequantize_nf4(gate.packed, gate.quant_state, torch.bfloat16,
+                                     out=_weight_workspace(dg.device, I, H, 0))
+                w_u = dequantize_nf4(up.packed, up.quant_state, torch.bfloat16,
+                                     out=_weight_workspace(dg.device, I, H, 1))
+            dx = gemm2(dg, w_g.t(), du, w_u.t())                       # dg W_g + du W_u
+            if p > 0:
+                gemm_mask_acc(v_g, a16_g.t(), bits_g, ctx.scale, dx)
+                gemm_mask_acc(v_u, a16_u.t(), bits_u, ctx.scale, dx)
+            else:
+                dx.addmm_(v_g, a16_g)
+                dx.addmm_(v_u, a16_u)
+            dx = dx.view(ctx.shape)
+        da_g = (v_g.t() @ xd_g).float() if ctx.needs_input_grad[1] else None
+        db_g = (dg.t() @ u_g).float() * gate.scaling if ctx.needs_input_grad[2] else None
+        da_u = (v_u.t() @ xd_u).float() if ctx.needs_input_grad[3] else None
+        db_u = (du.t() @ u_u).float() * up.scaling if ctx.needs_input_grad[4] else None
+        return dx, da_g, db_g, da_u, db_u, None, None, None, None, None, None
+
+
 class LoRANF4Proj(torch.autograd.Function):
     """The whole QLoRA projection (and the residual add it feeds) on this package's kernels:
 
@@ -80,23 +193,9 @@ class LoRANF4Proj(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual):
-        from .lora import dropout_apply, dropout_mask
         from .nf4 import nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
-        scale = 1.0 / (1.0 - p) if p > 0 else 1.0
-        bits = None
-        if p > 0:
-            # the mask is drawn once per step (Philox, the reference's stream) and kept as bits:
-            # the checkpoint recompute reuses it instead of redrawing
-            key = (id(mod), seed)
-            bits = MASKS.get(key)
-            if bits is None or bits.shape[0] != x2.shape[0]:
-                xd, bits = dropout_mask(x2, p, seed, scale)
-                MASKS[key] = bits
-            else:
-                xd = dropout_apply(x2, bits, scale)
-        else:
-            xd = x2
+        xd, bits, scale = _dropped(x2, mod, p, seed)
         a16 = lora_a.to(x.dtype)
         sb16 = (lora_b * mod.scaling).to(x.dtype)
         u = xd @ a16.t()
@@ -204,7 +303,23 @@ class DecoderLayer(torch.nn.Module):
         self.up = LoRANF4Linear(H, I, False, s, device, gen)
         self.down = LoRANF4Linear(I, H, False, s, device, gen)
 
-    def forward(self, h, cos, sin, seed):
+    def mlp_fused_ok(self, x):
+        """The gate/up pair runs as one GEMM with the SwiGLU in its epilogue on the long-token
+        path (bf16, NF4 weights the fused kernels take, in_features a multiple of 64)."""
+        from .nf4 import fused_ok, uses_dequant_path
+        g, u = self.gate, self.up
+        return (g.fused and u.fused and fused_ok(x, g.quant_state) and fused_ok(x, u.quant_state)
+                and uses_dequant_path(x.numel() // x.shape[-1]) and g.in_features % 64 == 0
+                and g.lora_A.shape == u.lora_A.shape and g.p == u.p)
+
+    def forward(self, h, cos, sin, seed, ckpt_calls=None):
+        """ckpt_calls: a one-element list the activation checkpoint passes to both of its calls;
+        the first call's saved tensors are discarded, so it skips storing what only a backward
+        reads."""
+        first_of_checkpoint = False
+        if ckpt_calls is not None:
+            first_of_checkpoint = ckpt_calls[0] == 0
+            ckpt_calls[0] += 1
         s = self.shape
         B, S, _ = h.shape
         x = rmsnorm(h, self.ln1, s.eps)
@@ -216,7 +331,13 @@ class DecoderLayer(torch.nn.Module):
         a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
         h = self.o(a, seed + 3, residual=h)
         x = rmsnorm(h, self.ln2, s.eps)
-        m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
+        if self.mlp_fused_ok(x):
+            p = self.gate.p if self.training else 0.0
+            m = GateUpSwiGLU.apply(x, self.gate.lora_A, self.gate.lora_B, self.up.lora_A,
+                                   self.up.lora_B, self.gate, self.up, p, seed + 4, seed + 5,
+                                   torch.is_grad_enabled() and not first_of_checkpoint)
+        else:
+            m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
         return self.down(m, seed + 6, residual=h)
 
 
@@ -262,8 +383,12 @@ class QwenQLoRA(torch.nn.Module):
             # per (step, layer) seeds: a checkpoint recompute replays the same dropout masks
             seed = (self.step_seed * 1_000_003 + i * 7919) & 0x7FFFFFFF
             if self.checkpoint and self.training:
-                h = torch.utils.checkpoint.checkpoint(layer, h, cos, sin, seed,
-                                                      use_reentrant=False)
+                # the recompute replays the dropout masks from their bits, so it is
+                # deterministic; the first pass saves placeholders where only the recompute's
+                # tensors are ever read (shape check off for those)
+                h = torch.utils.checkpoint.checkpoint(layer, h, cos, sin, seed, [0],
+                                                      use_reentrant=False,
+                                                      determinism_check="none")
             else:
                 h = layer(h, cos, sin, seed)
         h = rmsnorm(h, self.norm, self.shape.eps)

@@ -212,6 +212,23 @@ int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,
                   int64_t ldc, int c_dtype, const float* bias, const void* residual, int64_t ldr,
                   int64_t M, int64_t N, cudaStream_t stream);
 
+/* The gate and up projections of a SwiGLU MLP in one GEMM, with the SwiGLU in its epilogue:
+ *   g = x w_gate^T + u1 b1_gate^T,  u = x w_up^T + u1 b1_up^T     (fp32 accumulation)
+ *   h[M, I] = silu(bf16(g)) * bf16(u)   (bf16; the arithmetic of qb_swiglu_fwd)
+ * and, when g_out / u_out are given (both or neither), bf16(g) and bf16(u) themselves ([M, I],
+ * row stride ldgu) for the backward. x [M, K0], w_gate / w_up [I, K0] (row stride ldw), all
+ * K-major bf16 with 16-byte-aligned rows. The LoRA terms ride as extra K (K1 = 2r, 0 for none):
+ * u1 = [dropout_g(x) A_g^T | dropout_u(x) A_u^T] [M, 2r], b1_gate = [s B_g | 0] and
+ * b1_up = [0 | s B_u] ([I, 2r], row stride ldb1). Each 256-wide output tile is 128 gate and the
+ * same 128 up features, the B tile loaded by TMA from both weights. Replaces
+ * solution/swiglu.py:68-81 (gate_proj, up_proj, then the SwiGLU kernel) with the weights the
+ * 4-bit path dequantised (solution/nf4.py:100-104) and the LoRA branches of solution/lora.py:172. */
+int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_gate, const void* w_up,
+                          int64_t ldw, int64_t K0, const void* u1, int64_t ldu1,
+                          const void* b1_gate, const void* b1_up, int64_t ldb1, int64_t K1,
+                          void* h, int64_t ldh, void* g_out, void* u_out, int64_t ldgu, int64_t M,
+                          int64_t I, cudaStream_t stream);
+
 /* C[M, N] (bf16, in place) += scale * mask .* (A[M, K] * B[N, K]^T): fp32 product, one rounding
  * per element, A K-major, B K- or MN-major; mask bit (n & 31) of bits[m * ldbits + n / 32] (the
  * words qb_dropout_mask records). The input gradient of a dropped-out LoRA branch,

@@ -152,3 +152,66 @@ def test_decoder_layer_matches_eager_oracle(cuda):
     gr = t["down"].lora_b.grad
     rel = (ga - gr).norm() / gr.norm()
     assert rel < 5e-2, float(rel)
+
+
+@pytest.mark.parametrize("p", [0.0, 0.1])
+def test_fused_gate_up_swiglu_matches_separate_projections(cuda, p):
+    """The MLP's gate/up pair as one GEMM with the SwiGLU in its epilogue (long-token path)
+    against the separate LoRANF4Proj projections + the SwiGLU kernel: forward bit for bit (same
+    bf16 g and u, same SwiGLU arithmetic), all gradients within bf16 tolerance, with and without
+    activation checkpointing of the layer."""
+    from hackathon_b200.nf4 import DEQUANT_GEMM_MIN_TOKENS
+    from hackathon_b200.qlora import DecoderLayer, preset
+    shape = preset("0.5b", layers=1, lora_dropout=p, lora_r=16, lora_alpha=32)
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    layer = DecoderLayer(shape, cuda, gen)
+    layer.train()
+    with torch.no_grad():
+        for mod in (layer.gate, layer.up):
+            mod.lora_B.normal_(0, 0.05, generator=gen)
+    T = DEQUANT_GEMM_MIN_TOKENS
+    x = torch.randn(1, T, shape.hidden, device=cuda, generator=gen).to(torch.bfloat16)
+    gy = torch.randn(1, T, shape.intermediate, device=cuda, generator=gen).to(torch.bfloat16)
+    from hackathon_b200.qlora import GateUpSwiGLU, MASKS
+    from hackathon_b200.swiglu import swiglu
+    assert layer.mlp_fused_ok(x)
+    outs = []
+    for fused in (True, False):
+        MASKS.clear()
+        for mod in (layer.gate, layer.up):
+            mod.lora_A.grad = mod.lora_B.grad = None
+        xi = x.clone().requires_grad_()
+        if fused:
+            m = GateUpSwiGLU.apply(xi, layer.gate.lora_A, layer.gate.lora_B, layer.up.lora_A,
+                                   layer.up.lora_B, layer.gate, layer.up, p, 40, 41, True)
+        else:
+            m = swiglu(layer.gate(xi, 40), layer.up(xi, 41))
+        m.backward(gy)
+        outs.append([m.detach(), xi.grad] + [t.grad.clone() for mod in (layer.gate, layer.up)
+                                            for t in (mod.lora_A, mod.lora_B)])
+    (m1, dx1, *g1), (m0, dx0, *g0) = outs
+    assert torch.equal(m1.view(torch.int16), m0.view(torch.int16))
+    torch.testing.assert_close(dx1.float(), dx0.float(), rtol=2e-2, atol=2e-2)
+    for a, b in zip(g1, g0):
+        rel = (a - b).norm() / b.norm()
+        assert rel < 2e-2, float(rel)
+
+
+def test_checkpointed_layer_with_fused_mlp_matches_uncheckpointed(cuda):
+    """A decoder layer at the long-token path (fused gate/up SwiGLU, placeholders saved in the
+    checkpoint's first pass) gives the same adapter gradients with and without checkpointing.
+    At this length the attention backward (cuDNN) accumulates dQ with atomics, so the two runs
+    agree to rounding, not bit for bit: compared by relative norm."""
+    from hackathon_b200.nf4 import DEQUANT_GEMM_MIN_TOKENS
+    from hackathon_b200.qlora import QwenQLoRA, preset, synthetic_batch
+    shape = preset("0.5b", layers=2, lora_dropout=0.1)
+    ids, labels = synthetic_batch(shape, 1, DEQUANT_GEMM_MIN_TOKENS, cuda, seed=4)
+    grads = []
+    for ckpt in (True, False):
+        model = QwenQLoRA(shape, cuda, seed=0, checkpoint=ckpt)
+        model.train()
+        loss, _ = model(ids, labels)
+        loss.backward()
+        grads.append(torch.cat([p.grad.flatten() for p in model.adapter_parameters()]))
+    rel = (grads[0] - grads[1]).norm() / grads[1].norm()
+    assert rel < 1e-3, float(rel)
