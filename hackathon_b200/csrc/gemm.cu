@@ -121,6 +121,71 @@ struct EpiSwiGLU {
   }
 };
 
+// Projection output with the rotate-half RoPE of its heads applied (q / k, head_dim 128): each
+// row is a token at position m % S; acc + bias is rounded to bf16 — the projection's output —
+// then rotated in fp32 with that position's cos/sin (qb::rope_rotate, the RoPE kernel's
+// arithmetic) and rounded again. A 256-wide tile holds two whole heads; chunk c (32 columns)
+// pairs with chunk c + 2 (dims d and d + 64 of the same head).
+struct EpiStoreRope {
+  __nv_bfloat16* c;
+  int64_t ldc;
+  int M, N, S;
+  const float* bias;            // [N] or null
+  const __nv_bfloat16* cosp;    // [S, 128], row stride css
+  const __nv_bfloat16* sinp;
+  int64_t css;
+  bool vec;
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
+    static_assert(BN % 128 == 0, "whole heads of 128 per tile");
+    const int m = m0 + row;
+    const bool live = m < M;
+    const __nv_bfloat16* cr = cosp + static_cast<int64_t>(live ? m % S : 0) * css;
+    const __nv_bfloat16* sr = sinp + static_cast<int64_t>(live ? m % S : 0) * css;
+#pragma unroll 1
+    for (int p = 0; p < BN / 64; ++p) {
+      const int ch = (p & 1) + (p >> 1) * 4;   // 0, 1, 4, 5: first halves of the two heads
+      float x1[32], x2[32];
+      tc::tmem_ld32(taddr + ch * 32, x1);
+      tc::tmem_ld32(taddr + (ch + 2) * 32, x2);
+      const int n1 = n0 + ch * 32, n2 = n1 + 64;
+      if (!live || n1 >= N) continue;
+      const int d = (ch & 1) * 32;             // dim of x1[0] within its head
+      float c1[32], c2[32], s1[32], s2[32];
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        qb::load8(cr + d + i, c1 + i);
+        qb::load8(cr + 64 + d + i, c2 + i);
+        qb::load8(sr + d + i, s1 + i);
+        qb::load8(sr + 64 + d + i, s2 + i);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = x1[i] + (bias ? __ldg(bias + n1 + i) : 0.f);
+        const float b = x2[i] + (bias ? __ldg(bias + n2 + i) : 0.f);
+        qb::rope_rotate(__bfloat162float(__float2bfloat16_rn(a)),
+                        __bfloat162float(__float2bfloat16_rn(b)), c1[i], c2[i], s1[i], s2[i],
+                        x1[i], x2[i]);
+      }
+      __nv_bfloat16* dst = c + static_cast<int64_t>(m) * ldc;
+      if (vec) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          qb::store8<__nv_bfloat16>(dst + n1 + i, x1 + i);
+          qb::store8<__nv_bfloat16>(dst + n2 + i, x2 + i);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          dst[n1 + i] = __float2bfloat16_rn(x1[i]);
+          dst[n2 + i] = __float2bfloat16_rn(x2[i]);
+        }
+      }
+    }
+  }
+};
+
 int map_operand(CUtensorMap* map, const void* p, int64_t ld, bool mn_major, int64_t rows,
                 int64_t k, int box_rows) {
   // K-major: [rows, k] with row stride ld; MN-major: stored [k, rows] with row stride ld
@@ -346,4 +411,40 @@ extern "C" int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_g
   using namespace tcg;
   return launch<kTmaK, kTmaKDual, kTmaK, kTmaKDual, kBN>(m[0], m[1], m[2], m[3], pb, epi, stream,
                                                          what, &mb0b, &mb1b);
+}
+
+extern "C" int qb_gemm2_rope_bf16(const void* A0, int64_t lda0, const void* B0, int64_t ldb0,
+                                  int64_t K0, const void* A1, int64_t lda1, const void* B1,
+                                  int64_t ldb1, int64_t K1, void* C, int64_t ldc,
+                                  const float* bias, const void* cos_, const void* sin_,
+                                  int64_t cs_stride_s, int64_t S, int64_t head_dim, int64_t M,
+                                  int64_t N, cudaStream_t stream) {
+  const char* what = "gemm2_rope_bf16";
+  if (M < 0 || N < 0 || K0 <= 0 || K1 < 0 || M > (1 << 30) || N > (1 << 30) || K0 > (1 << 30) ||
+      K1 > (1 << 30) || S <= 0)
+    return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
+  if (head_dim != 128 || N % 128)
+    return qb::fail(QB_ERR_UNSUPPORTED, "%s: heads of 128 dims, N a multiple of 128", what);
+  if (M == 0 || N == 0) return QB_OK;
+  if (!A0 || !B0 || !C || !cos_ || !sin_ || (K1 > 0 && (!A1 || !B1)))
+    return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  if (!qb::aligned16(cos_) || !qb::aligned16(sin_) || (cs_stride_s * 2) % 16)
+    return qb::fail(QB_ERR_INVALID, "%s: cos/sin rows must be 16-byte aligned", what);
+  CUtensorMap m[4];
+  if (int s = map_operand(&m[0], A0, lda0, false, M, K0, tcg::BM)) return s;
+  if (int s = map_operand(&m[1], B0, ldb0, false, N, K0, kBN)) return s;
+  if (K1 > 0) {
+    if (int s = map_operand(&m[2], A1, lda1, false, M, K1, tcg::BM)) return s;
+    if (int s = map_operand(&m[3], B1, ldb1, false, N, K1, kBN)) return s;
+  } else {
+    m[2] = m[0];
+    m[3] = m[1];
+  }
+  const tcg::Problem pb = problem(M, N, K0, K1);
+  EpiStoreRope epi{static_cast<__nv_bfloat16*>(C), ldc, static_cast<int>(M), static_cast<int>(N),
+                   static_cast<int>(S), bias, static_cast<const __nv_bfloat16*>(cos_),
+                   static_cast<const __nv_bfloat16*>(sin_), cs_stride_s,
+                   qb::aligned16(C) && (ldc * 2) % 16 == 0};
+  using namespace tcg;
+  return launch<kTmaK, kTmaK, kTmaK, kTmaK, kBN>(m[0], m[1], m[2], m[3], pb, epi, stream, what);
 }

@@ -88,6 +88,22 @@ __device__ __forceinline__ void store8(T* p, const float* in) {
   }
 }
 
+// Rotate-half RoPE on one (first half, second half) pair of a head, every product and sum
+// rounded on its own (no contraction into a fused multiply-add), so the RoPE kernel and the
+// projection epilogue that applies it produce the same bits:
+//   forward  o1 = x1 c1 - x2 s1,  o2 = x2 c2 + x1 s2;   backward  o1 = x1 c1 + x2 s2,  o2 = x2 c2 - x1 s1
+__device__ __forceinline__ void rope_rotate(float x1, float x2, float c1, float c2, float s1,
+                                            float s2, float& o1, float& o2) {
+  o1 = __fsub_rn(__fmul_rn(x1, c1), __fmul_rn(x2, s1));
+  o2 = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
+}
+
+__device__ __forceinline__ void rope_rotate_t(float x1, float x2, float c1, float c2, float s1,
+                                              float s2, float& o1, float& o2) {
+  o1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x2, s2));
+  o2 = __fsub_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s1));
+}
+
 // Rounds v through T's precision and back (identity for fp32).
 template <typename T>
 __device__ __forceinline__ float round_through(float v) {

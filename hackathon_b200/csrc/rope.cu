@@ -60,13 +60,10 @@ __global__ void rope_qk_kernel(const QT* __restrict__ q, const QT* __restrict__ 
     ld<QT, VEC>(src + half + d, x2);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
-      if (BACKWARD) {  // transpose of the rotation
-        o1[e] = x1[e] * c1[e] + x2[e] * s2[e];
-        o2[e] = x2[e] * c2[e] - x1[e] * s1[e];
-      } else {
-        o1[e] = x1[e] * c1[e] - x2[e] * s1[e];
-        o2[e] = x2[e] * c2[e] + x1[e] * s2[e];
-      }
+      if (BACKWARD)  // transpose of the rotation
+        qb::rope_rotate_t(x1[e], x2[e], c1[e], c2[e], s1[e], s2[e], o1[e], o2[e]);
+      else
+        qb::rope_rotate(x1[e], x2[e], c1[e], c2[e], s1[e], s2[e], o1[e], o2[e]);
     }
     st<OT, VEC>(dst + d, o1);
     st<OT, VEC>(dst + half + d, o2);

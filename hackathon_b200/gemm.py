@@ -86,6 +86,34 @@ def gemm2(a0, b0_t, a1, b1_t, out=None, out_dtype=torch.bfloat16, bias=None, res
     return out
 
 
+def gemm2_rope(a0, b0_t, a1, b1_t, cos, sin, bias=None):
+    """rope(bf16(a0 @ b0_t.T + a1 @ b1_t.T + bias)) for a q/k projection with heads of 128 dims
+    (C-ABI qb_gemm2_rope_bf16): row m is the token at position m % S of cos/sin [S, 128]. All
+    operands bf16 row-major; a1 may be None. Returns [M, N] bf16."""
+    tensors = (a0, b0_t, cos, sin) if a1 is None else (a0, b0_t, a1, b1_t, cos, sin)
+    _lib.require_cuda(*tensors, what="gemm2_rope")
+    M, K0 = a0.shape
+    N = b0_t.shape[0]
+    for t in tensors:
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise TypeError("gemm2_rope: bf16 row-major operands")
+    S = cos.shape[0]
+    if cos.shape != sin.shape or cos.shape[1] != 128 or cos.stride() != sin.stride():
+        raise ValueError("gemm2_rope: cos/sin [S, 128] with one layout")
+    K1, a1p, lda1, b1p, ldb1 = 0, None, 0, None, 0
+    if a1 is not None and a1.shape[1] > 0:
+        K1 = a1.shape[1]
+        a1p, lda1, b1p, ldb1 = a1.data_ptr(), a1.stride(0), b1_t.data_ptr(), b1_t.stride(0)
+    if bias is not None:
+        bias = bias.float().contiguous()
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=a0.device)
+    _lib.call("qb_gemm2_rope_bf16", a0.data_ptr(), a0.stride(0), b0_t.data_ptr(), b0_t.stride(0),
+              K0, a1p, lda1, b1p, ldb1, K1, out.data_ptr(), out.stride(0), _lib.ptr(bias),
+              cos.data_ptr(), sin.data_ptr(), cos.stride(0), S, 128, M, N,
+              _lib.stream(a0.device), work=(0, 2 * M * N * (K0 + K1)))
+    return out
+
+
 def gemm_gateup_swiglu(x, w_gate, w_up, lora_u=None, b1_gate=None, b1_up=None, save_gu=False):
     """h = silu(g) * u for the gate/up pair in one tcgen05 GEMM (C-ABI qb_gemm_gateup_swiglu):
     g = x @ w_gate.T (+ lora_u @ b1_gate.T), u = x @ w_up.T (+ lora_u @ b1_up.T), rounded to bf16

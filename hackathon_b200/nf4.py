@@ -232,13 +232,15 @@ def uses_dequant_path(tokens, path=None):
 
 
 def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=None,
-                   residual=None, weight_out=None):
+                   residual=None, weight_out=None, rope=None):
     """y = residual + x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T), bf16 in and out, fp32
     accumulation. path "fused": the tcgen05 kernel that rebuilds the NF4 weight in registers inside
     the GEMM; "dequant": W rebuilt into a transient bf16 copy, then the TMA-fed GEMM (bias, LoRA
     term and residual in its one accumulation / epilogue); None picks by token count
     (DEQUANT_GEMM_MIN_TOKENS). On the dequant path the copy goes to `weight_out` (bf16
     [out, in]) when given — a caller keeps it for the backward — else to a shared scratch.
+    rope = (cos, sin) [S, 128]: the output's heads get the rotate-half RoPE of their token's
+    position (row m = position m % S), in the GEMM epilogue on the dequant path.
     x [..., in] -> y [..., out]."""
     out_f, in_f = qs.shape
     x2 = _rows2d(x)
@@ -251,7 +253,13 @@ def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=No
         from .gemm import gemm2
         w = weight_out if weight_out is not None else _weight_workspace(x.device, out_f, in_f)
         dequantize_nf4(packed, qs, torch.bfloat16, out=w)
-        y = gemm2(x2, w, u2, lb, bias=bias, residual=res2)
+        if rope is not None:
+            if res2 is not None:
+                raise ValueError("nf4_linear_fwd: rope and residual do not combine")
+            from .gemm import gemm2_rope
+            y = gemm2_rope(x2, w, u2, lb, rope[0], rope[1], bias=bias)
+        else:
+            y = gemm2(x2, w, u2, lb, bias=bias, residual=res2)
         return y.view(*x.shape[:-1], out_f)
     y = torch.empty((T, out_f), dtype=torch.bfloat16, device=x.device)
     b = None if bias is None else bias.to(torch.bfloat16).contiguous()
@@ -259,6 +267,9 @@ def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=No
               out_f, _lib.ptr(b), _lib.ptr(u2), u2.stride(0) if u2 is not None else 0,
               _lib.ptr(lb), lb.stride(0) if lb is not None else 0, r, y.data_ptr(), y.stride(0),
               _lib.stream(x.device), work=(0, 2 * T * out_f * (in_f + r)))
+    if rope is not None:
+        from .rope import rope_rows
+        y = rope_rows(y, rope[0], rope[1])
     if res2 is not None:
         y += res2
     return y.view(*x.shape[:-1], out_f)

@@ -192,7 +192,7 @@ class LoRANF4Proj(torch.autograd.Function):
     rebuilds W (both live only from the layer's recompute to its backward)."""
 
     @staticmethod
-    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual):
+    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual, rope):
         from .nf4 import nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
         xd, bits, scale = _dropped(x2, mod, p, seed)
@@ -204,10 +204,11 @@ class LoRANF4Proj(torch.autograd.Function):
             w_keep = torch.empty((mod.out_features, mod.in_features), dtype=torch.bfloat16,
                                  device=x.device)
         y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16,
-                           residual=residual, weight_out=w_keep)
+                           residual=residual, weight_out=w_keep, rope=rope)
         ctx.save_for_backward(xd, u, lora_a, lora_b, bits, w_keep)
         ctx.mod, ctx.p, ctx.seed, ctx.scale, ctx.shape = mod, p, seed, scale, x.shape
         ctx.has_residual = residual is not None
+        ctx.rope = rope     # the position tables (constants, not activations)
         return y.view(*x.shape[:-1], y.shape[-1])
 
     @staticmethod
@@ -219,6 +220,9 @@ class LoRANF4Proj(torch.autograd.Function):
         g2 = g.reshape(-1, g.shape[-1])
         if g2.dtype != xd.dtype:
             g2 = g2.to(xd.dtype)
+        if ctx.rope is not None:      # through the RoPE first: its transpose
+            from .rope import rope_rows
+            g2 = rope_rows(g2, ctx.rope[0], ctx.rope[1], backward=True)
         a16 = lora_a.to(xd.dtype)
         sb16 = (lora_b * mod.scaling).to(xd.dtype)
         v = g2 @ sb16                                              # [T, r]
@@ -237,7 +241,7 @@ class LoRANF4Proj(torch.autograd.Function):
         da = (v.t() @ xd).float() if ctx.needs_input_grad[1] else None
         db = (g2.t() @ u).float() * mod.scaling if ctx.needs_input_grad[2] else None
         dres = g if ctx.has_residual and ctx.needs_input_grad[6] else None
-        return dx, da, db, None, None, None, dres
+        return dx, da, db, None, None, None, dres, None
 
 
 class LoRANF4Linear(torch.nn.Module):
@@ -266,16 +270,19 @@ class LoRANF4Linear(torch.nn.Module):
         self.in_features, self.out_features = in_features, out_features
         self.fused = True
 
-    def forward(self, x, seed, residual=None):
+    def forward(self, x, seed, residual=None, rope=None):
         """residual + this projection of x (the residual add of the decoder layer rides in the
-        projection's epilogue on the fused path)."""
+        projection's epilogue on the fused path); rope = (cos, sin) [S, 128] applies the
+        rotate-half RoPE to the output heads (fused path only)."""
         from .nf4 import fused_ok
         p = self.p if self.training else 0.0
         if self.fused and fused_ok(x, self.quant_state):
             if residual is not None and (residual.dtype != torch.bfloat16
                                          or residual.shape[:-1] != x.shape[:-1]):
                 raise ValueError("residual: bf16, one row per input row")
-            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual)
+            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual, rope)
+        if rope is not None:
+            raise ValueError("rope: only on the fused path")
         # the reference's composition: NF4Linear + DropoutCast + adapter GEMMs + ScaledAdd
         base = NF4Linear.apply(x, self.packed, self.quant_state, self.bias)
         xd = DropoutCast.apply(x, p, seed, x.dtype) if p > 0 else x
@@ -303,6 +310,14 @@ class DecoderLayer(torch.nn.Module):
         self.up = LoRANF4Linear(H, I, False, s, device, gen)
         self.down = LoRANF4Linear(I, H, False, s, device, gen)
 
+    def rope_fused_ok(self, x, cos):
+        """q and k take the RoPE in their GEMM epilogue: both on the fused path, heads of 128,
+        one position table for the batch, bf16 tables with 16-byte rows."""
+        from .nf4 import fused_ok
+        return (self.q.fused and self.k.fused and fused_ok(x, self.q.quant_state)
+                and fused_ok(x, self.k.quant_state) and self.shape.head_dim == 128
+                and cos.shape[0] == 1 and cos.dtype == torch.bfloat16 and cos.is_contiguous())
+
     def mlp_fused_ok(self, x):
         """The gate/up pair runs as one GEMM with the SwiGLU in its epilogue on the long-token
         path (bf16, NF4 weights the fused kernels take, in_features a multiple of 64)."""
@@ -323,10 +338,16 @@ class DecoderLayer(torch.nn.Module):
         s = self.shape
         B, S, _ = h.shape
         x = rmsnorm(h, self.ln1, s.eps)
-        q = self.q(x, seed + 0).view(B, S, s.heads, s.head_dim).transpose(1, 2)
-        k = self.k(x, seed + 1).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        if self.rope_fused_ok(x, cos):
+            # RoPE in the q / k projections' epilogue (tables [S, 128] of this sequence)
+            cs = (cos[0], sin[0])
+            q = self.q(x, seed + 0, rope=cs).view(B, S, s.heads, s.head_dim).transpose(1, 2)
+            k = self.k(x, seed + 1, rope=cs).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        else:
+            q = self.q(x, seed + 0).view(B, S, s.heads, s.head_dim).transpose(1, 2)
+            k = self.k(x, seed + 1).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+            q, k = CudaRoPE.apply(q, k, cos, sin)
         v = self.v(x, seed + 2).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
-        q, k = CudaRoPE.apply(q, k, cos, sin)
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
         h = self.o(a, seed + 3, residual=h)

@@ -17,6 +17,12 @@ from . import _common, _lib
 def _launch(q, k, cos, sin, q_out, k_out, backward):
     B, HQ, S, D = q.shape
     HK = k.shape[1]
+    # the kernel reads cos/sin at b * stride(0) + s * stride(1): the tables must cover every
+    # (b, s) it visits (a batch-broadcast table comes in expanded, batch stride 0)
+    for t in (cos, sin):
+        if t.dim() != 3 or t.shape[0] != B or t.shape[1] < S or t.shape[2] != D:
+            raise ValueError(f"rope: table {tuple(t.shape)} does not cover (B, S, D) = "
+                             f"({B}, {S}, {D})")
     if q.dtype != k.dtype or q_out.dtype != k_out.dtype or cos.dtype != sin.dtype:
         raise TypeError("rope: q/k, q_out/k_out and cos/sin must share dtypes")
     if cos.stride() != sin.stride():  # the kernel walks both with one set of strides
@@ -28,6 +34,23 @@ def _launch(q, k, cos, sin, q_out, k_out, backward):
               int(backward), _lib.stream(q.device),
               work=((HQ + HK) * B * S * D * (q.element_size() + q_out.element_size())
                     + 2 * S * D * cos.element_size(), 0))
+
+
+def rope_rows(x2, cos, sin, backward=False):
+    """RoPE (or its transpose) on a projection output laid out as rows of tokens: x2 [B*S, H*D]
+    bf16 with row m the token at position m % S, cos/sin [S, D]. Returns a new [B*S, H*D]."""
+    S, D = cos.shape
+    T, F = x2.shape
+    if cos.shape != sin.shape or T % S or F % D:
+        raise ValueError(f"rope_rows: rows {T} x {F} do not tile by cos/sin {tuple(cos.shape)}")
+    B = T // S
+    q = x2.contiguous().view(B, S, F // D, D).transpose(1, 2)          # (B, H, S, D) view
+    out = torch.empty((T, F), dtype=x2.dtype, device=x2.device)
+    qo = out.view(B, S, F // D, D).transpose(1, 2)
+    # one table for every sequence of the batch: batch stride 0, as CudaRoPE passes it
+    c, s = cos[None].expand(B, S, D), sin[None].expand(B, S, D)
+    _launch(q, q[:, :0], c, s, qo, qo[:, :0], backward)
+    return out
 
 
 def _unit_last(t):

@@ -212,6 +212,18 @@ int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,
                   int64_t ldc, int c_dtype, const float* bias, const void* residual, int64_t ldr,
                   int64_t M, int64_t N, cudaStream_t stream);
 
+/* A q or k projection with the rotate-half RoPE of its heads in the epilogue:
+ *   C[M, N] = rope(bf16(A0 B0^T + A1 B1^T + bias))   (bf16; heads of head_dim = 128 along N)
+ * row m is the token at position m % S (rows are batch-major tokens), rotated with
+ * cos[m % S, :] / sin[m % S, :] (bf16 [S, 128], row stride cs_stride_s) in the arithmetic of
+ * qb_rope_qk (forward). All operands K-major bf16; K1 = 0 for no LoRA term. Replaces the
+ * projection + solution/rope.py:82-104 (TritonRoPE forward) pair. */
+int qb_gemm2_rope_bf16(const void* A0, int64_t lda0, const void* B0, int64_t ldb0, int64_t K0,
+                       const void* A1, int64_t lda1, const void* B1, int64_t ldb1, int64_t K1,
+                       void* C, int64_t ldc, const float* bias, const void* cos_,
+                       const void* sin_, int64_t cs_stride_s, int64_t S, int64_t head_dim,
+                       int64_t M, int64_t N, cudaStream_t stream);
+
 /* The gate and up projections of a SwiGLU MLP in one GEMM, with the SwiGLU in its epilogue:
  *   g = x w_gate^T + u1 b1_gate^T,  u = x w_up^T + u1 b1_up^T     (fp32 accumulation)
  *   h[M, I] = silu(bf16(g)) * bf16(u)   (bf16; the arithmetic of qb_swiglu_fwd)

@@ -215,3 +215,44 @@ def test_checkpointed_layer_with_fused_mlp_matches_uncheckpointed(cuda):
         grads.append(torch.cat([p.grad.flatten() for p in model.adapter_parameters()]))
     rel = (grads[0] - grads[1]).norm() / grads[1].norm()
     assert rel < 1e-3, float(rel)
+
+
+@pytest.mark.parametrize("T", [256, 8192])
+def test_projection_with_rope_epilogue_matches_rope_kernel(cuda, T):
+    """q projection with the RoPE in its GEMM epilogue (long-token path) or right after the
+    fused kernel (short) against the projection followed by the RoPE kernel: forward bit for bit
+    (same rounding points, same rotation arithmetic), input and adapter gradients within bf16
+    tolerance (the backward applies the RoPE transpose before the projection's)."""
+    from hackathon_b200.qlora import MASKS, LoRANF4Linear, preset
+    from hackathon_b200.rope import CudaRoPE
+    from oracle import ops_ref
+    s = preset("0.5b", lora_r=16, lora_alpha=32, lora_dropout=0.1, heads=8, head_dim=128)
+    gen = torch.Generator(device=cuda).manual_seed(12)
+    in_f, heads = 896, 8
+    mod = LoRANF4Linear(in_f, heads * 128, True, s, cuda, gen)
+    with torch.no_grad():
+        mod.lora_B.normal_(0, 0.05, generator=gen)
+    S = 128 if T == 256 else 1024
+    cos, sin = ops_ref.qwen_cos_sin(1, S, 128, 1e6, torch.bfloat16)
+    cos, sin = cos.to(cuda), sin.to(cuda)
+    x = torch.randn(T // S, S, in_f, device=cuda, generator=gen).to(torch.bfloat16)
+    gy = torch.randn(T // S, heads, S, 128, device=cuda, generator=gen).to(torch.bfloat16)
+    outs = []
+    for fused_rope in (True, False):
+        MASKS.clear()
+        mod.lora_A.grad = mod.lora_B.grad = None
+        xi = x.clone().requires_grad_()
+        if fused_rope:
+            q = mod(xi, 5, rope=(cos[0], sin[0])).view(T // S, S, heads, 128).transpose(1, 2)
+        else:
+            q = mod(xi, 5).view(T // S, S, heads, 128).transpose(1, 2)
+            q, _ = CudaRoPE.apply(q, q[:, :0], cos, sin)
+        q.backward(gy)
+        outs.append((q.detach().contiguous(), xi.grad.float(), mod.lora_A.grad.clone(),
+                     mod.lora_B.grad.clone()))
+    (q1, dx1, da1, db1), (q0, dx0, da0, db0) = outs
+    assert torch.equal(q1.view(torch.int16), q0.view(torch.int16))
+    torch.testing.assert_close(dx1, dx0, rtol=2e-2, atol=2e-2)
+    for a, b in ((da1, da0), (db1, db0)):
+        rel = (a - b).norm() / b.norm()
+        assert rel < 2e-2, float(rel)
