@@ -42,7 +42,7 @@ WORKLOADS = {
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernel,
 # from ncu captures of each of its launch shapes in the step, averaged over the step's launch mix
 # (profiles/tc_gemm_kernel_dram_traffic_7b_projections.md). Keyed by --config.
-TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1031.9e6}}
+TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1793e6, "qb_gemm_gateup_swiglu": 4211e6}}
 
 # per-kernel roofline class: "hbm" (bytes) or "tensor" (flops)
 BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hbm",
@@ -52,7 +52,8 @@ BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hb
          "qb_nf4_linear_fwd": "tensor",
          "qb_nf4_linear_dgrad": "tensor", "qb_linear_ce_stats": "tensor",
          "qb_linear_ce_grad": "tensor", "qb_linear_ce_stats_logits": "tensor",
-         "qb_ce_grad_from_logits": "hbm", "qb_gemm_bf16_mask_acc": "hbm"}
+         "qb_ce_grad_from_logits": "hbm", "qb_gemm_bf16_mask_acc": "hbm",
+         "qb_gemm_gateup_swiglu": "tensor", "qb_gemm2_rope_bf16": "tensor"}
 
 
 def peaks():
@@ -177,7 +178,8 @@ def run_reference(args, rank, world):
 
 
 KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
-           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce", "mask_acc")
+           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce", "mask_acc",
+           "gateup_swiglu", "gemm2_dgrad_pair", "gemm2_rope")
 GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd")
 
 
@@ -237,6 +239,29 @@ def kernel_case(args):
         gate, up = rnd(T, fo), rnd(T, fo)
         fn = lambda: swiglu(gate, up)  # noqa: E731
         nbytes = 3 * T * fo * 2
+    elif name in ("gateup_swiglu", "gemm2_dgrad_pair"):
+        # the MLP pair at intermediate size --out-features: h = silu(g) * u in one GEMM (LoRA
+        # terms as extra K), or its input gradient dx = dg W_g + du W_u
+        from hackathon_b200.gemm import gemm_gateup_swiglu
+        wg, wu = rnd(fo, fi, s=0.02), rnd(fo, fi, s=0.02)
+        if name == "gateup_swiglu":
+            x, lu = rnd(T, fi), rnd(T, 2 * r)
+            bg, bu = rnd(fo, 2 * r, s=0.05), rnd(fo, 2 * r, s=0.05)
+            fn = lambda: gemm_gateup_swiglu(x, wg, wu, lu, bg, bu, save_gu=True)  # noqa
+            flops = 2 * T * 2 * fo * (fi + 2 * r)
+        else:
+            dg, du = rnd(T, fo), rnd(T, fo)
+            fn = lambda: gemm2(dg, wg.t(), du, wu.t())  # noqa: E731
+            flops = 2 * T * fi * 2 * fo
+    elif name == "gemm2_rope":
+        from hackathon_b200.gemm import gemm2_rope
+        w, x, u, sb = rnd(fo, fi, s=0.02), rnd(T, fi), rnd(T, r), rnd(fo, r, s=0.05)
+        pos = torch.arange(4096, device=dev, dtype=torch.float32)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=dev, dtype=torch.float32) / 128))
+        emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+        cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        fn = lambda: gemm2_rope(x, w, u, sb, cos, sin)  # noqa: E731
+        flops = 2 * T * fo * (fi + r)
     elif name == "mask_acc":
         # the backward LoRA input-gradient term: dx[T, in] += s * mask .* (V[T, r] A[r, in])
         from hackathon_b200.gemm import gemm_mask_acc
