@@ -50,6 +50,7 @@ _SIGNATURES = {
     "qb_gemm_bf16": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p],
     "qb_gemm2_bf16": [_p, _i64, _i32, _p, _i64, _i32, _i64, _p, _i64, _i32, _p, _i64, _i32, _i64,
                       _p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p],
+    "qb_selftest_bounded_wait": [_i64, _p],
     "qb_gemm2_rope_bf16": [_p, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _p, _i64, _p, _p,
                            _p, _i64, _i64, _i64, _i64, _i64, _p],
     "qb_gemm_gateup_swiglu": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _p,

@@ -66,21 +66,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete. Gives up (false) after kWaitLimitNs or
-// as soon as another role has raised the error flag.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Waits for the phase with the given parity to complete. Gives up (false) after limit_ns —
+// recording `code` in *err — or as soon as another role has raised the error flag.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         atomicCAS(err, 0, code);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_for(bar, parity, err, code, kWaitLimitNs);
 }
 
 // Bounded wait that only reports (used while draining after an error).

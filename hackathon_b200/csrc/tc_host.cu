@@ -103,6 +103,33 @@ int take_device_error(cudaStream_t stream) {
 
 }  // namespace tc_host
 
+namespace {
+
+constexpr int kProbeSite = 99;
+
+// One thread waits on an mbarrier that nothing ever arrives on: the bounded wait gives up after
+// limit_ns and records its site in the error flag, exactly as a stuck tensor-core kernel would.
+__global__ void bounded_wait_probe(int* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) tc::mbar_wait_for(&bar, 0, err, kProbeSite, limit_ns);
+}
+
+}  // namespace
+
+extern "C" int qb_selftest_bounded_wait(int64_t limit_ns, cudaStream_t stream) {
+  if (limit_ns < 1000000 || limit_ns > 2000000000)
+    return qb::fail(QB_ERR_INVALID, "selftest_bounded_wait: limit must be 1 ms .. 2 s");
+  int* err = tc_host::device_error_flag();
+  if (!err) return qb::fail(QB_ERR_CUDA, "selftest_bounded_wait: no device error flag");
+  bounded_wait_probe<<<1, 32, 0, stream>>>(err, static_cast<uint64_t>(limit_ns));
+  return qb::check_launch("selftest_bounded_wait");
+}
+
 extern "C" int qb_device_error(cudaStream_t stream) {
   const int v = tc_host::take_device_error(stream);
   if (v < 0) return qb::fail(QB_ERR_CUDA, "could not read the device error flag");

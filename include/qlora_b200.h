@@ -334,6 +334,12 @@ int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight, int64
  * QB_ERR_TIMEOUT when a kernel gave up one of its bounded waits (its output is then invalid). */
 int qb_device_error(cudaStream_t stream);
 
+/* Self-test of the failure path, no counterpart in the reference: launches one thread that waits
+ * (bounded, limit_ns between 1 ms and 2 s) on an mbarrier nothing arrives on, so the wait gives up
+ * and raises the device error flag as a stuck kernel would; qb_device_error then reports
+ * QB_ERR_TIMEOUT and the context stays usable. */
+int qb_selftest_bounded_wait(int64_t limit_ns, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

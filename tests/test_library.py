@@ -56,6 +56,9 @@ def test_error_message_plumbing_without_gpu():
     with pytest.raises(RuntimeError, match="residual row stride"):
         _lib.call("qb_gemm2_bf16", fake, 64, 0, fake, 64, 0, 64, None, 0, 0, None, 0, 0, 0,
                   fake, 128, 2, None, fake, 64, 128, 128, None)
+    # the failure-path self-test refuses limits outside 1 ms .. 2 s before launching anything
+    assert lib.qb_selftest_bounded_wait(10, None) == 1
+    assert lib.qb_selftest_bounded_wait(10_000_000_000, None) == 1
     with pytest.raises(RuntimeError, match="mask row stride"):
         _lib.call("qb_gemm_bf16_mask_acc", fake, 64, fake, 64, 1, fake, 3, 1.0, fake, 128, 128,
                   128, 64, None)
