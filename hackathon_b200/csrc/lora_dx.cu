@@ -144,7 +144,7 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
         bool ok = true;
         for (int kb = 0; kb < pb.nk; ++kb) {
           if (!tc::mbar_wait(&full[s], ph, err, 44)) { ok = false; break; }
-          tc::fence_after_sync();
+          // TMA -> MMA is ordered by the barrier's transaction count: no tcgen05 fence here
           const uint32_t sA = tc::smem_u32(ringAB + s * (kA + kB));
           const uint32_t sB = sA + kA;
 #pragma unroll

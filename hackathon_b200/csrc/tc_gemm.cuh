@@ -185,7 +185,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
           const bool seg1 = kb >= pb.nk0;
           const int asrc = seg1 ? A1 : A0, bsrc = seg1 ? B1 : B0;
           if (!tc::mbar_wait(&full[stage], phase, err, 3)) { ok = false; break; }
-          tc::fence_after_sync();
+          // TMA -> MMA is ordered by the barrier's transaction count: no tcgen05 fence here
           const uint32_t sA = tc::smem_u32(smem + stage * C::STAGE);
           const uint32_t sB = sA + C::A_BYTES;
           const uint32_t idesc = seg1 ? kIdesc1 : kIdesc0;

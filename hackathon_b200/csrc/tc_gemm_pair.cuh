@@ -159,7 +159,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!tc::mbar_wait(&full[s], ph, err, 23)) { ok = false; break; }
-          tc::fence_after_sync();
+          // TMA -> MMA is ordered by the barrier's transaction count: no tcgen05 fence here
           const bool seg1 = kb >= pb.nk0;
           const bool bmn = (seg1 ? B1 : B0) == kTmaMN;
           const uint32_t idesc = seg1 ? kIdesc1 : kIdesc0;
