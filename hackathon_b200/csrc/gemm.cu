@@ -205,14 +205,14 @@ int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
   return tcg::launch<A0, B0, A1, B1, BN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
 }
 
-// Which launches take the 2-SM kernel. It is correct (the GPU tests run with it forced on) but
-// measured at half the one-CTA kernel's throughput, so it is off unless QB_GEMM_PAIR=1 (K-major
-// A operands only); QB_GEMM_PAIR=2 takes it where there are enough 256 x 256 pair tiles to give
-// every SM pair one.
+// Which launches take the 2-SM kernel (K-major A operands): those with enough 256 x 256 pair
+// tiles to give every SM pair one (1.47-1.50 PFLOP/s against the one-CTA kernel's 1.32-1.38 at
+// the 7B projection shapes); smaller problems keep the one-CTA kernel's finer tiles. The
+// environment variable QB_GEMM_PAIR=0 / 1 turns it off / on regardless of size (A/B runs).
 bool use_pair(bool a_k_major, int64_t M, int64_t N) {
   static const int mode = [] {
     const char* e = std::getenv("QB_GEMM_PAIR");
-    return e ? std::atoi(e) : 0;
+    return e ? std::atoi(e) : -1;
   }();
   if (!a_k_major || mode == 0) return false;
   if (mode == 1) return true;
@@ -231,16 +231,20 @@ int pair_maps(CUtensorMap (&m)[4], const void* B0, int64_t ldb0, bool b0_mn, int
   return QB_OK;
 }
 
+// The pair kernel's problem: 256-row m-blocks, the same 256-wide n-blocks.
+tcg::Problem pair_problem(const tcg::Problem& pb) {
+  tcg::Problem pp = pb;
+  pp.num_m = (pb.M + 255) / 256;
+  return pp;
+}
+
 template <int B0, int B1, typename OutT>
 int run_pair(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
              const float* bias, const void* resid, int64_t ldr, bool vec, cudaStream_t s,
              const char* what) {
   EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias,
                         static_cast<const OutT*>(resid), ldr, vec};
-  tcg::Problem pp = pb;
-  pp.num_m = (pb.M + 255) / 256;
-  pp.num_n = (pb.N + tcp::BN - 1) / tcp::BN;
-  return tcp::launch<B0, B1>(m[0], m[1], m[2], m[3], pp, epi, s, what);
+  return tcp::launch<B0, B1>(m[0], m[1], m[2], m[3], pair_problem(pb), epi, s, what);
 }
 
 template <int A0, int B0, int A1, int B1>
@@ -409,6 +413,9 @@ extern "C" int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_g
                 static_cast<__nv_bfloat16*>(u_out), ldgu, static_cast<int>(M), static_cast<int>(I),
                 vec};
   using namespace tcg;
+  if (use_pair(true, M, 2 * halves * kHalf))   // the dual maps already have 128-row boxes
+    return tcp::launch<kTmaKDual, kTmaKDual>(m[0], m[1], m[2], m[3], pair_problem(pb), epi, stream,
+                                             what, &mb0b, &mb1b);
   return launch<kTmaK, kTmaKDual, kTmaK, kTmaKDual, kBN>(m[0], m[1], m[2], m[3], pb, epi, stream,
                                                          what, &mb0b, &mb1b);
 }
@@ -446,5 +453,14 @@ extern "C" int qb_gemm2_rope_bf16(const void* A0, int64_t lda0, const void* B0, 
                    static_cast<const __nv_bfloat16*>(sin_), cs_stride_s,
                    qb::aligned16(C) && (ldc * 2) % 16 == 0};
   using namespace tcg;
+  if (use_pair(true, M, N)) {
+    if (int s = map_operand(&m[1], B0, ldb0, false, N, K0, tcp::kHalfN)) return s;
+    if (K1 > 0) {
+      if (int s = map_operand(&m[3], B1, ldb1, false, N, K1, tcp::kHalfN)) return s;
+    } else {
+      m[3] = m[1];
+    }
+    return tcp::launch<kTmaK, kTmaK>(m[0], m[1], m[2], m[3], pair_problem(pb), epi, stream, what);
+  }
   return launch<kTmaK, kTmaK, kTmaK, kTmaK, kBN>(m[0], m[1], m[2], m[3], pb, epi, stream, what);
 }

@@ -212,9 +212,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 
 // ------------------------------------------------------------------------------------------
 // CTA pairs (cluster of 2) for the 2-SM MMA: the even CTA ("leader") issues the MMAs for both;
-// the other CTA signals the leader's barriers through their shared::cluster addresses, and the
-// leader commits each MMA completion to the barrier of either CTA by its shared::cluster address.
-// Nothing multicasts: every CTA loads its own tiles from this GPU's memory.
+// the other CTA's TMA loads complete on the leader's barriers (shared::cluster addresses), and the
+// leader's MMA completions arrive on the barriers of both CTAs. No load multicasts: every CTA
+// loads its own tiles from this GPU's memory.
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -296,6 +296,17 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, u
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at the same shared-memory offset in both CTAs of the pair once the pair
+// MMAs this thread issued so far complete: one commit signals both (an mbarrier arrive; no data
+// moves). Two separate commits, one per CTA, measured at half the pair's MMA throughput.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(static_cast<uint16_t>(0x3))
       : "memory");
 }
 

@@ -8,20 +8,22 @@
 // same shared-memory offsets, and the even CTA (the leader) issues M=256, N=256 MMAs that read
 // both CTAs' halves and accumulate each CTA's 128 rows in its own TMEM. Per SM that halves the
 // B bytes brought in and read by the tensor core per flop against the one-CTA 128 x 256 tile.
+// A dual B source (the gate / up pair) is natural here: CTA 0 loads its half from the first
+// weight and CTA 1 from the second, at the same rows.
 //
 // Roles per CTA (one CTA per SM, persistent over the pair's tiles):
-//   warp 0      TMA producer: its halves of A and B; completion counted on the LEADER's full[s]
+//   warp 0      TMA producer of this CTA's halves; both CTAs' loads complete on the LEADER's
+//               full[s], whose expected byte count the leader alone arms (for both CTAs)
 //   warp 1      TMEM allocation (both CTAs); the leader's lane 0 issues the MMAs and commits each
-//               completion to the barrier of both CTAs (empty[s], tfull[b]) one after the other
+//               stage's completion with one arrive on the same barrier in both CTAs (empty[s],
+//               tfull[b])
 //   warps 2-5   epilogue of this CTA's 128 rows; arrive on the leader's tempty[b]
+// Per k-block there is no signal from one CTA's threads to the other's: an earlier version in
+// which the other CTA armed its own bytes on the leader's barrier and the leader committed to each
+// CTA separately ran at half this throughput (0.72 against 1.47-1.50 PFLOP/s).
 // 6 stages of 32 KiB, accumulators double-buffered (2 x 256 TMEM columns). Every wait is bounded;
 // a wait that gives up raises the device error flag, every role drains out, and the two CTAs meet
-// at a cluster barrier before TMEM is released. Nothing multicasts.
-//
-// Measured (16384 tokens, 7B projection shapes): correct, at ~0.72-0.77 PFLOP/s against the
-// one-CTA kernel's 1.33-1.42, with the tensor pipe busy 36 % of active cycles. Neither a
-// multicast completion commit nor CTA-scope waits changed that; the launcher keeps this kernel
-// off unless asked for.
+// at a cluster barrier before TMEM is released. No load multicasts.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -57,6 +59,7 @@ template <int B0, int B1, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mB0,
                     const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mB1,
+                    const __grid_constant__ CUtensorMap mB0b, const __grid_constant__ CUtensorMap mB1b,
                     const Problem pb, Epi epi, int* err) {
   constexpr uint32_t kIdesc0 = tc::idesc_bf16(2 * BMC, BN, false, B0 == kTmaMN);
   constexpr uint32_t kIdesc1 = tc::idesc_bf16(2 * BMC, BN, false, B1 == kTmaMN);
@@ -74,7 +77,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
   const uint32_t rank = tc::cluster_rank();
   const bool leader = rank == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 2); tc::mbar_init(&empty[s], 1); }
+    for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { tc::mbar_init(&tfull[b], 1); tc::mbar_init(&tempty[b], 8); }
     tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
@@ -111,7 +114,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
         int mb, nb;
         pair_tile_blocks(pb, tile, mb, nb);
         const int m0 = mb * 2 * BMC + static_cast<int>(rank) * BMC;
-        const int nh = nb * BN + static_cast<int>(rank) * kHalfN;
+        const int nh = nb * BN + static_cast<int>(rank) * kHalfN;   // dual B: nb * kHalfN
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!tc::mbar_wait(&empty[s], ph ^ 1, err, 21)) { ok = false; break; }
@@ -119,13 +122,17 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
           uint8_t* sB = sA + kA;
           const bool seg1 = kb >= pb.nk0;
           const int k = (seg1 ? kb - pb.nk0 : kb) * BK;
+          const int bsrc = seg1 ? B1 : B0;
           const CUtensorMap* ma = seg1 ? &mA1 : &mA0;
-          const CUtensorMap* mb_ = seg1 ? &mB1 : &mB0;
+          const CUtensorMap* mb_ = seg1 ? (bsrc == tcg::kTmaKDual && rank ? &mB1b : &mB1)
+                                        : (bsrc == tcg::kTmaKDual && rank ? &mB0b : &mB0);
           const uint32_t bar = full_l + s * 8;
-          tc::mbar_expect_tx_cluster(bar, kStage);
+          if (leader) tc::mbar_expect_tx(&full[s], 2 * kStage);   // both CTAs' bytes
           tc::tma_load_2d_pair(sA, ma, bar, k, m0);
-          if ((seg1 ? B1 : B0) == kTmaK) {
+          if (bsrc == kTmaK) {
             tc::tma_load_2d_pair(sB, mb_, bar, k, nh);
+          } else if (bsrc == tcg::kTmaKDual) {
+            tc::tma_load_2d_pair(sB, mb_, bar, k, nb * kHalfN);
           } else {
             tc::tma_load_2d_pair(sB, mb_, bar, nh, k);
             tc::tma_load_2d_pair(sB + 8192, mb_, bar, nh + 64, k);
@@ -144,10 +151,7 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader)
     if (lane == 0 && leader) {
-      auto both = [&](uint64_t* bar) {          // commit to this barrier in both CTAs
-        tc::mma_commit_pair_to(tc::mapa(bar, 0));
-        tc::mma_commit_pair_to(tc::mapa(bar, 1));
-      };
+      auto both = [&](uint64_t* bar) { tc::mma_commit_pair_both(bar); };
       int s = 0;
       uint32_t ph = 0;
       int t = 0;
@@ -215,7 +219,10 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
 template <int B0, int B1, class Epi>
 int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA1,
            const CUtensorMap& mB1, const Problem& pb, const Epi& epi, cudaStream_t stream,
-           const char* what) {
+           const char* what, const CUtensorMap* mB0b = nullptr,
+           const CUtensorMap* mB1b = nullptr) {
+  if ((B0 == tcg::kTmaKDual && !mB0b) || (B1 == tcg::kTmaKDual && !mB1b))
+    return qb::fail(QB_ERR_INVALID, "%s: dual B needs its second tensor map", what);
   auto kernel = tc_gemm_pair_kernel<B0, B1, Epi>;
   static bool configured[64] = {};
   int dev = 0;
@@ -245,7 +252,8 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mA0, mB0, mA1, mB1, pb, epi, err);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
+                                     mB1b ? *mB1b : mB1, pb, epi, err);
   if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: launch: %s", what, cudaGetErrorString(e));
   return qb::check_launch(what);
 }
