@@ -232,13 +232,14 @@ def uses_dequant_path(tokens, path=None):
 
 
 def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=None,
-                   residual=None, weight_out=None, rope=None):
+                   residual=None, weight_out=None, rope=None, weight=None):
     """y = residual + x @ deq(W).T (+ bias) (+ u @ lora_b_scaled.T), bf16 in and out, fp32
     accumulation. path "fused": the tcgen05 kernel that rebuilds the NF4 weight in registers inside
     the GEMM; "dequant": W rebuilt into a transient bf16 copy, then the TMA-fed GEMM (bias, LoRA
     term and residual in its one accumulation / epilogue); None picks by token count
     (DEQUANT_GEMM_MIN_TOKENS). On the dequant path the copy goes to `weight_out` (bf16
-    [out, in]) when given — a caller keeps it for the backward — else to a shared scratch.
+    [out, in]) when given — a caller keeps it for the backward — else to a shared scratch;
+    `weight` is a copy the caller already rebuilt (dequant path, no rebuild here).
     rope = (cos, sin) [S, 128]: the output's heads get the rotate-half RoPE of their token's
     position (row m = position m % S), in the GEMM epilogue on the dequant path.
     x [..., in] -> y [..., out]."""
@@ -249,10 +250,12 @@ def nf4_linear_fwd(x, packed, qs, bias=None, u=None, lora_b_scaled=None, path=No
     u2 = None if u is None else _rows2d(u)
     lb = None if lora_b_scaled is None else lora_b_scaled.contiguous()
     res2 = None if residual is None else _rows2d(residual)
-    if uses_dequant_path(T, path):
+    if weight is not None or uses_dequant_path(T, path):
         from .gemm import gemm2
-        w = weight_out if weight_out is not None else _weight_workspace(x.device, out_f, in_f)
-        dequantize_nf4(packed, qs, torch.bfloat16, out=w)
+        w = weight
+        if w is None:
+            w = weight_out if weight_out is not None else _weight_workspace(x.device, out_f, in_f)
+            dequantize_nf4(packed, qs, torch.bfloat16, out=w)
         if rope is not None:
             if res2 is not None:
                 raise ValueError("nf4_linear_fwd: rope and residual do not combine")

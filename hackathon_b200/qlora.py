@@ -189,11 +189,13 @@ class LoRANF4Proj(torch.autograd.Function):
                   dA = V^T xd,  dB = s g^T U,  dh = g                   (fp32 adapter grads)
     Under activation checkpointing the recompute keeps xd and, on the long-token path, the bf16
     weight it rebuilt, so the backward of the same layer neither replays the mask on x nor
-    rebuilds W (both live only from the layer's recompute to its backward)."""
+    rebuilds W (both live only from the layer's recompute to its backward). output_dead: the
+    caller discards y (the recompute of a layer's last projection) - everything the backward
+    reads is built, the output GEMM is not run."""
 
     @staticmethod
-    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual, rope):
-        from .nf4 import nf4_linear_fwd, uses_dequant_path
+    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual, rope, output_dead=False):
+        from .nf4 import dequantize_nf4, nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
         xd, bits, scale = _dropped(x2, mod, p, seed)
         a16 = lora_a.to(x.dtype)
@@ -201,11 +203,17 @@ class LoRANF4Proj(torch.autograd.Function):
         u = xd @ a16.t()
         w_keep = None
         if ctx.needs_input_grad[0] and uses_dequant_path(x2.shape[0]):
-            w_keep = torch.empty((mod.out_features, mod.in_features), dtype=torch.bfloat16,
-                                 device=x.device)
-        y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16,
-                           residual=residual, weight_out=w_keep, rope=rope)
+            w_keep = dequantize_nf4(mod.packed, mod.quant_state, torch.bfloat16,
+                                    out=torch.empty((mod.out_features, mod.in_features),
+                                                    dtype=torch.bfloat16, device=x.device))
         ctx.save_for_backward(xd, u, lora_a, lora_b, bits, w_keep)
+        if output_dead:
+            # a checkpoint recompute's last projection: torch keeps only the recompute's saved
+            # tensors (and stops at the last of them), never its output
+            y = torch.empty((x2.shape[0], mod.out_features), dtype=x.dtype, device=x.device)
+        else:
+            y = nf4_linear_fwd(x2, mod.packed, mod.quant_state, mod.bias, u, sb16,
+                               residual=residual, weight=w_keep, rope=rope)
         ctx.mod, ctx.p, ctx.seed, ctx.scale, ctx.shape = mod, p, seed, scale, x.shape
         ctx.has_residual = residual is not None
         ctx.rope = rope     # the position tables (constants, not activations)
@@ -241,7 +249,7 @@ class LoRANF4Proj(torch.autograd.Function):
         da = (v.t() @ xd).float() if ctx.needs_input_grad[1] else None
         db = (g2.t() @ u).float() * mod.scaling if ctx.needs_input_grad[2] else None
         dres = g if ctx.has_residual and ctx.needs_input_grad[6] else None
-        return dx, da, db, None, None, None, dres, None
+        return dx, da, db, None, None, None, dres, None, None
 
 
 class LoRANF4Linear(torch.nn.Module):
@@ -270,17 +278,19 @@ class LoRANF4Linear(torch.nn.Module):
         self.in_features, self.out_features = in_features, out_features
         self.fused = True
 
-    def forward(self, x, seed, residual=None, rope=None):
+    def forward(self, x, seed, residual=None, rope=None, output_dead=False):
         """residual + this projection of x (the residual add of the decoder layer rides in the
         projection's epilogue on the fused path); rope = (cos, sin) [S, 128] applies the
-        rotate-half RoPE to the output heads (fused path only)."""
+        rotate-half RoPE to the output heads (fused path only); output_dead: the caller only
+        needs what the backward saves (a checkpoint recompute), the result is left unwritten."""
         from .nf4 import fused_ok
         p = self.p if self.training else 0.0
         if self.fused and fused_ok(x, self.quant_state):
             if residual is not None and (residual.dtype != torch.bfloat16
                                          or residual.shape[:-1] != x.shape[:-1]):
                 raise ValueError("residual: bf16, one row per input row")
-            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual, rope)
+            return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual, rope,
+                                     output_dead)
         if rope is not None:
             raise ValueError("rope: only on the fused path")
         # the reference's composition: NF4Linear + DropoutCast + adapter GEMMs + ScaledAdd
@@ -330,10 +340,12 @@ class DecoderLayer(torch.nn.Module):
     def forward(self, h, cos, sin, seed, ckpt_calls=None):
         """ckpt_calls: a one-element list the activation checkpoint passes to both of its calls;
         the first call's saved tensors are discarded, so it skips storing what only a backward
-        reads."""
-        first_of_checkpoint = False
+        reads; the second call (the recompute) has its output discarded, so the last
+        projection, whose output is the layer's output, builds only what its backward reads."""
+        first_of_checkpoint = recompute = False
         if ckpt_calls is not None:
             first_of_checkpoint = ckpt_calls[0] == 0
+            recompute = ckpt_calls[0] == 1
             ckpt_calls[0] += 1
         s = self.shape
         B, S, _ = h.shape
@@ -359,7 +371,7 @@ class DecoderLayer(torch.nn.Module):
                                    torch.is_grad_enabled() and not first_of_checkpoint)
         else:
             m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
-        return self.down(m, seed + 6, residual=h)
+        return self.down(m, seed + 6, residual=h, output_dead=recompute)
 
 
 class QwenQLoRA(torch.nn.Module):
