@@ -53,7 +53,11 @@ BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hb
          "qb_nf4_linear_dgrad": "tensor", "qb_linear_ce_stats": "tensor",
          "qb_linear_ce_grad": "tensor", "qb_linear_ce_stats_logits": "tensor",
          "qb_ce_grad_from_logits": "hbm", "qb_gemm_bf16_mask_acc": "hbm",
-         "qb_gemm_gateup_swiglu": "tensor", "qb_gemm2_rope_bf16": "tensor"}
+         "qb_gemm_gateup_swiglu": "tensor", "qb_gemm2_rope_bf16": "tensor",
+         "qb_dropout_mask": "hbm", "qb_dropout_apply": "hbm",
+         # integer-pipe work (Philox rounds), counted in mask elements drawn: no HBM or tensor
+         # roofline applies; on a side stream its events span the GEMMs it shares the SMs with
+         "qb_dropout_bits": "philox"}
 
 
 def peaks():
@@ -131,6 +135,9 @@ def kernel_table(summary, pk):
             gbs = d["bytes"] / (ms * 1e-3) / 1e9
             entry.update(achieved_gbs=round(gbs, 1), frac=round(gbs / pk["hbm_gbs"], 3),
                          bytes_per_launch=d["bytes"] // max(1, d["launches"]))
+        elif ms > 0 and entry["bound"] == "philox":
+            entry.update(achieved_gdraws_per_s=round(d["flops"] / (ms * 1e-3) / 1e9, 1),
+                         draws_per_launch=d["flops"] // max(1, d["launches"]))
         elif ms > 0:
             tf = d["flops"] / (ms * 1e-3) / 1e12
             # kernels timed inside a seconds-long step: the sustained (power-capped) GEMM peak
@@ -179,8 +186,9 @@ def run_reference(args, rank, world):
 
 KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
            "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce", "mask_acc",
-           "gateup_swiglu", "gemm2_dgrad_pair", "gemm2_rope")
-GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd")
+           "gateup_swiglu", "gemm2_dgrad_pair", "gemm2_rope", "dropout_bits")
+GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd",
+             "dropout_bits")
 
 
 def kernel_case(args):
@@ -204,7 +212,7 @@ def kernel_case(args):
         return (torch.randn(*shape, device=dev, generator=g) * s).to(torch.bfloat16)
 
     name = args.kernel
-    flops, nbytes = 0, 0
+    flops, nbytes, draws = 0, 0, 0
     if name in ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant"):
         packed, st = nf4m.quantize_nf4(rnd(fo, fi, s=0.02))
         w = nf4m.dequantize_nf4(packed, st, torch.bfloat16)
@@ -235,6 +243,12 @@ def kernel_case(args):
         else:
             fn = lambda: dropout_apply(x, bits, 1 / 0.95, out=xd)  # noqa: E731
         nbytes = 2 * T * fi * 2 + bits.numel() * 4
+    elif name == "dropout_bits":
+        # the mask alone (no data), full grid: Philox draws per second
+        from hackathon_b200.lora import dropout_bits
+        bits = dropout_bits(T, fi, 0.05, 1234, dev)
+        fn = lambda: dropout_bits(T, fi, 0.05, 1234, dev, out=bits)  # noqa: E731
+        draws = T * fi
     elif name == "swiglu_fwd":
         gate, up = rnd(T, fo), rnd(T, fo)
         fn = lambda: swiglu(gate, up)  # noqa: E731
@@ -309,6 +323,11 @@ def kernel_case(args):
     pk = peaks()
     line = {"kernel": name, "tokens": T, "in_features": fi, "out_features": fo, "ms": round(ms, 4),
             "graph": bool(args.graph)}
+    if draws:      # integer-pipe work: Philox draws per second, no HBM / tensor peak applies
+        line.update(achieved=round(draws / (ms * 1e-3) / 1e9, 1), unit="Gdraws/s",
+                    draws_per_launch=draws)
+        print(json.dumps(line), flush=True)
+        return
     if flops:
         tf = flops / (ms * 1e-3) / 1e12
         line.update(achieved=round(tf, 1), unit="TFLOP/s", peak=pk["bf16_tflops"],

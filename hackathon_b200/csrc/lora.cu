@@ -5,8 +5,14 @@
 // seed (low word k0, high word k1) with counter (offset, 0, 0, 0), offset = int32(row*cols+col).
 // The first output word w becomes a uniform in [0,1) as float(w >= 2^31 ? ~w : w) * 4.6566127342e-10
 // (w read as int32) — the stream Triton's tl.rand(seed, offset) draws, so the masks equal the
-// reference kernel's. Nothing is stored: the backward regenerates the mask from the seed.
+// reference kernel's. The mask depends on (seed, offset) only, never on the data: it can be drawn
+// ahead as bits (qb_dropout_bits) and applied later (qb_dropout_apply), or drawn and applied in
+// one pass that also records the bits (qb_dropout_mask).
 #include "qb_common.cuh"
+
+namespace tc_host {
+int sm_count();   // tc_host.cu: SMs of the current device (cached)
+}
 
 namespace {
 
@@ -202,6 +208,34 @@ dropout_apply_kernel(const IT* __restrict__ in, int64_t ins, const uint32_t* __r
   }
 }
 
+// Mask bits only, no data: one thread per 32-bit word (bit j = column 32w + j; bits past the
+// row's end are 0, as the ballot of dropout_mask_kernel leaves them). A fixed grid of a few
+// 256-thread blocks per SM with at most 32 registers a thread, so that the kernel can run on a
+// side stream beside a persistent GEMM that holds one CTA per SM (the GEMM's CTAs still fit:
+// its shared memory is untouched, and 2 x 256 x 32 registers leave 48K for it).
+__global__ void __launch_bounds__(kThreads, 8)
+dropout_bits_kernel(uint32_t* __restrict__ bits, int64_t words, int64_t rows, int64_t cols,
+                    uint32_t k0, uint32_t k1, int32_t thresh) {
+  const int64_t total = rows * words;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t row = t / words, w = t % words;
+    const int64_t c0 = w * 32;
+    const int n = cols - c0 < 32 ? static_cast<int>(cols - c0) : 32;
+    const uint32_t off0 = static_cast<uint32_t>(row * cols + c0);  // int32 wrap, as the reference
+    uint32_t word = 0;
+    if (n == 32) {
+#pragma unroll 8
+      for (int j = 0; j < 32; ++j)
+        word |= static_cast<uint32_t>(keep_of(philox_first_word(off0 + j, k0, k1), thresh)) << j;
+    } else {
+      for (int j = 0; j < n; ++j)
+        word |= static_cast<uint32_t>(keep_of(philox_first_word(off0 + j, k0, k1), thresh)) << j;
+    }
+    bits[t] = word;
+  }
+}
+
 unsigned grid_cap(int64_t work_items) {
   int64_t g = (work_items + kThreads - 1) / kThreads;
   if (g > 148 * 16) g = 148 * 16;
@@ -238,6 +272,25 @@ extern "C" int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stri
     });
   });
   return qb::check_launch("dropout_mask");
+}
+
+extern "C" int qb_dropout_bits(uint32_t* bits, int64_t rows, int64_t cols, uint64_t seed,
+                               float p, int ctas_per_sm, cudaStream_t stream) {
+  if (rows < 0 || cols < 0) return qb::fail(QB_ERR_INVALID, "dropout_bits: bad shape");
+  if (ctas_per_sm < 0 || ctas_per_sm > 8)
+    return qb::fail(QB_ERR_INVALID, "dropout_bits: ctas_per_sm must be 0..8");
+  if (p >= 1.0f) return qb::fail(QB_ERR_INVALID, "dropout_bits: p must be < 1");
+  if (rows == 0 || cols == 0) return QB_OK;
+  if (!bits) return qb::fail(QB_ERR_INVALID, "dropout_bits: null pointer");
+  const int32_t thresh = keep_threshold(p);
+  const int64_t words = (cols + 31) / 32;
+  int64_t grid = (rows * words + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(tc_host::sm_count()) * (ctas_per_sm ? ctas_per_sm : 8);
+  if (grid > cap) grid = cap;
+  dropout_bits_kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+      bits, words, rows, cols, static_cast<uint32_t>(seed & 0xffffffffu),
+      static_cast<uint32_t>(seed >> 32), thresh);
+  return qb::check_launch("dropout_bits");
 }
 
 extern "C" int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_stride,

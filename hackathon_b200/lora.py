@@ -49,6 +49,19 @@ def dropout_mask(x2, p, seed, scale, out_dtype=None):
     return out, bits
 
 
+def dropout_bits(rows, cols, p, seed, device, ctas_per_sm=0, out=None):
+    """The mask bits dropout_mask records for a [rows, cols] input (int32 [rows, ceil(cols/32)]),
+    drawn without the data: the mask depends on (seed, element index) only. ctas_per_sm caps
+    the grid (1..8 blocks per SM) so the kernel can share the SMs with a GEMM on another
+    stream; 0 fills the GPU."""
+    if out is None:
+        out = torch.empty((rows, (cols + 31) // 32), dtype=torch.int32, device=device)
+    _lib.call("qb_dropout_bits", out.data_ptr(), rows, cols, int(seed) & 0xFFFFFFFFFFFFFFFF,
+              float(p), int(ctas_per_sm), _lib.stream(torch.device(device)),
+              work=(out.numel() * 4, rows * cols))
+    return out
+
+
 def dropout_apply(x2, bits, scale, out=None, accumulate=False):
     """out = x2 * mask * scale (or out += ...) from recorded mask bits."""
     rows, cols = x2.shape

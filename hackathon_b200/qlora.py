@@ -62,6 +62,49 @@ def preset(name, **overrides):
 # QwenQLoRA.forward clears whatever a forward without backward left behind.
 MASKS = {}
 
+# Dropout masks drawn ahead on a side stream (one per device): the mask depends only on (seed,
+# element index), so the next layer's masks are drawn while this layer's tensor-core GEMMs run
+# (the Philox rounds load the integer pipes, which those GEMMs leave idle).
+_SIDE_STREAMS = {}
+MASK_CTAS_PER_SM = 2    # fixed grid beside the GEMMs' one CTA per SM (qb_dropout_bits)
+
+
+def _side_stream(device):
+    d = torch.device(device)
+    if d not in _SIDE_STREAMS:
+        _SIDE_STREAMS[d] = torch.cuda.Stream(device=d)
+    return _SIDE_STREAMS[d]
+
+
+def prefetch_masks(layer, seed, rows, device):
+    """Draws the dropout masks of `layer`'s seven projections (seeds seed + 0 .. 6, the seeds
+    DecoderLayer.forward gives them) into MASKS on the side stream and returns the event the
+    consumer's stream must wait on before the layer runs (None: nothing drawn). The bits are
+    allocated on the current stream and the side stream waits for it first, so memory reuse
+    stays ordered on the current stream."""
+    from .lora import dropout_bits
+    main = torch.cuda.current_stream(device)
+    todo = []
+    for k, name in enumerate(_PROJ):
+        mod = getattr(layer, name)
+        key = (id(mod), seed + k)
+        if (mod.training and mod.p > 0 and mod.fused and mod.in_features % 8 == 0
+                and key not in MASKS):
+            todo.append((key, mod, seed + k,
+                         torch.empty((rows, (mod.in_features + 31) // 32), dtype=torch.int32,
+                                     device=device)))
+    if not todo:
+        return None
+    side = _side_stream(device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        for key, mod, sd, bits in todo:
+            dropout_bits(rows, mod.in_features, mod.p, sd, device, MASK_CTAS_PER_SM, out=bits)
+            MASKS[key] = bits
+        ev = torch.cuda.Event()
+        ev.record(side)
+    return ev
+
 
 def _dropped(x2, mod, p, seed):
     """(dropout(x2) * scale, mask bits or None, scale) with the step's mask for (mod, seed): drawn
@@ -337,11 +380,13 @@ class DecoderLayer(torch.nn.Module):
                 and uses_dequant_path(x.numel() // x.shape[-1]) and g.in_features % 64 == 0
                 and g.lora_A.shape == u.lora_A.shape and g.p == u.p)
 
-    def forward(self, h, cos, sin, seed, ckpt_calls=None):
+    def forward(self, h, cos, sin, seed, ckpt_calls=None, prefetch=None):
         """ckpt_calls: a one-element list the activation checkpoint passes to both of its calls;
         the first call's saved tensors are discarded, so it skips storing what only a backward
         reads; the second call (the recompute) has its output discarded, so the last
-        projection, whose output is the layer's output, builds only what its backward reads."""
+        projection, whose output is the layer's output, builds only what its backward reads.
+        prefetch: called once, in the first pass only, as the o projection starts (the next
+        layer's dropout masks then overlap this layer's o / gate / up / down GEMMs)."""
         first_of_checkpoint = recompute = False
         if ckpt_calls is not None:
             first_of_checkpoint = ckpt_calls[0] == 0
@@ -362,6 +407,8 @@ class DecoderLayer(torch.nn.Module):
         v = self.v(x, seed + 2).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
+        if prefetch is not None and not recompute:
+            prefetch()
         h = self.o(a, seed + 3, residual=h)
         x = rmsnorm(h, self.ln2, s.eps)
         if self.mlp_fused_ok(x):
@@ -393,6 +440,7 @@ class QwenQLoRA(torch.nn.Module):
             head = torch.empty(shape.vocab, shape.hidden, device=dev, dtype=torch.bfloat16)
             self.lm_head = head.normal_(0.0, 0.02, generator=gen)
         self.checkpoint = checkpoint
+        self.mask_prefetch = True   # draw layer i+1's dropout masks beside layer i's GEMMs
         self._rope = {}
         self.step_seed = 0
 
@@ -409,23 +457,42 @@ class QwenQLoRA(torch.nn.Module):
 
     def forward(self, input_ids, labels, num_items_in_batch=None):
         B, S = input_ids.shape
+        dev = input_ids.device
+        if MASKS and dev in _SIDE_STREAMS:   # masks a side stream may still be writing
+            torch.cuda.current_stream(dev).wait_stream(_SIDE_STREAMS[dev])
         MASKS.clear()
-        cos, sin = self.rope_tables(S, input_ids.device)
+        cos, sin = self.rope_tables(S, dev)
         h = F.embedding(input_ids, self.embed)
+        seeds = [self.layer_seed(i) for i in range(len(self.layers))]
+        ready = [None] * len(self.layers)       # events of masks drawn ahead
+
+        def prefetcher(j):
+            if not (self.mask_prefetch and self.training and torch.is_grad_enabled()
+                    and j < len(self.layers)):
+                return None
+
+            def run():
+                ready[j] = prefetch_masks(self.layers[j], seeds[j], B * S, dev)
+            return run
+
         for i, layer in enumerate(self.layers):
-            # per (step, layer) seeds: a checkpoint recompute replays the same dropout masks
-            seed = (self.step_seed * 1_000_003 + i * 7919) & 0x7FFFFFFF
+            if ready[i] is not None:
+                torch.cuda.current_stream(dev).wait_event(ready[i])
             if self.checkpoint and self.training:
                 # the recompute replays the dropout masks from their bits, so it is
                 # deterministic; the first pass saves placeholders where only the recompute's
                 # tensors are ever read (shape check off for those)
-                h = torch.utils.checkpoint.checkpoint(layer, h, cos, sin, seed, [0],
-                                                      use_reentrant=False,
+                h = torch.utils.checkpoint.checkpoint(layer, h, cos, sin, seeds[i], [0],
+                                                      prefetcher(i + 1), use_reentrant=False,
                                                       determinism_check="none")
             else:
-                h = layer(h, cos, sin, seed)
+                h = layer(h, cos, sin, seeds[i], None, prefetcher(i + 1))
         h = rmsnorm(h, self.norm, self.shape.eps)
         return fused_causal_lm_loss(h, self.lm_head, labels, num_items_in_batch=num_items_in_batch)
+
+    def layer_seed(self, i):
+        """Per (step, layer) dropout seed; projection k of the layer draws with seed + k."""
+        return (self.step_seed * 1_000_003 + i * 7919) & 0x7FFFFFFF
 
     def adapter_parameters(self):
         return [p for p in self.parameters() if p.requires_grad]

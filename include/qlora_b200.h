@@ -154,6 +154,16 @@ int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stride, void* o
                     int out_dtype, int64_t out_row_stride, uint32_t* bits, int64_t rows,
                     int64_t cols, uint64_t seed, float p, float scale, cudaStream_t stream);
 
+/* The mask of qb_dropout_mask alone, no data read or written: bits[r * words + c / 32] bit
+ * (c % 32) = keep(r, c), words = ceil(cols / 32), bits past a row's end 0. The mask depends only
+ * on (seed, r, c), so it can be drawn ahead of the activations it will mask, e.g. on a side
+ * stream beside the tensor-core GEMMs (the Philox rounds are integer-pipe work). ctas_per_sm:
+ * 0 = as many 256-thread blocks as the work fills (up to 8 per SM); 1..8 = that many per SM at
+ * most, a fixed grid that leaves room for a GEMM's CTA on every SM. Replaces the mask half of
+ * solution/lora.py:29-46 (tl.rand(seed, offsets) > p). */
+int qb_dropout_bits(uint32_t* bits, int64_t rows, int64_t cols, uint64_t seed, float p,
+                    int ctas_per_sm, cudaStream_t stream);
+
 /* out = in * bit * scale (accumulate = 0) or out += in * bit * scale (accumulate = 1) with the
  * bits of qb_dropout_mask; cols a multiple of 8, 16-byte-aligned rows. */
 int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_stride, const uint32_t* bits,

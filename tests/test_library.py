@@ -62,6 +62,12 @@ def test_error_message_plumbing_without_gpu():
     with pytest.raises(RuntimeError, match="mask row stride"):
         _lib.call("qb_gemm_bf16_mask_acc", fake, 64, fake, 64, 1, fake, 3, 1.0, fake, 128, 128,
                   128, 64, None)
+    # mask bits drawn ahead: grid caps outside 0..8 and p >= 1 are refused before any launch
+    with pytest.raises(RuntimeError, match="ctas_per_sm"):
+        _lib.call("qb_dropout_bits", fake, 16, 64, 1, 0.1, 9, None)
+    with pytest.raises(RuntimeError, match="p must be < 1"):
+        _lib.call("qb_dropout_bits", fake, 16, 64, 1, 1.0, 2, None)
+    assert lib.qb_dropout_bits(None, 0, 64, 1, 0.1, 2, None) == 0     # empty: nothing to do
 
 
 @pytest.mark.parametrize("op", ["rmsnorm", "rope", "swiglu", "dropout", "dequant"])

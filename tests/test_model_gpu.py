@@ -103,6 +103,25 @@ def test_checkpoint_replays_dropout_masks(cuda):
     torch.testing.assert_close(grads[0], grads[1], rtol=1e-3, atol=1e-5)
 
 
+def test_masks_drawn_ahead_give_the_same_step(cuda):
+    """Dropout masks drawn ahead on the side stream (layer i+1's beside layer i's GEMMs) give
+    the same loss and adapter gradients as masks drawn inline, bit for bit."""
+    from hackathon_b200.qlora import QwenQLoRA, preset, synthetic_batch
+    shape = preset("0.5b", layers=3, lora_dropout=0.1)
+    ids, labels = synthetic_batch(shape, 1, 256, cuda, seed=5)
+    out = []
+    for ahead in (True, False):
+        model = QwenQLoRA(shape, cuda, seed=0)
+        model.mask_prefetch = ahead
+        model.train()
+        loss, _ = model(ids, labels)
+        loss.backward()
+        out.append((loss.detach(), torch.cat([p.grad.flatten()
+                                              for p in model.adapter_parameters()])))
+    assert torch.equal(out[0][0], out[1][0])
+    assert torch.equal(out[0][1], out[1][1])
+
+
 def test_decoder_layer_matches_eager_oracle(cuda):
     """One decoder layer (dropout off): GPU ops vs the eager CPU oracle with the same NF4
     bytes, bf16 activations; forward and the LoRA-A gradient within bf16 tolerance."""

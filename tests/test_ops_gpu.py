@@ -362,6 +362,49 @@ def test_recorded_mask_is_the_reference_stream(cuda, rows, cols):
         assert torch.equal(acc, expect.to(torch.bfloat16))   # one rounding, as the kernel
 
 
+@pytest.mark.parametrize("rows,cols,ctas", [(64, 1536, 0), (300, 3584, 2), (7, 40, 1),
+                                             (5, 33, 8), (16384, 3584, 2)])
+def test_bits_drawn_ahead_equal_recorded_mask(cuda, rows, cols, ctas):
+    """qb_dropout_bits (no data, any grid cap) writes the very words qb_dropout_mask records,
+    padding bits of a ragged last word included, and they are the reference's Philox mask."""
+    from hackathon_b200.lora import dropout_bits, dropout_mask
+    p, seed = 0.05, 20240607
+    x = torch.ones(rows, cols, device=cuda, dtype=torch.bfloat16)
+    _, want_bits = dropout_mask(x, p, seed, 1.0 / (1.0 - p))
+    bits = dropout_bits(rows, cols, p, seed, cuda, ctas_per_sm=ctas)
+    assert torch.equal(bits, want_bits)
+    for r in sorted({0, rows // 2, rows - 1}):
+        got = ((bits[r].cpu().numpy().view(np.uint32)[:, None] >> np.arange(32)) & 1).reshape(
+            -1)[:cols].astype(bool)
+        want = nf4_ref.philox_uniform(seed, r * cols + np.arange(cols)) > np.float32(p)
+        assert np.array_equal(got, want), r
+
+
+def test_bits_drawn_on_a_side_stream_beside_a_gemm(cuda):
+    """The prefetch pattern of the model: bits drawn on another stream while a tcgen05 GEMM
+    runs, the consumer stream waiting on an event; the result equals the inline mask."""
+    from hackathon_b200.gemm import gemm
+    from hackathon_b200.lora import dropout_bits, dropout_mask
+    rows, cols, p, seed = 16384, 3584, 0.05, 77
+    a = torch.randn(16384, 3584, device=cuda).to(torch.bfloat16)
+    b = torch.randn(3584, 3584, device=cuda).to(torch.bfloat16)
+    main = torch.cuda.current_stream(cuda)
+    side = torch.cuda.Stream(device=cuda)
+    bits = torch.empty((rows, cols // 32), dtype=torch.int32, device=cuda)
+    side.wait_stream(main)
+    c = gemm(a, b.t())
+    with torch.cuda.stream(side):
+        dropout_bits(rows, cols, p, seed, cuda, ctas_per_sm=2, out=bits)
+        ev = torch.cuda.Event()
+        ev.record(side)
+    c2 = gemm(a, b.t())
+    main.wait_event(ev)
+    _, want = dropout_mask(torch.ones(rows, cols, device=cuda, dtype=torch.bfloat16), p, seed,
+                           1.0 / (1.0 - p))
+    assert torch.equal(bits, want)
+    assert torch.equal(c, c2)
+
+
 @pytest.mark.parametrize("out_features", [1536, 256])
 def test_scaled_add_matches_peft(cuda, out_features):
     from hackathon_b200.lora import ScaledAdd
