@@ -186,7 +186,8 @@ def run_reference(args, rank, world):
 
 KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
            "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce", "mask_acc",
-           "gateup_swiglu", "gemm2_dgrad_pair", "gemm2_rope", "dropout_bits")
+           "gateup_swiglu", "gemm2_dgrad_pair", "gemm2_rope", "dropout_bits", "lora_xa",
+           "lora_xa_xd")
 GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd",
              "dropout_bits")
 
@@ -249,6 +250,14 @@ def kernel_case(args):
         bits = dropout_bits(T, fi, 0.05, 1234, dev)
         fn = lambda: dropout_bits(T, fi, 0.05, 1234, dev, out=bits)  # noqa: E731
         draws = T * fi
+    elif name in ("lora_xa", "lora_xa_xd"):
+        # U = dropout(x) A^T from x and the mask bits (rank r); _xd also stores xd
+        from hackathon_b200.lora import dropout_bits, lora_xa
+        x, a_l = rnd(T, fi), rnd(r, fi, s=0.05)
+        bits = dropout_bits(T, fi, 0.05, 1234, dev)
+        xd = torch.empty_like(x) if name == "lora_xa_xd" else None
+        fn = lambda: lora_xa(x, a_l, bits, 1 / 0.95, xd_out=xd)  # noqa: E731
+        nbytes = T * fi * 2 * (2 if xd is not None else 1) + bits.numel() * 4 + T * r * 2
     elif name == "swiglu_fwd":
         gate, up = rnd(T, fo), rnd(T, fo)
         fn = lambda: swiglu(gate, up)  # noqa: E731

@@ -62,6 +62,35 @@ def dropout_bits(rows, cols, p, seed, device, ctas_per_sm=0, out=None):
     return out
 
 
+def lora_xa(x2, a16, bits=None, scale=1.0, out=None, xd_out=None):
+    """U = dropout(x2) @ a16.T with the dropout taken from recorded mask bits inside the kernel
+    (xd = bf16(x * scale) where kept, else 0 — what dropout_apply writes); bits None: U = x2 @
+    a16.T. x2 [T, K] bf16, a16 [R, K] bf16 -> U [T, R] bf16 (into `out`, which may be a column
+    slice of a wider buffer). xd_out [T, K]: also stores xd (with bits)."""
+    _lib.require_cuda(x2, a16, what="lora_xa")
+    T, K = x2.shape
+    R = a16.shape[0]
+    if x2.dtype != torch.bfloat16 or a16.dtype != torch.bfloat16:
+        raise TypeError("lora_xa: bf16 input and adapter")
+    if out is None:
+        out = torch.empty((T, R), dtype=torch.bfloat16, device=x2.device)
+    _lib.call("qb_lora_xa", x2.data_ptr(), x2.stride(0), a16.data_ptr(), a16.stride(0),
+              _lib.ptr(bits), bits.stride(0) if bits is not None else 0, float(scale),
+              out.data_ptr(), out.stride(0), _lib.ptr(xd_out),
+              xd_out.stride(0) if xd_out is not None else 0, T, K, R, _lib.stream(x2.device),
+              work=(T * K * 2 * (2 if xd_out is not None else 1) + T * R * 2
+                    + (bits.numel() * 4 if bits is not None else 0), 0))
+    return out
+
+
+def lora_xa_ok(x2, a16):
+    """The shapes and layouts qb_lora_xa takes (else the caller composes dropout + GEMM)."""
+    R = a16.shape[0]
+    return (x2.dtype == torch.bfloat16 and x2.dim() == 2 and x2.stride(1) == 1
+            and x2.stride(0) % 8 == 0 and x2.data_ptr() % 16 == 0 and R % 32 == 0
+            and 32 <= R <= 256 and a16.is_contiguous() and a16.shape[1] % 8 == 0)
+
+
 def dropout_apply(x2, bits, scale, out=None, accumulate=False):
     """out = x2 * mask * scale (or out += ...) from recorded mask bits."""
     rows, cols = x2.shape

@@ -106,6 +106,44 @@ def prefetch_masks(layer, seed, rows, device):
     return ev
 
 
+def _mask_bits(x2, mod, p, seed):
+    """The step's mask bits for (mod, seed) over x2's shape: drawn ahead (prefetch_masks) or
+    drawn now (mask only, no data pass)."""
+    from .lora import dropout_bits
+    key = (id(mod), seed)
+    bits = MASKS.get(key)
+    if bits is None or bits.shape[0] != x2.shape[0]:
+        bits = dropout_bits(x2.shape[0], x2.shape[1], p, seed, x2.device)
+        MASKS[key] = bits
+    return bits
+
+
+# U = dropout(x) A^T in one kernel from x and the mask bits (qb_lora_xa); False composes
+# qb_dropout_apply (xd to HBM) with a GEMM instead - the same numbers up to accumulation order
+FUSED_ADAPTER_INPUT = True
+
+
+def _adapter_input(x2, mod, a16, p, seed, keep_xd, u_out=None):
+    """(xd, U = xd a16^T, bits, scale) of one projection with xd = dropout(x2) * scale: U comes
+    from x2 and the mask bits in one kernel (qb_lora_xa); xd is stored only when the backward
+    will read it (keep_xd), else an empty placeholder stands in its saved slot."""
+    from .lora import lora_xa, lora_xa_ok
+    if (not FUSED_ADAPTER_INPUT or not lora_xa_ok(x2, a16)
+            or (p > 0 and x2.shape[1] % 8)):
+        xd, bits, scale = _dropped(x2, mod, p, seed)
+        u = xd @ a16.t()
+        if u_out is not None:
+            u = u_out.copy_(u)
+        return xd, u, bits, scale
+    if p <= 0:
+        return x2, lora_xa(x2, a16, out=u_out), None, 1.0
+    scale = 1.0 / (1.0 - p)
+    bits = _mask_bits(x2, mod, p, seed)
+    xd = torch.empty_like(x2) if keep_xd else x2.new_empty(0)
+    u = lora_xa(x2, a16, bits, scale, out=u_out, xd_out=xd if keep_xd else None)
+    return xd, u, bits, scale
+
+
 def _dropped(x2, mod, p, seed):
     """(dropout(x2) * scale, mask bits or None, scale) with the step's mask for (mod, seed): drawn
     once (Philox, the reference's stream) and replayed from the bits afterwards."""
@@ -142,11 +180,12 @@ class GateUpSwiGLU(torch.autograd.Function):
         x2 = x.reshape(-1, x.shape[-1])
         T, H = x2.shape
         I, r = gate.out_features, a_g.shape[0]
-        xd_g, bits_g, scale = _dropped(x2, gate, p, seed_g)
-        xd_u, bits_u, _ = _dropped(x2, up, p, seed_u)
         a16_g, a16_u = a_g.to(x.dtype), a_u.to(x.dtype)
-        u_g, u_u = xd_g @ a16_g.t(), xd_u @ a16_u.t()
-        lora_u = torch.cat([u_g, u_u], dim=1)                        # [T, 2r]
+        lora_u = torch.empty((T, 2 * r), dtype=x.dtype, device=x.device)   # [U_g | U_u]
+        xd_g, u_g, bits_g, scale = _adapter_input(x2, gate, a16_g, p, seed_g, save_gu,
+                                                  u_out=lora_u[:, :r])
+        xd_u, u_u, bits_u, _ = _adapter_input(x2, up, a16_u, p, seed_u, save_gu,
+                                              u_out=lora_u[:, r:])
         b1_g = torch.zeros((I, 2 * r), dtype=x.dtype, device=x.device)
         b1_u = torch.zeros_like(b1_g)
         b1_g[:, :r] = b_g * gate.scaling
@@ -234,16 +273,18 @@ class LoRANF4Proj(torch.autograd.Function):
     weight it rebuilt, so the backward of the same layer neither replays the mask on x nor
     rebuilds W (both live only from the layer's recompute to its backward). output_dead: the
     caller discards y (the recompute of a layer's last projection) - everything the backward
-    reads is built, the output GEMM is not run."""
+    reads is built, the output GEMM is not run. keep_saved=False: what this forward saves is
+    discarded (an activation checkpoint's first pass), so xd is not stored (a placeholder keeps
+    its slot)."""
 
     @staticmethod
-    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual, rope, output_dead=False):
+    def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual, rope, output_dead=False,
+                keep_saved=True):
         from .nf4 import dequantize_nf4, nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
-        xd, bits, scale = _dropped(x2, mod, p, seed)
         a16 = lora_a.to(x.dtype)
+        xd, u, bits, scale = _adapter_input(x2, mod, a16, p, seed, keep_saved)
         sb16 = (lora_b * mod.scaling).to(x.dtype)
-        u = xd @ a16.t()
         w_keep = None
         if ctx.needs_input_grad[0] and uses_dequant_path(x2.shape[0]):
             w_keep = dequantize_nf4(mod.packed, mod.quant_state, torch.bfloat16,
@@ -292,7 +333,7 @@ class LoRANF4Proj(torch.autograd.Function):
         da = (v.t() @ xd).float() if ctx.needs_input_grad[1] else None
         db = (g2.t() @ u).float() * mod.scaling if ctx.needs_input_grad[2] else None
         dres = g if ctx.has_residual and ctx.needs_input_grad[6] else None
-        return dx, da, db, None, None, None, dres, None, None
+        return dx, da, db, None, None, None, dres, None, None, None
 
 
 class LoRANF4Linear(torch.nn.Module):
@@ -321,11 +362,13 @@ class LoRANF4Linear(torch.nn.Module):
         self.in_features, self.out_features = in_features, out_features
         self.fused = True
 
-    def forward(self, x, seed, residual=None, rope=None, output_dead=False):
+    def forward(self, x, seed, residual=None, rope=None, output_dead=False, keep_saved=True):
         """residual + this projection of x (the residual add of the decoder layer rides in the
         projection's epilogue on the fused path); rope = (cos, sin) [S, 128] applies the
         rotate-half RoPE to the output heads (fused path only); output_dead: the caller only
-        needs what the backward saves (a checkpoint recompute), the result is left unwritten."""
+        needs what the backward saves (a checkpoint recompute), the result is left unwritten;
+        keep_saved=False: the caller discards what the forward saves (a checkpoint's first
+        pass)."""
         from .nf4 import fused_ok
         p = self.p if self.training else 0.0
         if self.fused and fused_ok(x, self.quant_state):
@@ -333,7 +376,7 @@ class LoRANF4Linear(torch.nn.Module):
                                          or residual.shape[:-1] != x.shape[:-1]):
                 raise ValueError("residual: bf16, one row per input row")
             return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual, rope,
-                                     output_dead)
+                                     output_dead, keep_saved)
         if rope is not None:
             raise ValueError("rope: only on the fused path")
         # the reference's composition: NF4Linear + DropoutCast + adapter GEMMs + ScaledAdd
@@ -394,22 +437,27 @@ class DecoderLayer(torch.nn.Module):
             ckpt_calls[0] += 1
         s = self.shape
         B, S, _ = h.shape
+        keep = not first_of_checkpoint    # the first pass's saved tensors are discarded
         x = rmsnorm(h, self.ln1, s.eps)
         if self.rope_fused_ok(x, cos):
             # RoPE in the q / k projections' epilogue (tables [S, 128] of this sequence)
             cs = (cos[0], sin[0])
-            q = self.q(x, seed + 0, rope=cs).view(B, S, s.heads, s.head_dim).transpose(1, 2)
-            k = self.k(x, seed + 1, rope=cs).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+            q = self.q(x, seed + 0, rope=cs, keep_saved=keep).view(
+                B, S, s.heads, s.head_dim).transpose(1, 2)
+            k = self.k(x, seed + 1, rope=cs, keep_saved=keep).view(
+                B, S, s.kv_heads, s.head_dim).transpose(1, 2)
         else:
-            q = self.q(x, seed + 0).view(B, S, s.heads, s.head_dim).transpose(1, 2)
-            k = self.k(x, seed + 1).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+            q = self.q(x, seed + 0, keep_saved=keep).view(
+                B, S, s.heads, s.head_dim).transpose(1, 2)
+            k = self.k(x, seed + 1, keep_saved=keep).view(
+                B, S, s.kv_heads, s.head_dim).transpose(1, 2)
             q, k = CudaRoPE.apply(q, k, cos, sin)
-        v = self.v(x, seed + 2).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        v = self.v(x, seed + 2, keep_saved=keep).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
         if prefetch is not None and not recompute:
             prefetch()
-        h = self.o(a, seed + 3, residual=h)
+        h = self.o(a, seed + 3, residual=h, keep_saved=keep)
         x = rmsnorm(h, self.ln2, s.eps)
         if self.mlp_fused_ok(x):
             p = self.gate.p if self.training else 0.0
@@ -418,7 +466,7 @@ class DecoderLayer(torch.nn.Module):
                                    torch.is_grad_enabled() and not first_of_checkpoint)
         else:
             m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
-        return self.down(m, seed + 6, residual=h, output_dead=recompute)
+        return self.down(m, seed + 6, residual=h, output_dead=recompute, keep_saved=keep)
 
 
 class QwenQLoRA(torch.nn.Module):

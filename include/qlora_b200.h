@@ -164,6 +164,19 @@ int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stride, void* o
 int qb_dropout_bits(uint32_t* bits, int64_t rows, int64_t cols, uint64_t seed, float p,
                     int ctas_per_sm, cudaStream_t stream);
 
+/* The LoRA A product of a dropped-out input, from the input and the mask bits:
+ *     U[M, R] = xd[M, K] A[R, K]^T,   xd[m, k] = bf16(x[m, k] * scale) if mask bit set, else 0
+ * (bits: the words of qb_dropout_mask / qb_dropout_bits, row stride ldbits >= ceil(K / 32));
+ * bits = NULL: xd = x (no dropout). xd is formed in shared memory only; xd != NULL (with bits)
+ * also stores it ([M, K], row stride ldxd) for a backward that reads it. bf16 everywhere, fp32
+ * accumulation (tcgen05, TMEM); R a multiple of 32 in 32..256; x, A, xd row strides multiples
+ * of 8 elements, 16-byte-aligned bases; U rows 16-byte aligned (ldu a multiple of 8).
+ * Replaces the DropoutCast -> F.linear(xd, lora_A) pair of solution/lora.py:84-93 and the
+ * peft composition it serves (lora_A(dropout(x))). */
+int qb_lora_xa(const void* x, int64_t ldx, const void* a, int64_t lda, const uint32_t* bits,
+               int64_t ldbits, float scale, void* u, int64_t ldu, void* xd, int64_t ldxd,
+               int64_t M, int64_t K, int64_t R, cudaStream_t stream);
+
 /* out = in * bit * scale (accumulate = 0) or out += in * bit * scale (accumulate = 1) with the
  * bits of qb_dropout_mask; cols a multiple of 8, 16-byte-aligned rows. */
 int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_stride, const uint32_t* bits,

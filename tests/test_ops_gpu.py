@@ -405,6 +405,43 @@ def test_bits_drawn_on_a_side_stream_beside_a_gemm(cuda):
     assert torch.equal(c, c2)
 
 
+@pytest.mark.parametrize("T,K,R", [(300, 256, 64), (16384, 3584, 64), (129, 18944, 64),
+                                   (257, 40, 32), (64, 200, 128), (200, 136, 256),
+                                   (1000, 3584, 96)])
+def test_lora_xa_matches_dropout_then_product(cuda, T, K, R):
+    """qb_lora_xa: the stored xd equals qb_dropout_apply's bit for bit, and U equals the fp32
+    product of that xd with A rounded to bf16 (accumulation order aside); ragged row blocks,
+    ragged k-blocks, ranks 32..256."""
+    from hackathon_b200.lora import dropout_apply, dropout_bits, lora_xa
+    g = torch.Generator(device=cuda).manual_seed(T + K + R)
+    x = torch.randn(T, K, device=cuda, generator=g).to(torch.bfloat16)
+    a = (torch.randn(R, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
+    p, seed = 0.1, 31337
+    scale = 1.0 / (1.0 - p)
+    bits = dropout_bits(T, K, p, seed, cuda)
+    xd = torch.empty_like(x)
+    u = lora_xa(x, a, bits, scale, xd_out=xd)
+    want_xd = dropout_apply(x, bits, scale)
+    assert torch.equal(xd, want_xd)
+    ref = want_xd.float() @ a.float().t()
+    torch.testing.assert_close(u.float(), ref, rtol=1.6e-2, atol=1e-2)
+    assert torch.equal(lora_xa(x, a, bits, scale), u)        # without the xd store: same U
+
+
+def test_lora_xa_without_mask_and_into_a_column_slice(cuda):
+    """bits None: U = x A^T; U written into half of a [T, 2R] buffer (the gate / up pair's
+    layout), the other half untouched."""
+    from hackathon_b200.lora import lora_xa
+    T, K, R = 777, 512, 64
+    x = torch.randn(T, K, device=cuda).to(torch.bfloat16)
+    a = (torch.randn(R, K, device=cuda) / K ** 0.5).to(torch.bfloat16)
+    buf = torch.full((T, 2 * R), 7.0, device=cuda, dtype=torch.bfloat16)
+    lora_xa(x, a, out=buf[:, R:])
+    torch.testing.assert_close(buf[:, R:].float(), x.float() @ a.float().t(), rtol=1.6e-2,
+                               atol=1e-2)
+    assert torch.all(buf[:, :R] == 7.0)
+
+
 @pytest.mark.parametrize("out_features", [1536, 256])
 def test_scaled_add_matches_peft(cuda, out_features):
     from hackathon_b200.lora import ScaledAdd
