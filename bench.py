@@ -60,6 +60,16 @@ BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hb
          "qb_dropout_bits": "philox"}
 
 
+_T0 = time.monotonic()
+
+
+def _phase(msg):
+    """Progress of the run on stderr (seconds since start), so a run that is stopped early
+    still shows which phase it was in; stdout keeps the one JSON line."""
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(f"bench.py [{time.monotonic() - _T0:7.1f} s] {msg}", file=sys.stderr, flush=True)
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -397,6 +407,7 @@ def main():
     batch = args.batch or batch
     seq = args.seq or seq
     shape = preset(args.config)
+    _phase(f"building the {shape.name} model (NF4 quantisation on the GPU)")
     model = QwenQLoRA(shape, dev, seed=0)
     opt = make_optimizer(model)
     sync = AdapterGradSync(model.adapter_parameters()) if world > 1 else None
@@ -412,9 +423,11 @@ def main():
         if world > 1:
             dist.barrier()
 
+    _phase(f"{args.warmup} warm-up steps")
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        _phase(f"warm-up step {i} done")
 
     if args.profile_step:
         # every kernel of one step (ours, cuDNN, cuBLAS, torch) with its device time, from
@@ -436,6 +449,7 @@ def main():
             dist.destroy_process_group()
         return
 
+    _phase(f"timing {args.steps} steps")
     # ---- timed region: K steps, inputs resident in HBM (working set >> 126 MB L2)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -455,12 +469,14 @@ def main():
     tokens_per_step = batch * seq * world
     value = tokens_per_step / (ms * 1e-3)
 
+    _phase(f"{ms:.1f} ms/step; one instrumented step")
     # ---- per-kernel device times inside one step (events around every C-ABI call)
     barrier()
     with _lib.KernelTimer() as kt:
         step(0)
     ksum = kt.summary()
 
+    _phase("end-to-end steps through train_step")
     # ---- end to end through the public API: pinned host inputs copied in, loss read back
     host = [(ids.cpu().pin_memory(), lb.cpu().pin_memory()) for ids, lb in data]
     h2d = sum(x.numel() * x.element_size() for x in host[0])
@@ -512,7 +528,9 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        _phase("CPU baseline sample")
         cpu = cpu_baseline(shape, args.cpu_tokens)
+        _phase("CPU baseline done")
 
     if rank == 0:
         line = {

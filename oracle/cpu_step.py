@@ -102,9 +102,24 @@ class CpuDecoderLayer(torch.nn.Module):
         return h + self.down(m)
 
 
+def usable_cores():
+    """Host cores this process may run on: the affinity mask, capped by a cgroup v2 CPU quota
+    (a container's os.cpu_count() reports the whole machine; oversubscribing a quota makes
+    the thread pools stall)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    try:
+        with open("/sys/fs/cgroup/cpu.max") as f:
+            quota, period = f.read().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, int(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n or 1)
+
+
 def time_sample(shape, tokens=128, threads=None, repeats=1, seed=0):
     """(tokens/s scaled to the whole model, description dict) of the eager CPU path."""
-    threads = threads or os.cpu_count() or 1
+    threads = threads or usable_cores()
     torch.set_num_threads(threads)
     rng = np.random.default_rng(seed)
     torch.manual_seed(seed)
