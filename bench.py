@@ -70,6 +70,24 @@ def _phase(msg):
         print(f"bench.py [{time.monotonic() - _T0:7.1f} s] {msg}", file=sys.stderr, flush=True)
 
 
+# How many times a warm-up step, the timed steps, the instrumented step or the end-to-end steps
+# are repeated after a tensor-core kernel gave up a bounded wait in them (a run with a raised
+# device error flag is never measured).
+MAX_REPEATS = 3
+
+
+def fail(args, world, where, discarded):
+    """Every attempt at `where` raised the device error flag: no measurement, say why."""
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"metric": METRIC, "value": None, "unit": "tokens/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup,
+                          "error": f"{where}: a tensor-core kernel gave up a bounded wait in "
+                                   f"every attempt",
+                          "discarded_runs": discarded}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -423,11 +441,38 @@ def main():
         if world > 1:
             dist.barrier()
 
+    lib = _lib.load()
+    discarded = []    # runs in which a tensor-core kernel gave up a bounded wait
+
+    def device_error(where):
+        """Reads (and clears) the tensor-core kernels' error flag after the current stream's work,
+        agreed over the ranks so that every rank takes the same next step. A raised flag means a
+        kernel gave up a bounded wait and left its work undone: the run that raised it is not
+        measured, it is repeated."""
+        rc = lib.qb_device_error(_lib.stream(dev))
+        msg = lib.qb_last_error().decode(errors="replace") if rc else None
+        if world > 1:
+            f = torch.tensor([1 if rc else 0], device=dev)
+            dist.all_reduce(f, op=dist.ReduceOp.MAX)
+            if int(f[0]) and msg is None:
+                msg = "raised on another rank"
+        if msg:
+            discarded.append({"where": where, "error": msg})
+            _phase(f"{where}: {msg} - discarded, repeated")
+        return msg
+
     _phase(f"{args.warmup} warm-up steps")
-    for i in range(args.warmup):
+    done, i = 0, 0
+    while done < args.warmup:
+        if i >= args.warmup + MAX_REPEATS:
+            fail(args, world, "warm-up", discarded)
+            return
         step(i)
         torch.cuda.synchronize()
-        _phase(f"warm-up step {i} done")
+        if device_error(f"warm-up step {i}") is None:
+            done += 1
+            _phase(f"warm-up step {i} done")
+        i += 1
 
     if args.profile_step:
         # every kernel of one step (ours, cuDNN, cuBLAS, torch) with its device time, from
@@ -452,15 +497,21 @@ def main():
     _phase(f"timing {args.steps} steps")
     # ---- timed region: K steps, inputs resident in HBM (working set >> 126 MB L2)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        start.record()
-        for i in range(args.steps):
-            step(i)
-        end.record()
-        torch.cuda.synchronize()
-        barrier()
+    for attempt in range(MAX_REPEATS + 1):
+        with ClockSampler(local) as clocks:
+            barrier()
+            torch.cuda.synchronize()
+            start.record()
+            for i in range(args.steps):
+                step(i)
+            end.record()
+            torch.cuda.synchronize()
+            barrier()
+        if device_error(f"timed steps (attempt {attempt})") is None:
+            break
+    else:
+        fail(args, world, "timed steps", discarded)
+        return
     ms = start.elapsed_time(end) / args.steps
     t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -471,29 +522,41 @@ def main():
 
     _phase(f"{ms:.1f} ms/step; one instrumented step")
     # ---- per-kernel device times inside one step (events around every C-ABI call)
-    barrier()
-    with _lib.KernelTimer() as kt:
-        step(0)
-    ksum = kt.summary()
+    for attempt in range(MAX_REPEATS + 1):
+        barrier()
+        with _lib.KernelTimer() as kt:
+            step(0)
+        ksum = kt.summary()
+        if device_error(f"instrumented step (attempt {attempt})") is None:
+            break
+    else:
+        fail(args, world, "instrumented step", discarded)
+        return
 
     _phase("end-to-end steps through train_step")
     # ---- end to end through the public API: pinned host inputs copied in, loss read back
     host = [(ids.cpu().pin_memory(), lb.cpu().pin_memory()) for ids, lb in data]
     h2d = sum(x.numel() * x.element_size() for x in host[0])
-    barrier()
-    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.steps):
-        ids_h, lb_h = host[i % 2]
-        ids = ids_h.to(dev, non_blocking=True)
-        lb = lb_h.to(dev, non_blocking=True)
-        loss = train_step(model, opt, ids, lb, grad_sync=sync,
-                          num_items_in_batch=global_label_count(lb))
-        loss_value = float(loss.cpu())     # device -> host read of the step's result
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
+    for attempt in range(MAX_REPEATS + 1):
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(args.steps):
+            ids_h, lb_h = host[i % 2]
+            ids = ids_h.to(dev, non_blocking=True)
+            lb = lb_h.to(dev, non_blocking=True)
+            loss = train_step(model, opt, ids, lb, grad_sync=sync,
+                              num_items_in_batch=global_label_count(lb))
+            loss_value = float(loss.cpu())     # device -> host read of the step's result
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        if device_error(f"end-to-end steps (attempt {attempt})") is None:
+            break
+    else:
+        fail(args, world, "end-to-end steps", discarded)
+        return
     ems = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
     if world > 1:
         dist.all_reduce(ems, op=dist.ReduceOp.MAX)
@@ -549,6 +612,7 @@ def main():
             "kernels": table,
             "kernel_ms_per_step_ours": round(ours_ms, 2),
             "cpu_baseline": cpu,
+            "discarded_runs": discarded,
             "clocks": clocks.summary(),
             "peaks": pk,
         }

@@ -66,6 +66,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// How many failed try_waits pass between two looks at the error flag and the clock. Each failed
+// try_wait may sleep up to its 0.5 ms suspend hint, so a wait notices another role's (or an
+// earlier launch's) error within ~4 ms: after a give-up, the remaining launches of a step drain
+// in milliseconds each instead of stalling the stream for minutes.
+constexpr uint32_t kWaitCheckMask = 7u;
+
 // Waits for the phase with the given parity to complete. Gives up (false) after limit_ns —
 // recording `code` in *err — or as soon as another role has raised the error flag.
 __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code,
@@ -74,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, in
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0) {
+    if ((i & kWaitCheckMask) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
       if (globaltimer() - t0 > limit_ns) {
         atomicCAS(err, 0, code);
@@ -260,7 +266,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 255u) == 0) {
+    if ((i & kWaitCheckMask) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
       if (globaltimer() - t0 > kWaitLimitNs) {
         atomicCAS(err, 0, code);
