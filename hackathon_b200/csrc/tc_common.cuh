@@ -30,6 +30,21 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// Elapsed-time test of every bounded wait: limit_ns passed on %globaltimer AND at least
+// limit_ns / 2 cycles passed on this SM's free-running cycle counter. %globaltimer is kept by
+// the driver and may step forward when it is resynchronised; the cycle counter cannot jump, so
+// a timer step alone never makes a healthy wait give up. At any SM clock of 0.5 GHz or more the
+// cycle test holds by the time the timer test does, so the bound stays limit_ns.
+struct WaitClock {
+  uint64_t t0;
+  long long c0;
+  __device__ __forceinline__ WaitClock() : t0(globaltimer()), c0(clock64()) {}
+  __device__ __forceinline__ bool expired(uint64_t limit_ns) const {
+    return globaltimer() - t0 > limit_ns &&
+           static_cast<unsigned long long>(clock64() - c0) > limit_ns / 2;
+  }
+};
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -77,12 +92,12 @@ constexpr uint32_t kWaitCheckMask = 7u;
 __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code,
                                               uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const WaitClock clk;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & kWaitCheckMask) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > limit_ns) {
+      if (clk.expired(limit_ns)) {
         atomicCAS(err, 0, code);
         return false;
       }
@@ -96,9 +111,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // Bounded wait that only reports (used while draining after an error).
 __device__ __forceinline__ bool mbar_wait_quiet(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
+  const WaitClock clk;
   while (!mbar_try_wait(bar, parity))
-    if (globaltimer() - t0 > kWaitLimitNs / 16) return false;
+    if (clk.expired(kWaitLimitNs / 16)) return false;
   return true;
 }
 
@@ -263,12 +278,12 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err,
                                                   int code) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const WaitClock clk;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((i & kWaitCheckMask) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (clk.expired(kWaitLimitNs)) {
         atomicCAS(err, 0, code);
         return false;
       }
@@ -277,9 +292,9 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 __device__ __forceinline__ bool mbar_wait_cluster_quiet(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
+  const WaitClock clk;
   while (!mbar_try_wait_cluster(bar, parity))
-    if (globaltimer() - t0 > kWaitLimitNs / 16) return false;
+    if (clk.expired(kWaitLimitNs / 16)) return false;
   return true;
 }
 
