@@ -76,6 +76,22 @@ def _phase(msg):
 MAX_REPEATS = 3
 
 
+class RunFailed(Exception):
+    """Every attempt at a run raised the tensor-core kernels' device error flag."""
+
+
+def run_clean(run, device_error, where, repeats=MAX_REPEATS):
+    """Calls run() until device_error(label) reports nothing (None) after it, at most
+    repeats + 1 times, and returns run()'s last result. device_error reads (and clears) the
+    tensor-core kernels' error flag once the run's work is done: a run that raised it is
+    discarded, never measured. Raises RunFailed when every attempt raised it."""
+    for attempt in range(repeats + 1):
+        out = run()
+        if device_error(f"{where} (attempt {attempt})") is None:
+            return out
+    raise RunFailed(where)
+
+
 def fail(args, world, where, discarded):
     """Every attempt at `where` raised the device error flag: no measurement, say why."""
     if int(os.environ.get("RANK", "0")) == 0:
@@ -458,21 +474,21 @@ def main():
                 msg = "raised on another rank"
         if msg:
             discarded.append({"where": where, "error": msg})
-            _phase(f"{where}: {msg} - discarded, repeated")
+            _phase(f"{where}: {msg} - discarded")
         return msg
 
-    _phase(f"{args.warmup} warm-up steps")
-    done, i = 0, 0
-    while done < args.warmup:
-        if i >= args.warmup + MAX_REPEATS:
-            fail(args, world, "warm-up", discarded)
-            return
+    def synced_step(i):
         step(i)
         torch.cuda.synchronize()
-        if device_error(f"warm-up step {i}") is None:
-            done += 1
+
+    _phase(f"{args.warmup} warm-up steps")
+    try:
+        for i in range(args.warmup):
+            run_clean(lambda: synced_step(i), device_error, f"warm-up step {i}")
             _phase(f"warm-up step {i} done")
-        i += 1
+    except RunFailed as e:
+        fail(args, world, str(e), discarded)
+        return
 
     if args.profile_step:
         # every kernel of one step (ours, cuDNN, cuBLAS, torch) with its device time, from
@@ -497,7 +513,8 @@ def main():
     _phase(f"timing {args.steps} steps")
     # ---- timed region: K steps, inputs resident in HBM (working set >> 126 MB L2)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for attempt in range(MAX_REPEATS + 1):
+
+    def timed_steps():
         with ClockSampler(local) as clocks:
             barrier()
             torch.cuda.synchronize()
@@ -507,10 +524,12 @@ def main():
             end.record()
             torch.cuda.synchronize()
             barrier()
-        if device_error(f"timed steps (attempt {attempt})") is None:
-            break
-    else:
-        fail(args, world, "timed steps", discarded)
+        return clocks
+
+    try:
+        clocks = run_clean(timed_steps, device_error, "timed steps")
+    except RunFailed as e:
+        fail(args, world, str(e), discarded)
         return
     ms = start.elapsed_time(end) / args.steps
     t = torch.tensor([ms], device=dev)
@@ -522,15 +541,16 @@ def main():
 
     _phase(f"{ms:.1f} ms/step; one instrumented step")
     # ---- per-kernel device times inside one step (events around every C-ABI call)
-    for attempt in range(MAX_REPEATS + 1):
+    def instrumented_step():
         barrier()
         with _lib.KernelTimer() as kt:
             step(0)
-        ksum = kt.summary()
-        if device_error(f"instrumented step (attempt {attempt})") is None:
-            break
-    else:
-        fail(args, world, "instrumented step", discarded)
+        return kt.summary()
+
+    try:
+        ksum = run_clean(instrumented_step, device_error, "instrumented step")
+    except RunFailed as e:
+        fail(args, world, str(e), discarded)
         return
 
     _phase("end-to-end steps through train_step")
@@ -538,7 +558,8 @@ def main():
     host = [(ids.cpu().pin_memory(), lb.cpu().pin_memory()) for ids, lb in data]
     h2d = sum(x.numel() * x.element_size() for x in host[0])
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for attempt in range(MAX_REPEATS + 1):
+
+    def e2e_steps():
         barrier()
         torch.cuda.synchronize()
         e0.record()
@@ -548,14 +569,16 @@ def main():
             lb = lb_h.to(dev, non_blocking=True)
             loss = train_step(model, opt, ids, lb, grad_sync=sync,
                               num_items_in_batch=global_label_count(lb))
-            loss_value = float(loss.cpu())     # device -> host read of the step's result
+            last = float(loss.cpu())           # device -> host read of the step's result
         e1.record()
         torch.cuda.synchronize()
         barrier()
-        if device_error(f"end-to-end steps (attempt {attempt})") is None:
-            break
-    else:
-        fail(args, world, "end-to-end steps", discarded)
+        return last
+
+    try:
+        loss_value = run_clean(e2e_steps, device_error, "end-to-end steps")
+    except RunFailed as e:
+        fail(args, world, str(e), discarded)
         return
     ems = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
     if world > 1:

@@ -1,0 +1,81 @@
+"""Host logic of bench.py that needs no GPU: a run whose tensor-core kernels raised the device
+error flag is repeated and never measured, and the clock samples taken during the timed region
+are summarised with the throttle reasons seen under load."""
+
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+class FakeFlag:
+    """Stands in for the device error flag: raised after the listed attempts (0-based)."""
+
+    def __init__(self, raised_on):
+        self.raised_on = set(raised_on)
+        self.labels = []
+
+    def __call__(self, label):
+        n = len(self.labels)
+        self.labels.append(label)
+        return "a tensor-core kernel gave up a bounded wait (site 3)" if n in self.raised_on \
+            else None
+
+
+def test_clean_run_is_kept_at_once():
+    calls = []
+    flag = FakeFlag(raised_on=[])
+    out = bench.run_clean(lambda: calls.append(1) or len(calls), flag, "timed steps")
+    assert out == 1 and len(calls) == 1
+    assert flag.labels == ["timed steps (attempt 0)"]
+
+
+def test_run_that_raised_the_flag_is_repeated_and_the_clean_one_returned():
+    results = iter([10.0, 20.0, 30.0])
+    flag = FakeFlag(raised_on=[0, 1])
+    out = bench.run_clean(lambda: next(results), flag, "warm-up step 0")
+    assert out == 30.0                       # the measurement of the first clean attempt
+    assert flag.labels == [f"warm-up step 0 (attempt {k})" for k in range(3)]
+
+
+def test_every_attempt_raising_the_flag_is_a_failure():
+    runs = []
+    flag = FakeFlag(raised_on=range(100))
+    with pytest.raises(bench.RunFailed, match="end-to-end steps"):
+        bench.run_clean(lambda: runs.append(1), flag, "end-to-end steps", repeats=2)
+    assert len(runs) == 3                    # bounded: repeats + 1 attempts, no more
+
+
+def test_clock_summary_uses_loaded_samples_and_reports_throttle_reasons():
+    cs = bench.ClockSampler(0)
+    cs.proc = object()                       # as if nvidia-smi had been started
+    cs.out = "\n".join([
+        "0, 345, 1965, 120.5, 0, Not Active, Not Active, Not Active, Not Active",   # idle
+        "0, 1402, 1965, 990.1, 100, Not Active, Not Active, Not Active, Active",
+        "0, 1380, 1965, 995.0, 100, Not Active, Not Active, Not Active, Active",
+        "0, 1410, 1965, 980.7, 99, Not Active, Not Active, Not Active, Active",
+        "garbage line",
+    ])
+    s = cs.summary()
+    assert s["sm_mhz"] == 1402               # median of the three samples under load
+    assert s["sm_max_mhz"] == 1965
+    assert s["samples"] == 3
+    assert s["reasons"] == ["sw_power_cap"]
+    assert s["power_w_max"] == 995.0
+
+
+def test_kernel_table_fractions():
+    pk = {"hbm_gbs": 6000.0, "bf16_tflops": 1700.0, "bf16_tflops_sustained": 1400.0}
+    summary = {"qb_rmsnorm_fwd": {"launches": 2, "ms_total": 1.0, "bytes": 3_000_000_000,
+                                  "flops": 0},
+               "qb_gemm2_bf16": {"launches": 4, "ms_total": 10.0, "bytes": 0,
+                                 "flops": 14_000_000_000_000}}
+    t = bench.kernel_table(summary, pk)
+    assert t["qb_rmsnorm_fwd"]["achieved_gbs"] == 3000.0 and t["qb_rmsnorm_fwd"]["frac"] == 0.5
+    assert t["qb_gemm2_bf16"]["achieved_tflops"] == 1400.0
+    assert t["qb_gemm2_bf16"]["frac"] == 1.0     # against the sustained peak
