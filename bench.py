@@ -43,6 +43,8 @@ WORKLOADS = {
 # from ncu captures of each of its launch shapes in the step, averaged over the step's launch mix
 # (profiles/tc_gemm_kernel_dram_traffic_7b_projections.md). Keyed by --config.
 TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1793e6, "qb_gemm_gateup_swiglu": 4211e6}}
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the one-CTA tcgen05 GEMM "
+                  "at the step's launch shapes; large launches now run the 2-SM kernel")
 
 # per-kernel roofline class: "hbm" (bytes) or "tensor" (flops)
 BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hbm",
@@ -609,6 +611,7 @@ def main():
                         "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                         "frac": round(achieved / pk["bf16_tflops_sustained"], 3),
                         "traffic": TRAFFIC_PER_LAUNCH.get(args.config, {}).get(dom_name),
+                        "traffic_source": TRAFFIC_SOURCE,
                         "algorithmic_flops_per_launch": int(per),
                         "peak_source": pk["source"] + " (sustained)"}
 
