@@ -23,6 +23,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from datetime import timedelta
 
@@ -76,6 +77,94 @@ def _phase(msg):
 # are repeated after a tensor-core kernel gave up a bounded wait in them (a run with a raised
 # device error flag is never measured).
 MAX_REPEATS = 3
+# Deadline of one warm-up or instrumented step (and the unit of a K-step block's deadline) after
+# which the watchdog ends the run with what it can read of the stall. A 7B step takes under 1 s
+# (the first, with library set-up, a few seconds).
+STEP_DEADLINE_S = 180.0
+
+
+class Watchdog:
+    """Ends a run whose phase overruns its deadline with evidence instead of a silent timeout:
+    the tensor-core kernels' error flag (read on a stream of its own, which does not queue
+    behind the stuck work: a site code means a bounded wait gave up, a clear flag means
+    something else stalled), every thread's stack on stderr, and an error JSON line on rank 0;
+    then the process exits with status 3."""
+
+    def __init__(self, lib, dev, rank, world, args, stream=None):
+        self.lib, self.dev, self.rank, self.world, self.args = lib, dev, rank, world, args
+        # the stream the flag is read on: made now, not while the process is stalled
+        self.stream = stream if stream is not None else torch.cuda.Stream(device=dev)
+        self.cv = threading.Condition()
+        self.deadline = None
+        self.label, self.seconds = None, None
+        threading.Thread(target=self._watch, daemon=True, name="bench-watchdog").start()
+
+    def arm(self, label, seconds):
+        with self.cv:
+            self.label, self.seconds = label, seconds
+            self.deadline = time.monotonic() + seconds
+            self.cv.notify()
+
+    def disarm(self):
+        with self.cv:
+            self.deadline = None
+            self.cv.notify()
+
+    def watched(self, label, seconds, fn):
+        """fn wrapped so that each call runs under a deadline of `seconds`."""
+        def run():
+            self.arm(label, seconds)
+            try:
+                return fn()
+            finally:
+                self.disarm()
+        return run
+
+    def _watch(self):
+        while True:
+            with self.cv:
+                if self.deadline is None:
+                    self.cv.wait()
+                    continue
+                left = self.deadline - time.monotonic()
+                if left > 0:
+                    self.cv.wait(timeout=left)
+                    continue
+                label, seconds = self.label, self.seconds
+            self._fire(label, seconds)
+            return
+
+    def _read_flag(self, out):
+        try:
+            if self.dev is not None:
+                torch.cuda.set_device(self.dev)
+            rc = self.lib.qb_device_error(self.stream.cuda_stream)
+            out.append(self.lib.qb_last_error().decode(errors="replace") if rc
+                       else "clear: no bounded wait gave up")
+        except Exception as e:  # noqa: BLE001 - evidence only
+            out.append(f"unread: {e!r}")
+
+    def _fire(self, label, seconds):
+        import traceback
+        flag = []
+        reader = threading.Thread(target=self._read_flag, args=(flag,), daemon=True)
+        reader.start()
+        reader.join(timeout=15.0)
+        flag = flag[0] if flag else "unread: the read did not return within 15 s"
+        print(f"bench.py rank {self.rank}: watchdog: {label} overran {seconds:.0f} s; device "
+              f"error flag: {flag}", file=sys.stderr, flush=True)
+        names = {t.ident: t.name for t in threading.enumerate()}
+        for ident, frame in sys._current_frames().items():
+            print(f"-- thread {names.get(ident, ident)}", file=sys.stderr)
+            traceback.print_stack(frame, file=sys.stderr)
+        if self.rank == 0:
+            print(json.dumps({"metric": METRIC, "value": None, "unit": "tokens/s",
+                              "n_gpus": self.world, "steps": self.args.steps,
+                              "warmup": self.args.warmup,
+                              "error": f"watchdog: {label} did not finish in {seconds:.0f} s",
+                              "device_error_flag": flag}), flush=True)
+        sys.stderr.flush()
+        os._exit(3)
 
 
 class RunFailed(Exception):
@@ -461,6 +550,7 @@ def main():
 
     lib = _lib.load()
     discarded = []    # runs in which a tensor-core kernel gave up a bounded wait
+    dog = Watchdog(lib, dev, rank, world, args)
 
     def device_error(where):
         """Reads (and clears) the tensor-core kernels' error flag after the current stream's work,
@@ -486,7 +576,8 @@ def main():
     _phase(f"{args.warmup} warm-up steps")
     try:
         for i in range(args.warmup):
-            run_clean(lambda: synced_step(i), device_error, f"warm-up step {i}")
+            run_clean(dog.watched(f"warm-up step {i}", STEP_DEADLINE_S,
+                                  lambda: synced_step(i)), device_error, f"warm-up step {i}")
             _phase(f"warm-up step {i} done")
     except RunFailed as e:
         fail(args, world, str(e), discarded)
@@ -529,7 +620,8 @@ def main():
         return clocks
 
     try:
-        clocks = run_clean(timed_steps, device_error, "timed steps")
+        clocks = run_clean(dog.watched("timed steps", STEP_DEADLINE_S * (1 + args.steps / 4),
+                                       timed_steps), device_error, "timed steps")
     except RunFailed as e:
         fail(args, world, str(e), discarded)
         return
@@ -550,7 +642,8 @@ def main():
         return kt.summary()
 
     try:
-        ksum = run_clean(instrumented_step, device_error, "instrumented step")
+        ksum = run_clean(dog.watched("instrumented step", STEP_DEADLINE_S, instrumented_step),
+                         device_error, "instrumented step")
     except RunFailed as e:
         fail(args, world, str(e), discarded)
         return
@@ -578,7 +671,9 @@ def main():
         return last
 
     try:
-        loss_value = run_clean(e2e_steps, device_error, "end-to-end steps")
+        loss_value = run_clean(dog.watched("end-to-end steps",
+                                           STEP_DEADLINE_S * (1 + args.steps / 4), e2e_steps),
+                               device_error, "end-to-end steps")
     except RunFailed as e:
         fail(args, world, str(e), discarded)
         return

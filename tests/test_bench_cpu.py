@@ -79,3 +79,42 @@ def test_kernel_table_fractions():
     assert t["qb_rmsnorm_fwd"]["achieved_gbs"] == 3000.0 and t["qb_rmsnorm_fwd"]["frac"] == 0.5
     assert t["qb_gemm2_bf16"]["achieved_tflops"] == 1400.0
     assert t["qb_gemm2_bf16"]["frac"] == 1.0     # against the sustained peak
+
+
+def test_watchdog_reports_the_device_flag_when_a_phase_overruns(monkeypatch, capsys):
+    """A phase that overruns its deadline ends the run with the kernels' error flag (the site
+    of the wait that gave up) in an error JSON line, instead of hanging until killed."""
+    import json
+    import threading
+    import time
+    from types import SimpleNamespace
+
+    exited = threading.Event()
+    codes = []
+
+    def fake_exit(code):
+        codes.append(code)
+        exited.set()
+
+    monkeypatch.setattr(bench.os, "_exit", fake_exit)
+
+    class FakeLib:
+        def qb_device_error(self, stream):
+            return 4
+
+        def qb_last_error(self):
+            return b"a tensor-core kernel gave up a bounded wait (site 65)"
+
+    dog = bench.Watchdog(FakeLib(), None, 0, 1, SimpleNamespace(steps=5, warmup=3),
+                         stream=SimpleNamespace(cuda_stream=0))
+    slow = dog.watched("warm-up step 0", 0.05, lambda: time.sleep(0.01))
+    slow()                                    # finishes in time: nothing fires
+    time.sleep(0.2)
+    assert not exited.is_set()
+    dog.arm("warm-up step 1", 0.05)           # never disarmed: the phase overruns
+    assert exited.wait(5.0)
+    assert codes == [3]
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["value"] is None
+    assert "warm-up step 1" in line["error"]
+    assert "site 65" in line["device_error_flag"]
