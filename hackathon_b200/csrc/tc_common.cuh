@@ -35,13 +35,20 @@ __device__ __forceinline__ uint64_t globaltimer() {
 // the driver and may step forward when it is resynchronised; the cycle counter cannot jump, so
 // a timer step alone never makes a healthy wait give up. At any SM clock of 0.5 GHz or more the
 // cycle test holds by the time the timer test does, so the bound stays limit_ns.
+__device__ __forceinline__ uint64_t sm_cycles() {
+  uint64_t c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+
 struct WaitClock {
-  uint64_t t0;
-  long long c0;
-  __device__ __forceinline__ WaitClock() : t0(globaltimer()), c0(clock64()) {}
+  uint64_t t0, c0;
+  __device__ __forceinline__ WaitClock() {
+    t0 = globaltimer();
+    c0 = sm_cycles();
+  }
   __device__ __forceinline__ bool expired(uint64_t limit_ns) const {
-    return globaltimer() - t0 > limit_ns &&
-           static_cast<unsigned long long>(clock64() - c0) > limit_ns / 2;
+    return globaltimer() - t0 > limit_ns && sm_cycles() - c0 > limit_ns / 2;
   }
 };
 
