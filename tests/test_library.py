@@ -129,3 +129,15 @@ def test_apply_is_idempotent_without_gpu():
     x = torch.randn(2, 8)
     want = norm.weight * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6))
     torch.testing.assert_close(norm(x), want)
+
+
+def test_library_is_built_from_the_current_sources():
+    """The in-tree library is newer than every CUDA source and header it is built from, so the
+    tests here and on the GPU exercise the code in the tree, not an older build left behind by a
+    rebuild that failed."""
+    from hackathon_b200.csrc import build as b
+    assert os.path.exists(b.LIB), "library not built: python -m hackathon_b200.csrc.build"
+    lib_t = os.path.getmtime(b.LIB)
+    srcs = [os.path.join(b.HERE, f) for f in b._sources()] + b._headers()
+    stale = [os.path.relpath(p, ROOT) for p in srcs if os.path.getmtime(p) > lib_t]
+    assert not stale, f"sources newer than the library (rebuild): {stale}"
