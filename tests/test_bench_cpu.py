@@ -118,3 +118,46 @@ def test_watchdog_reports_the_device_flag_when_a_phase_overruns(monkeypatch, cap
     assert line["value"] is None
     assert "warm-up step 1" in line["error"]
     assert "site 65" in line["device_error_flag"]
+
+
+def _completed(code, out):
+    import subprocess
+    return subprocess.CompletedProcess(args=[], returncode=code, stdout=out)
+
+
+def test_supervisor_measures_again_after_a_stalled_attempt(capsys):
+    """A child whose watchdog fired (status 3) is followed by one fresh child; the line printed
+    is the fresh child's measurement, with the stalled attempt's own error line attached."""
+    import json
+    stalled = json.dumps({"value": None, "error": "watchdog: warm-up step 0 did not finish in 90 s",
+                          "device_error_flag": "clear: no bounded wait gave up"})
+    good = json.dumps({"metric": "m", "value": 22000.0})
+    results = iter([_completed(3, stalled + "\n"), _completed(0, good + "\n")])
+    calls = []
+
+    def fake_run(cmd, **kw):
+        calls.append(cmd)
+        return next(results)
+
+    assert bench.supervise(["python", "bench.py", "--worker"], run=fake_run) == 0
+    assert len(calls) == 2
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["value"] == 22000.0
+    assert line["restarts"][0]["device_error_flag"].startswith("clear")
+
+
+def test_supervisor_passes_a_clean_run_through_and_stops_after_the_last_attempt(capsys):
+    import json
+    good = json.dumps({"metric": "m", "value": 1.0})
+    assert bench.supervise(["x"], run=lambda cmd, **kw: _completed(0, good)) == 0
+    assert json.loads(capsys.readouterr().out.strip()) == {"metric": "m", "value": 1.0}
+    stalled = json.dumps({"value": None, "error": "watchdog"})
+    n = []
+
+    def always_stalls(cmd, **kw):
+        n.append(1)
+        return _completed(3, stalled)
+
+    assert bench.supervise(["x"], run=always_stalls) == 3
+    assert len(n) == 2                                   # bounded: one fresh attempt only
+    assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["value"] is None
