@@ -89,6 +89,10 @@ constexpr int kWarpCodes = 6, kWarpDeq0 = 7;
 constexpr int kGroups = 2;            // dequant warp-groups, alternating k-blocks
 constexpr int kGroupThreads = 256;    // one group rebuilds a whole 128 x 64 tile
 constexpr int kDeqThreads = kGroups * kGroupThreads;
+// A group waits for an item's codes after that item's A slot is free; its own previous item read
+// the codes stage before that, so the phase-parity wait on a codes stage is never two
+// generations ahead of its fills as long as the ring has a stage per group.
+static_assert(kStagesC >= kGroups, "codes ring shorter than the number of dequant groups");
 constexpr int kSmem = kStagesB * kB + kStagesA * kA + kStagesC * kC + 1024 + 1024 + (256 + 16) * 4;
 
 struct LoraA {               // segment-1 A operand (bf16), read by the dequant warps

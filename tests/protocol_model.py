@@ -72,7 +72,7 @@ class World:
         self.ev = {}
 
     def clone(self):
-        w = World.__new__(World)
+        w = self.__class__.__new__(self.__class__)
         w.roles, w.p = self.roles, self.p
         w.pc = dict(self.pc)
         w.bars = {k: b.clone() for k, b in self.bars.items()}
@@ -478,3 +478,162 @@ def lora_dx(S, nk, tiles, epi):
     params = {"masked": False, "maskers": 0, "mma_per_stage": 1, "store": False,
               "loads_per_stage": 2, "epilogue": epi, "mma_per_tile": nk}
     return World(roles, bars, params)
+
+
+# ------------------------------------------------------------- generic ring model (NF4 kernel)
+class RingWorld(World):
+    """The vocabulary for kernels with several rings and thread-written operands:
+        ("load", bar, nbytes, ring, s, g)  TMA into ring stage s, generation g
+        ("write", ring, s, g)              one thread's part of a thread-written stage
+        ("read", ring, s, g)               a thread reads a stage (must be complete)
+        ("use", ring, s, g)                a thread is done with a stage
+        ("mma2", ((ring, s, g), ...), tile, first)   MMA reading those stages
+    A stage may be refilled once all its consumers of the previous generation are done
+    (need_use[ring]); it is complete once need_ready[ring] loads / writes landed."""
+
+    def apply(self, m):
+        kind, x = m
+        P = self.p
+        if kind == "tma":
+            bar, nbytes, ring, s, g = self.tma[x]
+            self.tma = self.tma[:x] + self.tma[x + 1:]
+            self.inc("ready", ring, s, g)
+            self.bars[bar].complete_tx(nbytes)
+            return
+        if kind == "mma":
+            head, rest = self.mmaq[x][0], self.mmaq[x][1:]
+            self.mmaq[x] = rest
+            if head[0] == "mma2":
+                for ring, s, g in head[1]:
+                    self.inc("used", ring, s, g)
+                self.inc("tile_mma_done", head[2])
+            else:
+                for b in head[1]:
+                    self.bars[b].arrive(f"commit by {x}")
+            return
+        r = x
+        op = self.roles[r][self.pc[r]]
+        t = op[0]
+        if t not in ("load", "write", "read", "use", "mma2"):
+            return World.apply(self, m)
+        self.pc[r] += 1
+
+        def refill_ok(ring, s, g):
+            if g > 0 and self.get("used", ring, s, g - 1) != P["need_use"][ring]:
+                raise Hazard(f"{r}: refills {ring} stage {s} gen {g} before gen {g - 1} is used")
+
+        def complete(ring, s, g, who):
+            if self.get("ready", ring, s, g) != P["need_ready"][ring]:
+                raise Hazard(f"{who}: reads {ring} stage {s} gen {g} before it is complete")
+
+        if t == "load":
+            _, bar, nbytes, ring, s, g = op
+            refill_ok(ring, s, g)
+            self.tma = self.tma + ((bar, nbytes, ring, s, g),)
+        elif t == "write":
+            _, ring, s, g = op
+            refill_ok(ring, s, g)
+            self.inc("ready", ring, s, g)
+        elif t == "read":
+            _, ring, s, g = op
+            complete(ring, s, g, r)
+        elif t == "use":
+            _, ring, s, g = op
+            self.inc("used", ring, s, g)
+        elif t == "mma2":
+            _, stages, tile, first = op
+            for ring, s, g in stages:
+                complete(ring, s, g, r)
+            if first and tile >= P["acc_sets"] and \
+                    self.get("epi_done", tile - P["acc_sets"]) != P["epilogue"]:
+                raise Hazard(f"{r}: MMA of tile {tile} into accumulators still being drained")
+            self.mmaq[r] = self.mmaq.get(r, ()) + (("mma2", stages, tile),)
+
+
+def nf4_gemm(SB, SA, SC, nk0, nk1, tiles, warps_per_group=2, epi=1, groups=2):
+    """csrc/tc_nf4_gemm.cuh: B ring by TMA (warp 0), codes ring by TMA (warp 6, segment-0
+    k-blocks only), A ring written by `groups` dequant groups taking alternate k-blocks (item it
+    goes to group it % groups; every group steps through every stage index), one accumulator set
+    (tfull[0] / tempty[0], parity t & 1). Each group is modelled as `warps_per_group` threads:
+    fullA counts the group's threads, emptyC one arrival per warp.
+
+    A group waits for an item's codes only after that item's A slot is free, and its own previous
+    item (two items back) read the codes stage before that, so no codes stage is waited on two
+    generations ahead of its fills while the codes ring has at least as many stages as there are
+    groups (the kernel: 8 stages, 2 groups). With a one-stage ring the checker finds the parity
+    aliasing: a group would take an unfilled stage for a filled one."""
+    nk = nk0 + nk1
+    W = warps_per_group
+    roles = {}
+    ops, st, ph, it = [], 0, 0, 0
+    for t in range(tiles):
+        for kb in range(nk):
+            ops += [("wait", f"emptyB{st}", ph ^ 1), ("expect", f"fullB{st}", 1),
+                    ("load", f"fullB{st}", 1, "B", st, it // SB)]
+            st, ph = _adv(st, ph, SB)
+            it += 1
+    roles["prodB"] = ops
+    ops, st, ph, it = [], 0, 0, 0
+    for t in range(tiles):
+        for kb in range(nk0):
+            ops += [("wait", f"emptyC{st}", ph ^ 1), ("expect", f"fullC{st}", 1),
+                    ("load", f"fullC{st}", 1, "C", st, it // SC)]
+            st, ph = _adv(st, ph, SC)
+            it += 1
+    roles["prodC"] = ops
+    ops = []
+    sb = sa = 0
+    pbh = pah = 0
+    it = 0
+    for t in range(tiles):
+        ops.append(("wait", "tempty0", (t & 1) ^ 1))
+        for kb in range(nk):
+            ops += [("wait", f"fullB{sb}", pbh), ("wait", f"fullA{sa}", pah),
+                    ("mma2", (("B", sb, it // SB), ("A", sa, it // SA)), t, kb == 0),
+                    ("commit", (f"emptyB{sb}",)), ("commit", (f"emptyA{sa}",))]
+            sb, pbh = _adv(sb, pbh, SB)
+            sa, pah = _adv(sa, pah, SA)
+            it += 1
+        ops.append(("commit", ("tfull0",)))
+    ops += [("commit", ("drain",)), ("wait", "drain", 0)]
+    roles["mma"] = ops
+    for e in range(epi):
+        roles[f"epi{e}"] = sum(([("wait", "tfull0", t & 1), ("epi_read", t), ("epi_done", t),
+                                 ("arrive", ("tempty0",))] for t in range(tiles)), [])
+    for grp in range(groups):
+        for w in range(W):
+            ops = []
+            sa = sc = 0
+            pah = pch = 0
+            it = itc = 0
+            for t in range(tiles):
+                for kb in range(nk):
+                    seg0 = kb < nk0
+                    if it % groups == grp:
+                        ops.append(("wait", f"emptyA{sa}", pah ^ 1))
+                        if seg0:
+                            ops += [("wait", f"fullC{sc}", pch), ("read", "C", sc, itc // SC),
+                                    ("write", "A", sa, it // SA), ("use", "C", sc, itc // SC),
+                                    ("arrive", (f"emptyC{sc}",))]
+                        else:
+                            ops.append(("write", "A", sa, it // SA))
+                        ops.append(("arrive", (f"fullA{sa}",)))
+                    sa, pah = _adv(sa, pah, SA)
+                    if seg0:
+                        sc, pch = _adv(sc, pch, SC)
+                        itc += 1
+                    it += 1
+            roles[f"deq{grp}.{w}"] = ops
+    bars = {}
+    for k in range(SB):
+        bars[f"fullB{k}"], bars[f"emptyB{k}"] = Bar(1), Bar(1)
+    for k in range(SA):
+        bars[f"fullA{k}"], bars[f"emptyA{k}"] = Bar(W), Bar(1)
+    for k in range(SC):
+        bars[f"fullC{k}"], bars[f"emptyC{k}"] = Bar(1), Bar(W)
+    bars["tfull0"], bars["tempty0"], bars["drain"] = Bar(1), Bar(epi), Bar(1)
+    params = {"need_use": {"B": 1, "A": 1, "C": W}, "need_ready": {"B": 1, "A": W, "C": 1},
+              "acc_sets": 1, "epilogue": epi, "mma_per_tile": nk}
+    w = RingWorld.__new__(RingWorld)
+    World.__init__(w, roles, bars, params)
+    return w

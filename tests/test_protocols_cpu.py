@@ -59,3 +59,17 @@ def test_planted_mistake_leader_arming_only_its_own_bytes_is_found():
 def test_planted_mistake_wrong_epilogue_parity_is_found():
     with pytest.raises(pm.Hazard, match="DEADLOCK|before its MMAs"):
         pm.explore(pm.gemm1(2, 1, 3, 1, epi_parity_flip=1))
+
+
+def test_fused_nf4_kernel_rings_and_alternating_dequant_groups():
+    """csrc/tc_nf4_gemm.cuh: activations and codes by TMA, the A operand written by two dequant
+    groups taking alternate k-blocks (a stage's generations alternate between the groups), the
+    LoRA segment without codes, one accumulator set drained before the next tile."""
+    n, how = pm.explore(pm.nf4_gemm(1, 3, 2, 3, 1, 2, warps_per_group=1))
+    assert how == "complete" and n > 1000
+
+
+def test_planted_mistake_codes_ring_shorter_than_the_group_count_is_found():
+    # one codes stage for two alternating groups: a parity wait two generations ahead
+    with pytest.raises(pm.Hazard, match="before it is complete"):
+        pm.explore(pm.nf4_gemm(1, 3, 1, 3, 0, 2, warps_per_group=1))
