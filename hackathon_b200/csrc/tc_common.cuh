@@ -124,6 +124,15 @@ __device__ __forceinline__ bool mbar_wait_quiet(uint64_t* bar, uint32_t parity) 
   return true;
 }
 
+// Error path only: lets copies that no barrier of this CTA can observe land before the CTA
+// leaves (the 2-SM kernel's follower loads complete on the leader's barrier, in phases the
+// leader may not have armed once both stopped at different items). 100 us on both clocks:
+// a stage's copies land in a few microseconds.
+__device__ __forceinline__ void error_grace() {
+  const WaitClock clk;
+  while (!clk.expired(100000ull)) __nanosleep(2000);
+}
+
 __device__ __forceinline__ bool failed(int* err) {
   return *reinterpret_cast<volatile int*>(err) != 0;
 }

@@ -142,11 +142,18 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
         }
         if (!ok) break;
       }
-      if (tc::failed(err) && leader)   // the leader's barriers count both CTAs' copies
-        for (int i = 0; i < kStages && i < issued; ++i) {
-          if (--s < 0) { s = kStages - 1; ph ^= 1; }
-          tc::mbar_wait_quiet(&full[s], ph);
-        }
+      if (tc::failed(err)) {
+        if (leader)   // the leader's barriers count both CTAs' copies
+          for (int i = 0; i < kStages && i < issued; ++i) {
+            if (--s < 0) { s = kStages - 1; ph ^= 1; }
+            tc::mbar_wait_quiet(&full[s], ph);
+          }
+        // A wait that finds its phase complete does not look at the flag, so after a give-up
+        // the two producers may stop at different items: copies of the follower into a phase
+        // the leader never armed are seen by no barrier. Both wait them out here, before the
+        // pair meets at the final cluster barrier and leaves.
+        tc::error_grace();
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader)
