@@ -141,3 +141,34 @@ def test_library_is_built_from_the_current_sources():
     srcs = [os.path.join(b.HERE, f) for f in b._sources()] + b._headers()
     stale = [os.path.relpath(p, ROOT) for p in srcs if os.path.getmtime(p) > lib_t]
     assert not stale, f"sources newer than the library (rebuild): {stale}"
+
+
+def test_ctypes_bindings_match_the_header_declarations():
+    """Every binding in _lib passes exactly the arguments its C declaration takes, each of the
+    same kind (pointer / int64 / int / float / uint64): a shifted or missing argument would reach
+    a kernel launch as a wrong size or address."""
+    from hackathon_b200 import _lib
+    src = open(os.path.join(ROOT, "include", "qlora_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decls = re.findall(r"\b(?:int|int64_t|const char\*)\s+(qb_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src)
+    assert len(decls) >= 30
+
+    def c_kind(p):
+        p = p.strip()
+        if p in ("", "void"):
+            return None
+        if "*" in p or p.startswith("cudaStream_t"):
+            return "ptr"
+        t = p.rsplit(" ", 1)[0].replace("const ", "").strip()
+        return {"int64_t": "i64", "int": "i32", "float": "f32", "uint64_t": "u64"}[t]
+
+    def py_kind(t):
+        if t is ctypes.c_void_p or isinstance(t, type) and issubclass(t, ctypes._Pointer):
+            return "ptr"
+        return {ctypes.c_int64: "i64", ctypes.c_int: "i32", ctypes.c_float: "f32",
+                ctypes.c_uint64: "u64"}[t]
+
+    for name, params in decls:
+        want = [k for k in map(c_kind, params.split(",")) if k is not None]
+        have = [py_kind(t) for t in _lib._SIGNATURES[name]]
+        assert have == want, f"{name}: binding {have} vs declaration {want}"
