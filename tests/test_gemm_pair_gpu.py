@@ -1,7 +1,7 @@
-"""The 2-SM (cta_group::2) GEMM kernel, which the launcher uses only when QB_GEMM_PAIR is set
-(it measured slower than the one-CTA kernel): both B layouts, the LoRA segment, the residual
-epilogue and ragged shapes against fp32 products, in a child process with QB_GEMM_PAIR=1 (the
-switch is read once per process)."""
+"""The 2-SM (cta_group::2) GEMM kernel, which the launcher takes for launches with a 256 x 256
+tile for every SM pair: forced on (QB_GEMM_PAIR=1, read once per process, hence the child
+process) for small and ragged shapes too, with both B layouts, the LoRA segment and the residual
+epilogue, against fp32 products."""
 
 import os
 import subprocess
