@@ -165,6 +165,7 @@ class GateUpSwiGLU(torch.autograd.Function):
     """The MLP's gate and up projections and the SwiGLU between them, long-token path:
 
         forward   xd_g, xd_u = dropout(x) (each projection's own mask); U_* = xd_* A_*^T
+                  (qb_lora_xa, into the two halves of one [T, 2r] buffer)
                   h = silu(x W_g^T + U_g (s B_g)^T) * (x W_u^T + U_u (s B_u)^T)
                                         (one tcgen05 GEMM, SwiGLU in its epilogue; g and u are
                                          stored only when a backward will read them)
@@ -262,7 +263,8 @@ class LoRANF4Proj(torch.autograd.Function):
     """The whole QLoRA projection (and the residual add it feeds) on this package's kernels:
 
         forward   xd = dropout(x)                      (mask drawn once per step, kept as bits)
-                  U  = xd A^T                                           (skinny GEMM)
+                  U  = xd A^T            (qb_lora_xa: from x and the bits in one tcgen05 kernel;
+                                          xd itself is stored only when the backward reads it)
                   y  = h + x deq(W)^T + b + U (s B)^T                   (one tcgen05 GEMM)
         backward  V  = g (s B)                                          (skinny GEMM)
                   dx = g deq(W)  [+= s mask .* (V A)]                   (tcgen05 GEMM, then the
