@@ -45,7 +45,7 @@ def _worker(rank, world, port, out):
 @pytest.mark.timeout(120)
 def test_dp_gradient_equals_global_mean_gradient():
     world = 2
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()   # no fork of this (possibly threaded) process
     out = mgr.dict()
     mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
     torch.manual_seed(0)
