@@ -33,3 +33,21 @@ def cuda():
 
     _lib.load()  # fails loudly when the library is not built
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _tensor_core_error_flag(request):
+    """After every GPU test: reads (and clears) the tensor-core kernels' error flag, so a kernel
+    that gave up a bounded wait fails the test it ran in, with the wait's site, instead of making
+    every later tensor-core launch of the session bail out."""
+    yield
+    if "cuda" not in request.fixturenames:
+        return
+    import torch
+
+    from hackathon_b200 import _lib
+
+    lib = _lib.load()
+    if lib.qb_device_error(_lib.stream(torch.device("cuda:0"))) != 0:
+        pytest.fail("a tensor-core kernel gave up a bounded wait in this test: "
+                    + lib.qb_last_error().decode(errors="replace"))
