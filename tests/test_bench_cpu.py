@@ -161,3 +161,32 @@ def test_supervisor_passes_a_clean_run_through_and_stops_after_the_last_attempt(
     assert bench.supervise(["x"], run=always_stalls) == 3
     assert len(n) == 2                                   # bounded: one fresh attempt only
     assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["value"] is None
+
+
+def _reference_arm(extra_env):
+    import subprocess
+    env = dict(os.environ, **extra_env)
+    return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                           "--config", "0.5b", "--steps", "1", "--warmup", "0",
+                           "--cpu-tokens", "32"], env=env, cwd=ROOT, capture_output=True,
+                          text=True, timeout=600)
+
+
+def test_reference_arm_prints_the_driver_contract_line():
+    """--impl reference: the eager CPU path on the host cores, one JSON line with the same metric
+    and unit as the measured arm, `impl`, the CPU baseline it is, and an e2e without copies."""
+    import json
+    r = _reference_arm({"WORLD_SIZE": "1", "RANK": "0"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC
+    assert line["unit"] == "tokens/s" and line["higher_is_better"] is True
+    assert line["value"] > 0 and line["cpu_baseline"]["value"] == line["value"]
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_without_work():
+    r = _reference_arm({"WORLD_SIZE": "2", "RANK": "1"})
+    assert r.returncode == 0 and r.stdout.strip() == ""
