@@ -16,9 +16,10 @@ device times of this package's kernels with their roofline fractions, the roofli
 dominant one, the CPU baseline (the reference's eager path on the host cores, a bounded sample),
 and the SM clocks sampled during the timed region.
 
-On one GPU the measurement runs in a child process (`--worker`): if a phase stalls, the child's
-watchdog ends it with the evidence it can read, and one fresh child measures again; the line
-then lists the stalled attempt under `restarts`.
+Nothing is measured twice: a phase that overruns its deadline ends the run at once with the
+launch monitor's report (which tensor-core launch has CTAs that never finished, the site of a
+wait that gave up), and a phase whose kernels raised the device error flag ends it with the
+flag's message. Either way the line has `value` null and the evidence.
 """
 
 import argparse
@@ -45,11 +46,11 @@ WORKLOADS = {
     "0.5b": ("configs[0] shapes: Qwen2.5-0.5B-shaped QLoRA step, 2 x 256 tokens per GPU", 2, 256),
 }
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernel,
-# from ncu captures of each of its launch shapes in the step, averaged over the step's launch mix
-# (profiles/tc_gemm_kernel_dram_traffic_7b_projections.md). Keyed by --config.
+# from ncu captures of each of its launch shapes in the step, averaged over the step's launch mix.
+# Keyed by --config.
 TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1793e6, "qb_gemm_gateup_swiglu": 4211e6}}
 TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the one-CTA tcgen05 GEMM "
-                  "at the step's launch shapes; large launches now run the 2-SM kernel")
+                  "(the kernel the step runs) at the step's launch shapes")
 
 # per-kernel roofline class: "hbm" (bytes) or "tensor" (flops)
 BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hbm",
@@ -77,27 +78,31 @@ def _phase(msg):
         print(f"bench.py [{time.monotonic() - _T0:7.1f} s] {msg}", file=sys.stderr, flush=True)
 
 
-# How many times a warm-up step, the timed steps, the instrumented step or the end-to-end steps
-# are repeated after a tensor-core kernel gave up a bounded wait in them (a run with a raised
-# device error flag is never measured).
-MAX_REPEATS = 3
 # Deadline of one warm-up or instrumented step (and the unit of a K-step block's deadline) after
 # which the watchdog ends the run with what it can read of the stall. A 7B step takes under 1 s
 # (the first, with library set-up, about 4 s).
 STEP_DEADLINE_S = 90.0
 
 
+def monitor_report(lib, index):
+    """The launch monitor's report for device `index`: read from pinned host memory the kernels
+    write, with no CUDA call, so it answers while the device is stuck."""
+    import ctypes
+    buf = ctypes.create_string_buffer(2048)
+    if lib.qb_monitor_report(int(index), buf, len(buf)) != 0:
+        return "unread: " + lib.qb_last_error().decode(errors="replace")
+    return buf.value.decode(errors="replace")
+
+
 class Watchdog:
     """Ends a run whose phase overruns its deadline with evidence instead of a silent timeout:
-    the tensor-core kernels' error flag (read on a stream of its own, which does not queue
-    behind the stuck work: a site code means a bounded wait gave up, a clear flag means
-    something else stalled), every thread's stack on stderr, and an error JSON line on rank 0;
-    then the process exits with status 3."""
+    the launch monitor's report (which tensor-core launch, if any, has CTAs that started and
+    never finished; the site of a bounded wait that gave up - read from host memory, no CUDA
+    call), every thread's stack on stderr, and an error JSON line on rank 0; then the process
+    exits with status 3."""
 
-    def __init__(self, lib, dev, rank, world, args, stream=None):
-        self.lib, self.dev, self.rank, self.world, self.args = lib, dev, rank, world, args
-        # the stream the flag is read on: made now, not while the process is stalled
-        self.stream = stream if stream is not None else torch.cuda.Stream(device=dev)
+    def __init__(self, lib, index, rank, world, args):
+        self.lib, self.index, self.rank, self.world, self.args = lib, index, rank, world, args
         self.cv = threading.Condition()
         self.deadline = None
         self.label, self.seconds = None, None
@@ -138,25 +143,14 @@ class Watchdog:
             self._fire(label, seconds)
             return
 
-    def _read_flag(self, out):
-        try:
-            if self.dev is not None:
-                torch.cuda.set_device(self.dev)
-            rc = self.lib.qb_device_error(self.stream.cuda_stream)
-            out.append(self.lib.qb_last_error().decode(errors="replace") if rc
-                       else "clear: no bounded wait gave up")
-        except Exception as e:  # noqa: BLE001 - evidence only
-            out.append(f"unread: {e!r}")
-
     def _fire(self, label, seconds):
         import traceback
-        flag = []
-        reader = threading.Thread(target=self._read_flag, args=(flag,), daemon=True)
-        reader.start()
-        reader.join(timeout=15.0)
-        flag = flag[0] if flag else "unread: the read did not return within 15 s"
-        print(f"bench.py rank {self.rank}: watchdog: {label} overran {seconds:.0f} s; device "
-              f"error flag: {flag}", file=sys.stderr, flush=True)
+        try:
+            report = monitor_report(self.lib, self.index)
+        except Exception as e:  # noqa: BLE001 - evidence only
+            report = f"unread: {e!r}"
+        print(f"bench.py rank {self.rank}: watchdog: {label} overran {seconds:.0f} s; launch "
+              f"monitor: {report}", file=sys.stderr, flush=True)
         names = {t.ident: t.name for t in threading.enumerate()}
         for ident, frame in sys._current_frames().items():
             print(f"-- thread {names.get(ident, ident)}", file=sys.stderr)
@@ -166,69 +160,33 @@ class Watchdog:
                               "n_gpus": self.world, "steps": self.args.steps,
                               "warmup": self.args.warmup,
                               "error": f"watchdog: {label} did not finish in {seconds:.0f} s",
-                              "device_error_flag": flag}), flush=True)
+                              "launch_monitor": report}), flush=True)
         sys.stderr.flush()
         os._exit(3)
 
 
-def supervise(cmd, attempts=2, run=subprocess.run):
-    """The single-GPU run: the measurement runs in a child process (`cmd`), and when that child's
-    watchdog ended it (status 3: a phase stalled; its exit tore the stuck CUDA context down) one
-    more child measures from scratch. This process never touches CUDA. The child's JSON line is
-    printed, with `restarts` listing each stalled attempt's own error line; returns the exit
-    status of the last child."""
-    restarts = []
-    for attempt in range(attempts):
-        r = run(cmd, stdout=subprocess.PIPE, text=True)
-        lines = [ln for ln in (r.stdout or "").splitlines() if ln.strip()]
-        last = lines[-1] if lines else ""
-        if r.returncode == 3 and attempt + 1 < attempts:
-            try:
-                restarts.append(json.loads(last))
-            except ValueError:
-                restarts.append({"error": last or "no output"})
-            print(f"bench.py: attempt {attempt} stalled (watchdog); measuring again in a fresh "
-                  f"process", file=sys.stderr, flush=True)
-            continue
-        for ln in lines[:-1]:
-            print(ln)
-        try:
-            line = json.loads(last)
-        except ValueError:
-            if last:
-                print(last)
-            return r.returncode
-        if restarts:
-            line["restarts"] = restarts
-        print(json.dumps(line), flush=True)
-        return r.returncode
-    return 3
-
-
 class RunFailed(Exception):
-    """Every attempt at a run raised the tensor-core kernels' device error flag."""
+    """A tensor-core kernel gave up a bounded wait during a phase: its work is undone."""
 
 
-def run_clean(run, device_error, where, repeats=MAX_REPEATS):
-    """Calls run() until device_error(label) reports nothing (None) after it, at most
-    repeats + 1 times, and returns run()'s last result. device_error reads (and clears) the
-    tensor-core kernels' error flag once the run's work is done: a run that raised it is
-    discarded, never measured. Raises RunFailed when every attempt raised it."""
-    for attempt in range(repeats + 1):
-        out = run()
-        if device_error(f"{where} (attempt {attempt})") is None:
-            return out
-    raise RunFailed(where)
+def run_checked(run, device_error, where):
+    """run(), then device_error(where) reads (and clears) the tensor-core kernels' error flag
+    once the run's work is done. A raised flag ends the measurement (RunFailed): the run is
+    neither measured nor repeated."""
+    out = run()
+    msg = device_error(where)
+    if msg is not None:
+        raise RunFailed(f"{where}: {msg}")
+    return out
 
 
-def fail(args, world, where, discarded):
-    """Every attempt at `where` raised the device error flag: no measurement, say why."""
+def fail(args, world, error, monitor):
+    """A phase's kernels raised the device error flag: no measurement, say why."""
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps({"metric": METRIC, "value": None, "unit": "tokens/s", "n_gpus": world,
                           "steps": args.steps, "warmup": args.warmup,
-                          "error": f"{where}: a tensor-core kernel gave up a bounded wait in "
-                                   f"every attempt",
-                          "discarded_runs": discarded}), flush=True)
+                          "error": f"a tensor-core kernel gave up a bounded wait: {error}",
+                          "launch_monitor": monitor}), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
@@ -325,33 +283,46 @@ def cpu_baseline(shape, tokens):
     from oracle import cpu_step  # the checker's eager path, timed on the host cores
     v, threads, desc = cpu_step.time_sample(shape, tokens=tokens)
     return {"value": round(v, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": desc["sample"], "layer_s": desc["layer_s"], "head_s": desc["head_s"]}
+            "sample": desc["sample"], "tokens": desc["tokens"], "layer_s": desc["layer_s"],
+            "head_s": desc["head_s"]}
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's eager CPU path (the oracle port) on the host cores."""
+    """--impl reference: the reference's eager CPU path (the oracle port) on the host cores.
+    A step is one bounded sample of the configured step (one decoder layer fwd + checkpoint
+    recompute + bwd, and the head + CE, on --cpu-tokens tokens): `steps` counts the samples
+    timed and `ms_per_step` is their mean measured wall time; `value` is the whole-model
+    tokens/s scaled from them (layers x layer time + head time), reported beside the parts."""
     if rank != 0:
         return
     from hackathon_b200.qlora import preset
     workload, _, _ = WORKLOADS[args.config]
     shape = preset(args.config)
     from oracle import cpu_step
-    vals = []
+    smp = cpu_step.CpuSample(shape, tokens=args.cpu_tokens)
     for _ in range(args.warmup):
-        cpu_step.time_sample(shape, tokens=args.cpu_tokens)
-    threads, desc = None, None
-    for _ in range(max(1, args.steps)):
-        v, threads, desc = cpu_step.time_sample(shape, tokens=args.cpu_tokens)
-        vals.append(v)
-    value = statistics.median(vals)
+        smp.run()
+    steps = max(1, args.steps)
+    tl = th = 0.0
+    for _ in range(steps):
+        a, b = smp.run()
+        tl += a
+        th += b
+    t_layer, t_head = tl / steps, th / steps
+    value = smp.scaled_tokens_per_s(t_layer, t_head)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(1e3 * args.cpu_tokens / value, 1), "higher_is_better": True,
+            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * (t_layer + t_head), 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": workload, "parallelism": "none (host CPU)",
                        "sample_tokens": args.cpu_tokens},
-            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
-                             "kind": "port", "sample": desc["sample"]},
+            "sample": {"what": smp.describe(), "tokens": args.cpu_tokens,
+                       "layer_s": round(t_layer, 4), "head_s": round(t_head, 4),
+                       "layers_scaled": shape.layers,
+                       "scaled_step_s": round(shape.layers * t_layer + t_head, 3),
+                       "ms_per_step_is": "the measured wall time of one sample"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s",
+                             "cores": smp.threads, "kind": "port", "sample": smp.describe()},
             "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -542,8 +513,6 @@ def main():
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--in-features", type=int, default=3584)
     ap.add_argument("--out-features", type=int, default=3584)
-    ap.add_argument("--worker", action="store_true",
-                    help="measure in this process (the default single-GPU run starts one)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -552,13 +521,6 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    if world == 1 and not (args.worker or args.kernel or args.profile_step):
-        # the library is loaded here as well (dlopen only, no CUDA call), so this process's
-        # modules show the native code its measuring child runs
-        from hackathon_b200 import _lib
-        _lib.load()
-        sys.exit(supervise([sys.executable, os.path.abspath(__file__), *sys.argv[1:],
-                            "--worker"]))
     if args.kernel:
         kernel_case(args)
         return
@@ -596,14 +558,13 @@ def main():
             dist.barrier()
 
     lib = _lib.load()
-    discarded = []    # runs in which a tensor-core kernel gave up a bounded wait
-    dog = Watchdog(lib, dev, rank, world, args)
+    dog = Watchdog(lib, local, rank, world, args)
 
     def device_error(where):
         """Reads (and clears) the tensor-core kernels' error flag after the current stream's work,
         agreed over the ranks so that every rank takes the same next step. A raised flag means a
-        kernel gave up a bounded wait and left its work undone: the run that raised it is not
-        measured, it is repeated."""
+        kernel gave up a bounded wait and left its work undone: the run that raised it ends the
+        measurement."""
         rc = lib.qb_device_error(_lib.stream(dev))
         msg = lib.qb_last_error().decode(errors="replace") if rc else None
         if world > 1:
@@ -612,8 +573,7 @@ def main():
             if int(f[0]) and msg is None:
                 msg = "raised on another rank"
         if msg:
-            discarded.append({"where": where, "error": msg})
-            _phase(f"{where}: {msg} - discarded")
+            _phase(f"{where}: {msg}")
         return msg
 
     def synced_step(i):
@@ -623,11 +583,11 @@ def main():
     _phase(f"{args.warmup} warm-up steps")
     try:
         for i in range(args.warmup):
-            run_clean(dog.watched(f"warm-up step {i}", STEP_DEADLINE_S,
+            run_checked(dog.watched(f"warm-up step {i}", STEP_DEADLINE_S,
                                   lambda: synced_step(i)), device_error, f"warm-up step {i}")
             _phase(f"warm-up step {i} done")
     except RunFailed as e:
-        fail(args, world, str(e), discarded)
+        fail(args, world, str(e), monitor_report(lib, local))
         return
 
     if args.profile_step:
@@ -667,10 +627,10 @@ def main():
         return clocks
 
     try:
-        clocks = run_clean(dog.watched("timed steps", STEP_DEADLINE_S * (1 + args.steps / 4),
+        clocks = run_checked(dog.watched("timed steps", STEP_DEADLINE_S * (1 + args.steps / 4),
                                        timed_steps), device_error, "timed steps")
     except RunFailed as e:
-        fail(args, world, str(e), discarded)
+        fail(args, world, str(e), monitor_report(lib, local))
         return
     ms = start.elapsed_time(end) / args.steps
     t = torch.tensor([ms], device=dev)
@@ -689,10 +649,10 @@ def main():
         return kt.summary()
 
     try:
-        ksum = run_clean(dog.watched("instrumented step", STEP_DEADLINE_S, instrumented_step),
+        ksum = run_checked(dog.watched("instrumented step", STEP_DEADLINE_S, instrumented_step),
                          device_error, "instrumented step")
     except RunFailed as e:
-        fail(args, world, str(e), discarded)
+        fail(args, world, str(e), monitor_report(lib, local))
         return
 
     _phase("end-to-end steps through train_step")
@@ -718,11 +678,11 @@ def main():
         return last
 
     try:
-        loss_value = run_clean(dog.watched("end-to-end steps",
+        loss_value = run_checked(dog.watched("end-to-end steps",
                                            STEP_DEADLINE_S * (1 + args.steps / 4), e2e_steps),
                                device_error, "end-to-end steps")
     except RunFailed as e:
-        fail(args, world, str(e), discarded)
+        fail(args, world, str(e), monitor_report(lib, local))
         return
     ems = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
     if world > 1:
@@ -780,7 +740,6 @@ def main():
             "kernels": table,
             "kernel_ms_per_step_ours": round(ours_ms, 2),
             "cpu_baseline": cpu,
-            "discarded_runs": discarded,
             "clocks": clocks.summary(),
             "peaks": pk,
         }

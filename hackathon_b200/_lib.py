@@ -50,6 +50,7 @@ _SIGNATURES = {
                    _p],
     "qb_ce_rows": [_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p, _p, _f32, _i32, _p],
     "qb_device_error": [_p],
+    "qb_monitor_report": [_i32, ctypes.c_char_p, _i64],
     "qb_gemm_bf16": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p],
     "qb_gemm2_bf16": [_p, _i64, _i32, _p, _i64, _i32, _i64, _p, _i64, _i32, _p, _i64, _i32, _i64,
                       _p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p],

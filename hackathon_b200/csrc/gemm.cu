@@ -205,14 +205,16 @@ int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
   return tcg::launch<A0, B0, A1, B1, BN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
 }
 
-// Which launches take the 2-SM kernel (K-major A operands): those with enough 256 x 256 pair
-// tiles to give every SM pair one (1.47-1.50 PFLOP/s against the one-CTA kernel's 1.32-1.38 at
-// the 7B projection shapes); smaller problems keep the one-CTA kernel's finer tiles. The
-// environment variable QB_GEMM_PAIR=0 / 1 turns it off / on regardless of size (A/B runs).
+// Which launches take the 2-SM kernel (K-major A operands). By default none: the one-CTA kernel
+// runs every GEMM (1.32-1.38 PFLOP/s at the 7B projection shapes; the 2-SM kernel measured
+// 1.47-1.50). The 2-SM kernel was the default for large launches when runs of the 7B step began
+// to stall, and it stays opt-in until that is explained. QB_GEMM_PAIR=2 takes it for launches
+// with enough 256 x 256 pair tiles to give every SM pair one; QB_GEMM_PAIR=1 for every K-major-A
+// launch (the tests' small and ragged shapes).
 bool use_pair(bool a_k_major, int64_t M, int64_t N) {
   static const int mode = [] {
     const char* e = std::getenv("QB_GEMM_PAIR");
-    return e ? std::atoi(e) : -1;
+    return e ? std::atoi(e) : 0;
   }();
   if (!a_k_major || mode == 0) return false;
   if (mode == 1) return true;

@@ -40,7 +40,9 @@ template <bool kBmn>
 __global__ void __launch_bounds__(kThreads, 1)
 lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ CUtensorMap mB,
                const __grid_constant__ CUtensorMap mC, const uint32_t* __restrict__ bits,
-               const Problem pb, int* err) {
+               const Problem pb, const tc::Ctl ctl) {
+  int* err = ctl.err;
+  tc::trace_begin(ctl);
   constexpr uint32_t kIdesc = tc::idesc_bf16(BM, BN, false, kBmn);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -247,6 +249,7 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem_base, 2 * BN);
+    if (lane == 0) tc::trace_end(ctl);
   }
 }
 
@@ -294,11 +297,11 @@ extern "C" int qb_gemm_bf16_mask_acc(const void* A, int64_t lda, const void* B, 
       return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
     configured[b_mn_major ? 1 : 0][dev] = true;
   }
-  int* err = tc_host::device_error_flag();
-  if (!err) return qb::fail(QB_ERR_CUDA, "%s: no device error flag", what);
   const int tiles = pb.num_m * pb.num_n;
   int grid = tc_host::sm_count();
   if (grid > tiles) grid = tiles;
-  kernel<<<grid, kThreads, kSmem, stream>>>(mV, mB, mC, bits, pb, err);
+  tc::Ctl ctl;
+  if (int s = tc_host::launch_ctl(&ctl, what)) return s;
+  kernel<<<grid, kThreads, kSmem, stream>>>(mV, mB, mC, bits, pb, ctl);
   return qb::check_launch(what);
 }

@@ -79,7 +79,9 @@ __device__ __forceinline__ uint32_t drop_pair(uint32_t xp, uint32_t word, int c,
 __global__ void __launch_bounds__(kThreads, 1)
 lora_xa_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mA,
                const __grid_constant__ CUtensorMap mXd, const uint32_t* __restrict__ bits,
-               __nv_bfloat16* __restrict__ u, const Problem pb, int* err) {
+               __nv_bfloat16* __restrict__ u, const Problem pb, const tc::Ctl ctl) {
+  int* err = ctl.err;
+  tc::trace_begin(ctl);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -298,6 +300,7 @@ lora_xa_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ C
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem_base, tcols);
+    if (lane == 0) tc::trace_end(ctl);
   }
 }
 
@@ -361,11 +364,11 @@ extern "C" int qb_lora_xa(const void* x, int64_t ldx, const void* a, int64_t lda
       return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
     configured[dev] = true;
   }
-  int* err = tc_host::device_error_flag();
-  if (!err) return qb::fail(QB_ERR_CUDA, "%s: no device error flag", what);
   int grid = tc_host::sm_count();
   if (grid > pb.num_m) grid = pb.num_m;
+  tc::Ctl ctl;
+  if (int s = tc_host::launch_ctl(&ctl, what)) return s;
   lora_xa_kernel<<<grid, kThreads, kSmem, stream>>>(mX, mA, mXd, bits,
-                                                    static_cast<__nv_bfloat16*>(u), pb, err);
+                                                    static_cast<__nv_bfloat16*>(u), pb, ctl);
   return qb::check_launch(what);
 }

@@ -267,17 +267,25 @@ extern "C" int qb_nf4_quantize(const void* w, int w_dtype, int64_t n_weights, in
 // The partial sums live in this file-scope device array instead of a caller-provided workspace.
 // Every GPU that loads the library holds these 4 KiB until the process exits. Host code must
 // not pass `g_dq_scratch` to a kernel (on the host it names a stand-in, not device memory): the
-// device address is looked up once per device with cudaGetSymbolAddress and cached. Every slot a
+// device address is looked up with cudaGetSymbolAddress on a device's first call and cached
+// with the context it belongs to; a call under another context of that device (after
+// cudaDeviceReset, which destroys the old one) looks it up again. The first call on a device
+// makes that CUDA call, so it belongs before any stream capture. Every slot a
 // call uses is written by its first kernel before its second kernel reads it, so nothing needs
 // clearing between calls; calls whose kernels overlap on the GPU (different streams, or
 // different host threads on one device) race on the array.
 constexpr int kStaticPartials = 512;
 static __device__ __align__(256) double g_dq_scratch[kStaticPartials];
 
+namespace tc_host {
+void* current_context_handle();   // tc_host.cu: this thread's current driver context
+}
+
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
+void* g_scratch_ctx[kMaxDevices] = {};
 
 int static_scratch(double** out) {
   int dev = -1;
@@ -285,12 +293,14 @@ int static_scratch(double** out) {
   if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "nf4_double_quant_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return qb::fail(QB_ERR_UNSUPPORTED, "nf4_double_quant_noalloc: device %d", dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
+  void* ctx = tc_host::current_context_handle();
+  if (!g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_dq_scratch);
     if (e != cudaSuccess || !p)
       return qb::fail(QB_ERR_CUDA, "nf4_double_quant_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = tc_host::current_context_handle();   // current now, if it was not
   }
   *out = static_cast<double*>(g_scratch_addr[dev]);
   return QB_OK;

@@ -21,6 +21,28 @@ namespace tc {
 // ------------------------------------------------------------------------------------------
 // error flag + bounded waits. A wait that gives up records `code` in *err (first one wins) and
 // returns false; every role checks the flag and leaves its loop, so the CTA drains and exits.
+//
+// *err is word 0 of the device's ErrBlock. Its `host` member points into pinned host memory
+// mapped into the device (the launch monitor, tc_host.cu): the wait that raises the flag also
+// writes its site there, so a host thread can read it with a plain load while the device is
+// still busy, with no CUDA call that could queue behind the stuck work.
+
+struct ErrBlock {
+  int flag;          // polled by every bounded wait (device memory: cheap to read)
+  int pad;
+  int* host;         // mapped host record {site, block, sm} or null
+};
+
+// Per launch: the error flag and the launch monitor's trace. Each CTA writes 2 * seq into
+// trace[blockIdx.x] as it starts and 2 * seq + 1 once it has released TMEM and is leaving,
+// so a CTA that never leaves (and the launch it belongs to) can be named from the host.
+struct Ctl {
+  int* err;
+  uint32_t* trace;   // mapped host memory, kTraceSlots entries, or null
+  uint32_t seq;      // the host's launch sequence number
+};
+
+constexpr int kTraceSlots = 1024;
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 
@@ -39,6 +61,40 @@ __device__ __forceinline__ uint64_t sm_cycles() {
   uint64_t c;
   asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
   return c;
+}
+
+__device__ __forceinline__ uint32_t sm_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
+// System-scope store into mapped host memory (the launch monitor): no cache keeps it.
+__device__ __forceinline__ void st_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void trace_begin(const Ctl& c) {
+  if (threadIdx.x == 0 && c.trace && blockIdx.x < static_cast<unsigned>(kTraceSlots))
+    st_sys(c.trace + blockIdx.x, 2u * c.seq);
+}
+
+__device__ __forceinline__ void trace_end(const Ctl& c) {
+  if (c.trace && blockIdx.x < static_cast<unsigned>(kTraceSlots))
+    st_sys(c.trace + blockIdx.x, 2u * c.seq + 1u);
+}
+
+// Raises the flag with `code` (first one wins) and, for the first, writes the site, the CTA
+// and its SM into the mapped host record.
+__device__ __forceinline__ void raise_error(int* err, int code) {
+  if (atomicCAS(err, 0, code) != 0) return;
+  int* host = reinterpret_cast<ErrBlock*>(err)->host;
+  if (host) {
+    st_sys(reinterpret_cast<uint32_t*>(host) + 1, blockIdx.x);
+    st_sys(reinterpret_cast<uint32_t*>(host) + 2, sm_id());
+    st_sys(reinterpret_cast<uint32_t*>(host), static_cast<uint32_t>(code));
+    __threadfence_system();
+  }
 }
 
 struct WaitClock {
@@ -105,7 +161,7 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, in
     if ((i & kWaitCheckMask) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
       if (clk.expired(limit_ns)) {
-        atomicCAS(err, 0, code);
+        raise_error(err, code);
         return false;
       }
     }
@@ -124,13 +180,11 @@ __device__ __forceinline__ bool mbar_wait_quiet(uint64_t* bar, uint32_t parity) 
   return true;
 }
 
-// Error path only: lets copies that no barrier of this CTA can observe land before the CTA
-// leaves (the 2-SM kernel's follower loads complete on the leader's barrier, in phases the
-// leader may not have armed once both stopped at different items). 100 us on both clocks:
-// a stage's copies land in a few microseconds.
-__device__ __forceinline__ void error_grace() {
-  const WaitClock clk;
-  while (!clk.expired(100000ull)) __nanosleep(2000);
+// Counts `bytes` of a phase's expected transaction bytes as arrived without a copy (the error
+// path of the 2-SM kernel: the bytes of loads its partner never issued).
+__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ bool failed(int* err) {
@@ -228,9 +282,12 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       : "memory");
 }
 
-// 32 lanes x 32 columns of fp32: this thread gets its lane's 32 consecutive columns.
+// 32 lanes x 32 columns of fp32: this thread gets its lane's 32 consecutive columns. The load is
+// warp-collective (.sync.aligned): the warp is reconverged first, so a lane-dependent `continue`
+// in a caller's previous loop iteration cannot leave it split at the instruction.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
+  __syncwarp();
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -271,6 +328,11 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
                : "memory");
 }
 
+// 32-bit store into a shared variable of another CTA of the cluster (a mapa address).
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
                    cluster_addr),
@@ -300,17 +362,20 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     if ((i & kWaitCheckMask) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
       if (clk.expired(kWaitLimitNs)) {
-        atomicCAS(err, 0, code);
+        raise_error(err, code);
         return false;
       }
     }
   }
 }
 
-__device__ __forceinline__ bool mbar_wait_cluster_quiet(uint64_t* bar, uint32_t parity) {
+// Bounded wait that does not look at the error flag (the error path, and the pair's teardown
+// handshake, which must be waited out whether or not a wait gave up).
+__device__ __forceinline__ bool mbar_wait_cluster_quiet(uint64_t* bar, uint32_t parity,
+                                                        uint64_t limit_ns = kWaitLimitNs / 16) {
   const WaitClock clk;
   while (!mbar_try_wait_cluster(bar, parity))
-    if (clk.expired(kWaitLimitNs / 16)) return false;
+    if (clk.expired(limit_ns)) return false;
   return true;
 }
 
@@ -410,9 +475,13 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uin
 // SM count of the current device (cached).
 int sm_count();
 
-// Per-device error flag the tensor-core kernels raise when a bounded wait gives up.
+// Per-device error flag the tensor-core kernels raise when a bounded wait gives up (word 0 of
+// the device's tc::ErrBlock).
 int* device_error_flag();
 // Reads and clears the current device's flag (synchronises the stream).
 int take_device_error(cudaStream_t stream);
+// The control block of one tensor-core launch on the current device: the error flag and the
+// launch monitor's trace, with the next launch sequence number, recorded under `what`.
+int launch_ctl(tc::Ctl* ctl, const char* what);
 
 }  // namespace tc_host

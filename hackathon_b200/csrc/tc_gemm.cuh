@@ -72,8 +72,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mB0,
                const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mB1,
                const __grid_constant__ CUtensorMap mB0b, const __grid_constant__ CUtensorMap mB1b,
-               const Problem pb, Epi epi, int* err) {
+               const Problem pb, Epi epi, const tc::Ctl ctl) {
   using C = Cfg<BN>;
+  int* err = ctl.err;
+  tc::trace_begin(ctl);
   constexpr int STAGES = C::STAGES;
   constexpr uint32_t kIdesc0 = tc::idesc_bf16(BM, BN, is_mn(A0), is_mn(B0));
   constexpr uint32_t kIdesc1 = tc::idesc_bf16(BM, BN, is_mn(A1), is_mn(B1));
@@ -234,6 +236,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (lane == 0) tc::trace_end(ctl);
   }
 }
 
@@ -255,16 +258,16 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
     if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
     configured[dev] = true;
   }
-  int* err = tc_host::device_error_flag();
-  if (!err) return qb::fail(QB_ERR_CUDA, "%s: no device error flag", what);
   const int tiles = pb.num_m * pb.num_n;
   if (tiles == 0) return QB_OK;
   int grid = tc_host::sm_count();
   if (grid > tiles) grid = tiles;
   if ((B0 == kTmaKDual && !mB0b) || (B1 == kTmaKDual && !mB1b))
     return qb::fail(QB_ERR_INVALID, "%s: dual B needs its second tensor map", what);
+  tc::Ctl ctl;
+  if (int s = tc_host::launch_ctl(&ctl, what)) return s;
   kernel<<<grid, kThreads, C::SMEM, stream>>>(mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
-                                              mB1b ? *mB1b : mB1, pb, epi, err);
+                                              mB1b ? *mB1b : mB1, pb, epi, ctl);
   return qb::check_launch(what);
 }
 

@@ -22,8 +22,10 @@
 // which the other CTA armed its own bytes on the leader's barrier and the leader committed to each
 // CTA separately ran at half this throughput (0.72 against 1.47-1.50 PFLOP/s).
 // 6 stages of 32 KiB, accumulators double-buffered (2 x 256 TMEM columns). Every wait is bounded;
-// a wait that gives up raises the device error flag, every role drains out, and the two CTAs meet
-// at a cluster barrier before TMEM is released. No load multicasts.
+// a wait that gives up raises the device error flag and every role drains out (the two producers
+// first agree on what each issued, so that every copy in flight completes on an armed phase and
+// is waited for), and the two CTAs meet on a bounded mbarrier handshake before TMEM is released.
+// No load multicasts.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -60,7 +62,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mB0,
                     const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mB1,
                     const __grid_constant__ CUtensorMap mB0b, const __grid_constant__ CUtensorMap mB1b,
-                    const Problem pb, Epi epi, int* err) {
+                    const Problem pb, Epi epi, const tc::Ctl ctl) {
+  int* err = ctl.err;
+  tc::trace_begin(ctl);
   constexpr uint32_t kIdesc0 = tc::idesc_bf16(2 * BMC, BN, false, B0 == kTmaMN);
   constexpr uint32_t kIdesc1 = tc::idesc_bf16(2 * BMC, BN, false, B1 == kTmaMN);
   extern __shared__ uint8_t smem_raw[];
@@ -71,7 +75,11 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
   uint64_t* tfull = empty + kStages;    // each CTA: accumulator b ready
   uint64_t* tempty = tfull + 2;         // leader: both CTAs' epilogues drained accumulator b
   uint64_t* drain = tempty + 2;         // leader: every MMA completed (teardown)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* peer_done = drain + 1;      // each CTA: the other CTA has finished (teardown)
+  uint64_t* stopped = peer_done + 1;    // each CTA: the other producer's issued count is here
+  uint64_t* drained = stopped + 1;      // follower: the leader waited out both CTAs' copies
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drained + 1);
+  uint32_t* peer_issued = tmem_slot + 1;  // written by the other CTA's producer (error path)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_rank();
@@ -80,6 +88,9 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
     for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
     for (int b = 0; b < 2; ++b) { tc::mbar_init(&tfull[b], 1); tc::mbar_init(&tempty[b], 8); }
     tc::mbar_init(drain, 1);
+    tc::mbar_init(peer_done, 1);
+    tc::mbar_init(stopped, 1);
+    tc::mbar_init(drained, 1);
     tc::fence_mbar_init();
   }
   if (warp == 1) {
@@ -143,16 +154,31 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
         if (!ok) break;
       }
       if (tc::failed(err)) {
-        if (leader)   // the leader's barriers count both CTAs' copies
-          for (int i = 0; i < kStages && i < issued; ++i) {
-            if (--s < 0) { s = kStages - 1; ph ^= 1; }
-            tc::mbar_wait_quiet(&full[s], ph);
-          }
-        // A wait that finds its phase complete does not look at the flag, so after a give-up
-        // the two producers may stop at different items: copies of the follower into a phase
-        // the leader never armed are seen by no barrier. Both wait them out here, before the
-        // pair meets at the final cluster barrier and leaves.
-        tc::error_grace();
+        // After a give-up the two producers may have stopped at different items (a wait that
+        // finds its phase complete does not look at the flag), and all their copies complete on
+        // the leader's full[] barriers. Each tells the other how many items it issued; the
+        // leader then makes every phase either CTA started completable - arming the ones only
+        // the follower issued (its bytes alone), counting as arrived the follower bytes of the
+        // ones only the leader issued - and waits for the last phase of each stage, which
+        // completes once every copy in flight has landed. The follower leaves only after that.
+        const uint32_t peer = rank ^ 1u;
+        tc::st_cluster_u32(tc::mapa(peer_issued, peer), static_cast<uint32_t>(issued));
+        tc::mbar_arrive_cluster(tc::mapa(stopped, peer));
+        const bool heard = tc::mbar_wait_cluster_quiet(stopped, 0);
+        if (leader) {
+          const long f = heard ? static_cast<long>(*reinterpret_cast<volatile uint32_t*>(peer_issued))
+                               : issued;
+          for (long i = issued; i < f; ++i)   // follower-only items: arm the follower's bytes
+            tc::mbar_expect_tx(&full[i % kStages], kStage);
+          for (long i = f; i < issued; ++i)   // leader-only items: the follower's bytes never come
+            tc::mbar_complete_tx(&full[i % kStages], kStage);
+          const long n = f > issued ? f : issued;
+          for (long i = n - kStages < 0 ? 0 : n - kStages; i < n; ++i)
+            tc::mbar_wait_quiet(&full[i % kStages], static_cast<uint32_t>((i / kStages) & 1));
+          tc::mbar_arrive_cluster(tc::mapa(drained, 1));
+        } else if (heard) {
+          tc::mbar_wait_cluster_quiet(drained, 0);
+        }
       }
     }
   } else if (warp == 1) {
@@ -213,12 +239,20 @@ tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_consta
     }
   }
 
+  // Neither CTA leaves while the pair's MMAs or signals may touch it: each tells the other it is
+  // done (its last access to the other's shared memory) and waits for the other's word, bounded
+  // (a partner that never comes raises the flag instead of holding this SM for good).
   tc::fence_before_sync();
   __syncthreads();
-  tc::cluster_sync();   // neither CTA leaves while the pair's MMAs or signals may touch it
+  if (threadIdx.x == 0) {
+    tc::mbar_arrive_cluster(tc::mapa(peer_done, rank ^ 1u));
+    if (!tc::mbar_wait_cluster_quiet(peer_done, 0, tc::kWaitLimitNs)) tc::raise_error(err, 26);
+  }
+  __syncthreads();
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc_pair(tmem_base, 2 * BN);
+    if (lane == 0) tc::trace_end(ctl);
   }
 }
 
@@ -241,10 +275,10 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
       return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
     configured[dev] = true;
   }
-  int* err = tc_host::device_error_flag();
-  if (!err) return qb::fail(QB_ERR_CUDA, "%s: no device error flag", what);
   const int tiles = pb.num_m * pb.num_n;
   if (tiles == 0) return QB_OK;
+  tc::Ctl ctl;
+  if (int s = tc_host::launch_ctl(&ctl, what)) return s;
   int pairs = tc_host::sm_count() / 2;
   if (pairs > tiles) pairs = tiles;
   cudaLaunchConfig_t cfg = {};
@@ -260,7 +294,7 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
-                                     mB1b ? *mB1b : mB1, pb, epi, err);
+                                     mB1b ? *mB1b : mB1, pb, epi, ctl);
   if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: launch: %s", what, cudaGetErrorString(e));
   return qb::check_launch(what);
 }

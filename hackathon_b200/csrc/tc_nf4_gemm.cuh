@@ -147,7 +147,9 @@ template <int A0, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant__ CUtensorMap mB0,
               const __grid_constant__ CUtensorMap mB1, const NfProblem pb,
-              const Nf4Operand nf4, const LoraA lora, Epi epi, int* err) {
+              const Nf4Operand nf4, const LoraA lora, Epi epi, const tc::Ctl ctl) {
+  int* err = ctl.err;
+  tc::trace_begin(ctl);
   static_assert(A0 == kNf4K || A0 == kNf4MN, "A0 is an NF4 source");
   constexpr bool kMN = A0 == kNf4MN;
   constexpr uint32_t kIdesc0 = tc::idesc_bf16(BM, kBN, kMN, false);
@@ -397,6 +399,7 @@ tc_nf4_kernel(const __grid_constant__ CUtensorMap mCodes, const __grid_constant_
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem_base, 2 * kBN);
+    if (lane == 0) tc::trace_end(ctl);
   }
 }
 
@@ -414,13 +417,13 @@ int launch_nf4(const CUtensorMap& mCodes, const CUtensorMap& mB0, const CUtensor
     if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
     configured[dev] = true;
   }
-  int* err = tc_host::device_error_flag();
-  if (!err) return qb::fail(QB_ERR_CUDA, "%s: no device error flag", what);
   const int tiles = pb.num_m * pb.num_n;
   if (tiles == 0) return QB_OK;
   int grid = tc_host::sm_count();
   if (grid > tiles) grid = tiles;
-  kernel<<<grid, kThreads, kSmem, stream>>>(mCodes, mB0, mB1, pb, nf4, lora, epi, err);
+  tc::Ctl ctl;
+  if (int s = tc_host::launch_ctl(&ctl, what)) return s;
+  kernel<<<grid, kThreads, kSmem, stream>>>(mCodes, mB0, mB1, pb, nf4, lora, epi, ctl);
   return qb::check_launch(what);
 }
 

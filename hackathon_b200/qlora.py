@@ -118,22 +118,29 @@ def _mask_bits(x2, mod, p, seed):
     return bits
 
 
-# U = dropout(x) A^T in one kernel from x and the mask bits (qb_lora_xa); False composes
-# qb_dropout_apply (xd to HBM) with a GEMM instead - the same numbers up to accumulation order
-FUSED_ADAPTER_INPUT = True
+# U = dropout(x) A^T in one kernel from x and the mask bits (qb_lora_xa) when True; False (the
+# default) composes the dropout pass (xd to HBM: qb_dropout_mask, or qb_dropout_apply from
+# recorded bits) with the tcgen05 GEMM - the same numbers up to accumulation order. qb_lora_xa
+# entered the step together with the 2-SM GEMM and the side-stream masks, when runs of the 7B
+# step began to stall; it stays opt-in until that is explained.
+FUSED_ADAPTER_INPUT = False
 
 
 def _adapter_input(x2, mod, a16, p, seed, keep_xd, u_out=None):
     """(xd, U = xd a16^T, bits, scale) of one projection with xd = dropout(x2) * scale: U comes
     from x2 and the mask bits in one kernel (qb_lora_xa); xd is stored only when the backward
     will read it (keep_xd), else an empty placeholder stands in its saved slot."""
+    from .gemm import gemm
     from .lora import lora_xa, lora_xa_ok
     if (not FUSED_ADAPTER_INPUT or not lora_xa_ok(x2, a16)
             or (p > 0 and x2.shape[1] % 8)):
         xd, bits, scale = _dropped(x2, mod, p, seed)
-        u = xd @ a16.t()
-        if u_out is not None:
-            u = u_out.copy_(u)
+        if u_out is not None and u_out.stride(-1) == 1 and u_out.stride(0) % 8 == 0:
+            u = gemm(xd, a16, out=u_out)
+        else:
+            u = gemm(xd, a16)
+            if u_out is not None:
+                u = u_out.copy_(u)
         return xd, u, bits, scale
     if p <= 0:
         return x2, lora_xa(x2, a16, out=u_out), None, 1.0
@@ -490,7 +497,10 @@ class QwenQLoRA(torch.nn.Module):
             head = torch.empty(shape.vocab, shape.hidden, device=dev, dtype=torch.bfloat16)
             self.lm_head = head.normal_(0.0, 0.02, generator=gen)
         self.checkpoint = checkpoint
-        self.mask_prefetch = True   # draw layer i+1's dropout masks beside layer i's GEMMs
+        # True: draw layer i+1's dropout masks on a side stream beside layer i's GEMMs. Off by
+        # default: it entered the step together with the 2-SM GEMM and qb_lora_xa, when runs of
+        # the 7B step began to stall, and stays opt-in until that is explained.
+        self.mask_prefetch = False
         self._rope = {}
         self.step_seed = 0
 

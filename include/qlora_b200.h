@@ -357,6 +357,15 @@ int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight, int64
  * QB_ERR_TIMEOUT when a kernel gave up one of its bounded waits (its output is then invalid). */
 int qb_device_error(cudaStream_t stream);
 
+/* Report of this process's launch monitor for `device`, no counterpart in the reference. The
+ * tensor-core kernels write pinned host memory mapped into the device: each CTA the launch
+ * sequence number it started and, once it has released its tensor memory, finished; a bounded
+ * wait that gives up writes its site, CTA and SM. This call formats that record into buf (at most
+ * len bytes, NUL-terminated) from host memory alone - no CUDA call - so a watchdog thread can
+ * read it while the device is stuck: the last launch issued, the last one whose CTAs all
+ * finished, and each launch with CTAs that started and never finished. */
+int qb_monitor_report(int device, char* buf, int64_t len);
+
 /* Self-test of the failure path, no counterpart in the reference: launches one thread that waits
  * (bounded, limit_ns between 1 ms and 2 s) on an mbarrier nothing arrives on, so the wait gives up
  * and raises the device error flag as a stuck kernel would; qb_device_error then reports

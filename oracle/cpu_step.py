@@ -117,45 +117,60 @@ def usable_cores():
     return max(1, n or 1)
 
 
-def time_sample(shape, tokens=128, threads=None, repeats=1, seed=0):
-    """(tokens/s scaled to the whole model, description dict) of the eager CPU path."""
-    threads = threads or usable_cores()
-    torch.set_num_threads(threads)
-    rng = np.random.default_rng(seed)
-    torch.manual_seed(seed)
-    layer = CpuDecoderLayer(shape, rng, threads)
-    cos, sin = ops_ref.qwen_cos_sin(1, tokens, shape.head_dim, shape.theta, torch.bfloat16)
-    h0 = (torch.randn(1, tokens, shape.hidden) * 0.5).to(torch.bfloat16)
-    head = (torch.randn(shape.vocab, shape.hidden) * 0.02).to(torch.bfloat16)
-    labels = torch.randint(0, shape.vocab, (1, tokens))
+class CpuSample:
+    """The bounded sample of the eager CPU step, built once: one decoder layer of `shape` on
+    `tokens` tokens and the lm_head + CE on the same rows. run() times one sample and returns
+    (layer seconds, head seconds)."""
 
-    def layer_step():
+    def __init__(self, shape, tokens=128, threads=None, seed=0):
+        self.shape, self.tokens = shape, tokens
+        self.threads = threads or usable_cores()
+        torch.set_num_threads(self.threads)
+        rng = np.random.default_rng(seed)
+        torch.manual_seed(seed)
+        self.layer = CpuDecoderLayer(shape, rng, self.threads)
+        self.cos, self.sin = ops_ref.qwen_cos_sin(1, tokens, shape.head_dim, shape.theta,
+                                                  torch.bfloat16)
+        self.h0 = (torch.randn(1, tokens, shape.hidden) * 0.5).to(torch.bfloat16)
+        self.head = (torch.randn(shape.vocab, shape.hidden) * 0.02).to(torch.bfloat16)
+        self.labels = torch.randint(0, shape.vocab, (1, tokens))
+
+    def run(self):
+        t0 = time.perf_counter()
         with torch.no_grad():            # the checkpoint's first forward
-            layer(h0, cos, sin)
-        h = h0.clone().requires_grad_()
-        out = layer(h, cos, sin)         # recompute in backward
+            self.layer(self.h0, self.cos, self.sin)
+        h = self.h0.clone().requires_grad_()
+        out = self.layer(h, self.cos, self.sin)   # recompute in backward
         out.float().sum().backward()
-
-    def head_step():
-        hn = h0.clone().float().requires_grad_()
-        loss = ops_ref.ce_ref(hn, head, labels, matmul_dtype=torch.bfloat16)[0]
+        t1 = time.perf_counter()
+        hn = self.h0.clone().float().requires_grad_()
+        loss = ops_ref.ce_ref(hn, self.head, self.labels, matmul_dtype=torch.bfloat16)[0]
         loss.backward()
+        return t1 - t0, time.perf_counter() - t1
 
-    layer_step()  # warm-up (allocations, thread pools)
-    t0 = time.perf_counter()
+    def scaled_tokens_per_s(self, t_layer, t_head):
+        """tokens/s of the whole model's step, from one sample's layer and head times."""
+        return self.tokens / (self.shape.layers * t_layer + t_head)
+
+    def describe(self):
+        s = self.shape
+        return (f"1 decoder layer ({s.name} shapes) fwd + checkpoint recompute + bwd on "
+                f"{self.tokens} tokens (seq {self.tokens}), NF4 rebuilt by the C oracle per "
+                f"forward and backward, + lm_head/CE fwd+bwd on the same rows; the model figure "
+                f"is {s.layers} x layer + head; attention at seq {self.tokens}")
+
+
+def time_sample(shape, tokens=128, threads=None, repeats=1, seed=0):
+    """(tokens/s scaled to the whole model, threads, description dict) of the eager CPU path:
+    one warm-up sample, then `repeats` timed ones."""
+    smp = CpuSample(shape, tokens, threads, seed)
+    smp.run()  # warm-up (allocations, thread pools)
+    tl = th = 0.0
     for _ in range(repeats):
-        layer_step()
-    t_layer = (time.perf_counter() - t0) / repeats
-    t0 = time.perf_counter()
-    for _ in range(repeats):
-        head_step()
-    t_head = (time.perf_counter() - t0) / repeats
-    step = shape.layers * t_layer + t_head
-    desc = {
-        "sample": (f"1 decoder layer ({shape.name} shapes) fwd + checkpoint recompute + bwd on "
-                   f"{tokens} tokens (seq {tokens}), NF4 rebuilt by the C oracle per forward "
-                   f"and backward, x{shape.layers} layers, + lm_head/CE fwd+bwd on the same "
-                   f"rows; attention at seq {tokens}"),
-        "layer_s": round(t_layer, 4), "head_s": round(t_head, 4),
-    }
-    return tokens / step, threads, desc
+        a, b = smp.run()
+        tl += a
+        th += b
+    t_layer, t_head = tl / repeats, th / repeats
+    desc = {"sample": smp.describe(), "tokens": tokens, "layer_s": round(t_layer, 4),
+            "head_s": round(t_head, 4)}
+    return smp.scaled_tokens_per_s(t_layer, t_head), smp.threads, desc

@@ -1,8 +1,9 @@
-"""bench.py's measuring process (`--worker`) run end to end on the CPU, with only what needs a GPU
-replaced: CUDA events / streams / synchronisation, the model's training step, the per-call
-kernel timer and the tensor-core error flag. It checks the Python of every phase (warm-up under
-the watchdog, timed steps, instrumented step, end-to-end steps, the JSON line), and that a run
-whose kernels raised the error flag is repeated and listed, never measured."""
+"""bench.py's measurement run end to end on the CPU, with only what needs a GPU replaced: CUDA
+events / streams / synchronisation, the model's training step, the per-call kernel timer, the
+tensor-core error flag and the launch monitor. It checks the Python of every phase (warm-up
+under the watchdog, timed steps, instrumented step, end-to-end steps, the JSON line), and that a
+run whose kernels raised the error flag ends the measurement with the evidence - never measured,
+never repeated."""
 
 import json
 import os
@@ -72,6 +73,10 @@ class FakeLib:
     def qb_last_error(self):
         return b"a tensor-core kernel gave up a bounded wait (site 3)"
 
+    def qb_monitor_report(self, device, buf, n):
+        buf.value = b"launches issued: 40 (last gemm2_bf16); last wait that gave up: site 3"
+        return 0
+
 
 class FakeTimer:
     def __enter__(self):
@@ -109,14 +114,14 @@ def _run(monkeypatch, capsys, lib, steps=2):
     monkeypatch.setattr(dp, "global_label_count", lambda lb, group=None: torch.tensor(8.0))
     monkeypatch.setenv("WORLD_SIZE", "1")
     monkeypatch.setenv("RANK", "0")
-    monkeypatch.setattr(sys, "argv", ["bench.py", "--worker", "--config", "0.5b", "--steps",
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--config", "0.5b", "--steps",
                                       str(steps), "--warmup", "3", "--no-cpu-baseline"])
     bench.main()
     out = capsys.readouterr().out.strip().splitlines()
     return json.loads(out[-1]), steps_run
 
 
-def test_worker_prints_one_complete_line(monkeypatch, capsys):
+def test_run_prints_one_complete_line(monkeypatch, capsys):
     line, steps_run = _run(monkeypatch, capsys, FakeLib())
     # 3 warm-up + 2 timed + 1 instrumented + 2 end-to-end steps
     assert len(steps_run) == 8
@@ -127,23 +132,20 @@ def test_worker_prints_one_complete_line(monkeypatch, capsys):
     assert line["e2e"]["last_loss"] == 11.5
     assert line["roofline"]["kernel"] == "qb_gemm2_bf16"
     assert line["roofline"]["bound"] == "tensor"
-    assert line["discarded_runs"] == []
     assert line["gpu_launches"] == 6 * 2
     assert "reasons" in line["clocks"]
 
 
-def test_worker_repeats_a_run_that_raised_the_flag(monkeypatch, capsys):
-    # flag reads: 3 warm-up steps (1-3), the timed block (4: raised, 5: clean), instrumented (6),
-    # end-to-end (7)
+def test_run_that_raised_the_flag_ends_the_measurement(monkeypatch, capsys):
+    # flag reads: 3 warm-up steps (1-3), the timed block (4: raised)
     line, steps_run = _run(monkeypatch, capsys, FakeLib(raised_on={4}))
-    assert len(steps_run) == 10                             # the timed block ran twice
-    assert [d["where"] for d in line["discarded_runs"]] == ["timed steps (attempt 0)"]
-    assert "site 3" in line["discarded_runs"][0]["error"]
-    assert line["value"] is not None
-
-
-def test_worker_gives_up_after_every_attempt_raised_the_flag(monkeypatch, capsys):
-    line, steps_run = _run(monkeypatch, capsys, FakeLib(raised_on=set(range(1, 100))))
+    assert len(steps_run) == 3 + 2                          # nothing after the timed block
     assert line["value"] is None
-    assert "warm-up step 0" in line["error"]
-    assert len(line["discarded_runs"]) == bench.MAX_REPEATS + 1
+    assert "timed steps" in line["error"] and "site 3" in line["error"]
+    assert "site 3" in line["launch_monitor"]
+
+
+def test_flag_raised_in_warm_up_ends_it_there(monkeypatch, capsys):
+    line, steps_run = _run(monkeypatch, capsys, FakeLib(raised_on={1}))
+    assert len(steps_run) == 1
+    assert line["value"] is None and "warm-up step 0" in line["error"]

@@ -68,6 +68,13 @@ def test_error_message_plumbing_without_gpu():
     with pytest.raises(RuntimeError, match="p must be < 1"):
         _lib.call("qb_dropout_bits", fake, 16, 64, 1, 1.0, 2, None)
     assert lib.qb_dropout_bits(None, 0, 64, 1, 0.1, 2, None) == 0     # empty: nothing to do
+    # the launch monitor's report reads host memory only: it answers without a GPU (nothing
+    # launched yet) and refuses a missing buffer or an impossible device index
+    buf = ctypes.create_string_buffer(256)
+    assert lib.qb_monitor_report(0, buf, len(buf)) == 0
+    assert b"no launch monitor" in buf.value
+    assert lib.qb_monitor_report(0, None, 16) == 1
+    assert lib.qb_monitor_report(99, buf, len(buf)) == 1
 
 
 @pytest.mark.parametrize("op", ["rmsnorm", "rope", "swiglu", "dropout", "dequant"])
@@ -163,7 +170,8 @@ def test_ctypes_bindings_match_the_header_declarations():
         return {"int64_t": "i64", "int": "i32", "float": "f32", "uint64_t": "u64"}[t]
 
     def py_kind(t):
-        if t is ctypes.c_void_p or isinstance(t, type) and issubclass(t, ctypes._Pointer):
+        if t in (ctypes.c_void_p, ctypes.c_char_p) or isinstance(t, type) and \
+                issubclass(t, ctypes._Pointer):
             return "ptr"
         return {ctypes.c_int64: "i64", ctypes.c_int: "i32", ctypes.c_float: "f32",
                 ctypes.c_uint64: "u64"}[t]
