@@ -142,10 +142,12 @@ def philox_uniform(seed, offsets):
     return x.astype(np.float32) * np.float32(4.6566127342e-10)
 
 
-def dropout_keep(seed, rows, cols, p):
+def dropout_keep(seed, rows, cols, p, row_range=None):
     """Boolean keep mask [rows, cols] of the reference's dropout kernel (lora.py:40-43):
-    offset = int32(row * cols + col), keep = rand > p."""
-    r = np.arange(rows, dtype=np.int64)[:, None]
+    offset = int32(row * cols + col), keep = rand > p. row_range=(lo, hi): only those rows of
+    the [rows, cols] tensor's mask (offsets as in the whole tensor)."""
+    lo, hi = (0, rows) if row_range is None else row_range
+    r = np.arange(lo, hi, dtype=np.int64)[:, None]
     c = np.arange(cols, dtype=np.int64)[None, :]
     return philox_uniform(seed, r * cols + c) > np.float32(p)
 

@@ -135,6 +135,71 @@ def test_fused_ce_baseline_shape_rows(cuda):
     torch.testing.assert_close(h.grad[0].float().cpu(), dh_ref, rtol=2e-2, atol=2e-3)
 
 
+def _fp32_ce_reference(hidden2d, weight, target, chunk=1024):
+    """The reference's loss (test_cross_entropy.py:9-30: fp32 logits, logsumexp, mean over the
+    labelled rows) and dH = dZ W with dZ = (softmax - onehot) / n, chunked over rows so no more
+    than `chunk` rows of fp32 logits exist at a time. Exact products of the bf16 operands with
+    fp32 sums (TF32 off), on the GPU: a plain PyTorch fp32 reference of this floating-point op."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        w = weight.float()
+        n = int((target != -100).sum())
+        tok = torch.empty(target.shape[0], dtype=torch.float32, device=hidden2d.device)
+        dh = torch.empty(hidden2d.shape, dtype=torch.float32, device=hidden2d.device)
+        for a in range(0, target.shape[0], chunk):
+            z = hidden2d[a:a + chunk].float() @ w.t()
+            t = target[a:a + chunk]
+            lab = t != -100
+            lse = torch.logsumexp(z, dim=1)
+            zl = z.gather(1, t.clamp(min=0)[:, None])[:, 0]
+            tok[a:a + chunk] = torch.where(lab, lse - zl, torch.zeros_like(lse))
+            p = torch.softmax(z, dim=1)
+            p[torch.arange(t.shape[0], device=t.device)[lab], t[lab]] -= 1.0
+            p[~lab] = 0.0
+            dh[a:a + chunk] = (p / n) @ w
+            del z, p
+        return tok.sum() / n, tok, dh
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@pytest.mark.parametrize("store_logits", [False, True])
+def test_fused_ce_cfg3_full_size(cuda, store_logits):
+    """Cfg3 at its full size: 16384 tokens (8 x 2048), hidden 3584, vocab 152064, hidden N(0,1),
+    head N(0, 0.02), 10 % of labels -100, on the tcgen05 path (with the logits recomputed for
+    the gradient, and with them stored). Every row's loss and every dH element against the
+    chunked fp32 reference: loss within 1e-4 relative, dH within bf16 tolerance."""
+    from hackathon_b200 import cross_entropy as ce
+    from hackathon_b200.gemm import device_error
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    B, S, H, V = 8, 2048, 3584, 152064
+    hidden = torch.randn(B, S, H, device=cuda, generator=gen).to(torch.bfloat16)
+    weight = (torch.randn(V, H, device=cuda, generator=gen) * 0.02).to(torch.bfloat16)
+    labels = torch.randint(0, V, (B, S), device=cuda, generator=gen)
+    labels[torch.rand(B, S, device=cuda, generator=gen) < 0.1] = -100
+    prev = ce.STORE_LOGITS
+    ce.STORE_LOGITS = store_logits
+    try:
+        h = hidden.detach().requires_grad_()
+        loss, step = ce.fused_causal_lm_loss(h, weight, labels)
+        loss.backward()
+        device_error()
+    finally:
+        ce.STORE_LOGITS = prev
+    target = ce.shift_labels_of(labels).reshape(-1)
+    loss_ref, tok_ref, dh_ref = _fp32_ce_reference(hidden.reshape(-1, H), weight, target)
+    assert abs(float(loss) - float(loss_ref)) <= 1e-4 * abs(float(loss_ref))
+    torch.testing.assert_close(step.token_loss.reshape(-1), tok_ref, rtol=1e-4, atol=1e-4)
+    assert int(step.labelled) == int((target != -100).sum())
+    # per-row gradients (x n: the 1/n scale would make any absolute bound vacuous)
+    n = int(step.labelled)
+    got = h.grad.reshape(-1, H).float() * n
+    want = dh_ref * n
+    torch.testing.assert_close(got, want, rtol=2e-2, atol=1e-3)
+    assert float((got - want).norm() / want.norm()) < 1e-2
+
+
 def test_ce_rows_kernel_edge_cases(cuda):
     """Unlabelled rows (0 loss, 0 gradient), ties (first index wins), a ragged vocab and an
     unaligned row stride (scalar path)."""

@@ -275,3 +275,139 @@ def test_projection_with_rope_epilogue_matches_rope_kernel(cuda, T):
     for a, b in ((da1, da0), (db1, db0)):
         rel = (a - b).norm() / b.norm()
         assert rel < 2e-2, float(rel)
+
+
+def _mask_of_bits(bits, cols):
+    """bool [rows, cols] from the step's mask words (bit j of word w = element 32 w + j)."""
+    sh = torch.arange(32, device=bits.device, dtype=torch.int32)
+    return ((bits.unsqueeze(-1) >> sh) & 1).bool().reshape(bits.shape[0], -1)[:, :cols]
+
+
+def test_long_token_checkpointed_layer_with_dropout_matches_eager_oracle(cuda):
+    """The decoder layer on the path the 7B step runs - T >= DEQUANT_GEMM_MIN_TOKENS (transient
+    bf16 weights), dropout p = 0.1, activation checkpointing, the q/k projections with the RoPE
+    in their GEMM epilogue, the gate/up pair as one GEMM with the SwiGLU in its epilogue, the
+    masked LoRA input gradient - against the eager oracle: the reference's composition
+    (NF4 rebuilt by the numpy oracle, F.linear, peft's dropout -> lora_A -> lora_B -> scaled add,
+    eager RMSNorm / RoPE / SwiGLU, fp32 attention), run with torch ops on the device. Both apply
+    the masks the step drew; those masks are first checked, on sampled rows of every
+    projection, against the oracle's Philox-4x32-10 stream (the reference's tl.rand). Forward,
+    input gradient and all fourteen adapter gradients within bf16 tolerance."""
+    from hackathon_b200 import qlora
+    from hackathon_b200.gemm import device_error
+    from hackathon_b200.nf4 import DEQUANT_GEMM_MIN_TOKENS
+    from oracle import nf4_ref, ops_ref
+    p = 0.1
+    shape = qlora.preset("0.5b", hidden=512, intermediate=1408, heads=4, kv_heads=2,
+                         head_dim=128, layers=1, lora_r=64, lora_alpha=128, lora_dropout=p)
+    gen = torch.Generator(device=cuda).manual_seed(21)
+    layer = qlora.DecoderLayer(shape, cuda, gen)
+    layer.train()
+    with torch.no_grad():
+        for name in qlora._PROJ:
+            getattr(layer, name).lora_B.normal_(0, 0.05, generator=gen)
+    B, S, H = 2, 4096, shape.hidden
+    assert B * S >= DEQUANT_GEMM_MIN_TOKENS
+    h = (torch.randn(B, S, H, device=cuda, generator=gen) * 0.5).to(torch.bfloat16)
+    cos, sin = ops_ref.qwen_cos_sin(1, S, 128, shape.theta, torch.bfloat16, device=cuda)
+    cos, sin = cos.contiguous(), sin.contiguous()
+    assert layer.rope_fused_ok(h, cos) and layer.mlp_fused_ok(h)
+    seed = 777
+    qlora.MASKS.clear()
+    hg = h.clone().requires_grad_()
+    out = torch.utils.checkpoint.checkpoint(layer, hg, cos, sin, seed, [0], None,
+                                            use_reentrant=False, determinism_check="none")
+    bits = {name: qlora.MASKS[(id(getattr(layer, name)), seed + k)].clone()
+            for k, name in enumerate(qlora._PROJ)}
+    gout = torch.randn(out.shape, device=cuda, generator=gen).to(torch.bfloat16)
+    out.backward(gout)
+    device_error()
+
+    # the masks are the reference's Philox stream (sampled rows of every projection)
+    rows = [0, 1, 4097, B * S - 1]
+    for k, name in enumerate(qlora._PROJ):
+        mod = getattr(layer, name)
+        got = _mask_of_bits(bits[name][rows], mod.in_features).cpu().numpy()
+        for i, r in enumerate(rows):
+            want = nf4_ref.dropout_keep(seed + k, B * S, mod.in_features, p, row_range=(r, r + 1))
+            assert np.array_equal(got[i], want[0]), (name, r)
+
+    # eager twin: same NF4 bytes, same adapters, the same masks
+    scale = 1.0 / (1.0 - p)
+
+    class Twin(torch.nn.Module):
+        def __init__(self, m, mask):
+            super().__init__()
+            qs = m.quant_state
+            n = m.out_features * m.in_features
+            wb = nf4_ref.dequant_nf4(m.packed.cpu().numpy().reshape(-1), n,
+                                     qs.absmax.cpu().numpy(), True, qs.state2.code.cpu().numpy(),
+                                     qs.state2.absmax.cpu().numpy(), qs.offset, 64, 256,
+                                     out="bf16")
+            self.w = torch.from_numpy(wb.view(np.int16).copy()).view(torch.bfloat16).view(
+                m.out_features, m.in_features).to(cuda)
+            self.b = m.bias
+            self.a = torch.nn.Parameter(m.lora_A.detach().clone())
+            self.bb = torch.nn.Parameter(m.lora_B.detach().clone())
+            self.s = m.scaling
+            self.mask = mask
+
+        def forward(self, x):
+            x2 = x.reshape(-1, x.shape[-1])
+            base = torch.nn.functional.linear(x2, self.w, self.b)
+            xd = (x2.float() * self.mask * scale).to(x.dtype)          # DropoutCast
+            lo = torch.nn.functional.linear(torch.nn.functional.linear(xd, self.a.to(x.dtype)),
+                                            self.bb.to(x.dtype))
+            return ops_ref.scaled_add_ref(base, lo, self.s).view(*x.shape[:-1], -1)
+
+    t = {name: Twin(getattr(layer, name),
+                    _mask_of_bits(bits[name], getattr(layer, name).in_features))
+         for name in qlora._PROJ}
+    hr = h.clone().requires_grad_()
+    x = ops_ref.rmsnorm_ref(hr, layer.ln1, shape.eps)
+    q = t["q"](x).view(B, S, shape.heads, 128).transpose(1, 2)
+    kk = t["k"](x).view(B, S, shape.kv_heads, 128).transpose(1, 2)
+    v = t["v"](x).view(B, S, shape.kv_heads, 128).transpose(1, 2)
+    q, kk = ops_ref.rope_ref(q, kk, cos, sin)
+    rep = shape.heads // shape.kv_heads
+    a = torch.nn.functional.scaled_dot_product_attention(
+        q.float(), kk.float().repeat_interleave(rep, 1), v.float().repeat_interleave(rep, 1),
+        is_causal=True).to(torch.bfloat16)
+    hh = hr + t["o"](a.transpose(1, 2).reshape(B, S, -1))
+    x2 = ops_ref.rmsnorm_ref(hh, layer.ln2, shape.eps)
+    m = ops_ref.swiglu_ref(t["gate"](x2), t["up"](x2)).to(torch.bfloat16)
+    ref = hh + t["down"](m)
+    ref.backward(gout)
+
+    torch.testing.assert_close(out.detach().float(), ref.detach().float(), rtol=5e-2, atol=5e-2)
+    torch.testing.assert_close(hg.grad.float(), hr.grad.float(), rtol=5e-2, atol=5e-2)
+    for name in qlora._PROJ:
+        mod, tw = getattr(layer, name), t[name]
+        for mine, theirs in ((mod.lora_A.grad, tw.a.grad), (mod.lora_B.grad, tw.bb.grad)):
+            rel = (mine.float() - theirs.float()).norm() / theirs.float().norm()
+            assert rel < 5e-2, (name, float(rel))
+
+
+def test_many_long_token_steps_in_a_row(cuda):
+    """Twenty consecutive training steps of 7B-shaped layers at the step's token count (4 x
+    4096), each followed by a read of the tensor-core error flag, and the launch monitor after
+    each: every step's loss is finite, no bounded wait gives up, and no traced launch is left
+    with CTAs that started and never finished."""
+    import ctypes
+    from hackathon_b200 import _lib
+    from hackathon_b200.gemm import device_error
+    from hackathon_b200.qlora import QwenQLoRA, make_optimizer, preset, synthetic_batch, \
+        train_step
+    shape = preset("7b", layers=2)
+    model = QwenQLoRA(shape, cuda, seed=0)
+    opt = make_optimizer(model)
+    data = [synthetic_batch(shape, 4, 4096, cuda, seed=i) for i in range(2)]
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(1024)
+    for i in range(20):
+        ids, labels = data[i % 2]
+        loss = float(train_step(model, opt, ids, labels))
+        device_error()
+        assert np.isfinite(loss), (i, loss)
+        assert lib.qb_monitor_report(cuda.index or 0, buf, len(buf)) == 0
+        assert "no CTA of these launches is running" in buf.value.decode(), (i, buf.value)
