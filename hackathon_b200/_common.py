@@ -23,3 +23,21 @@ def round_mode(dtype):
     if dtype == torch.bfloat16:
         return 2
     return 0
+
+
+PATCH_MARK = "_qlora_b200_patch"
+
+
+def install(owner, name, build):
+    """Replaces owner.<name> by build(original) once: the replacement carries PATCH_MARK and the
+    original as __wrapped__, so a second call (and apply() run twice) leaves it alone. Every
+    patch of this package goes through here; each replacement hands the inputs its kernels do
+    not take to `original` unchanged. Returns the function now installed."""
+    current = getattr(owner, name)
+    if getattr(current, PATCH_MARK, False):
+        return current
+    replacement = build(current)
+    setattr(replacement, PATCH_MARK, True)
+    replacement.__wrapped__ = current
+    setattr(owner, name, replacement)
+    return replacement

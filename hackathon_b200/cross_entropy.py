@@ -3,39 +3,41 @@
 
     loss = sum over labelled rows of CE(hidden @ W.T, target) / denominator
 plus per-token loss, entropy and argmax (what TRL's metrics and Soup's rewind recorder read).
-The head W is frozen: the gradient of the hidden states is computed in forward, chunk by chunk,
-and the backward only scales it by the incoming loss gradient (cross_entropy.py:93-138).
+The head W is frozen. The custom op qlora_b200::linear_ce computes, chunk by chunk of rows, the
+per-row statistics and each row's loss gradient w.r.t. its hidden state; the backward only
+scales those rows by the incoming gradient (cross_entropy.py:93-138).
 
-Rows go through in chunks of `chunk_rows`: logits_chunk = h @ W.T in the matmul dtype, then the
-row kernel (qb_ce_rows) streams each row once for the statistics and rewrites it in place with
-(softmax - onehot) * GRAD_GAIN / denominator, then dH_chunk = dZ @ W. Only one chunk of logits
-is alive at a time.
+bf16 head and hidden states take the tcgen05 kernels: the logits tile lives in TMEM, pass 1
+reduces it to row statistics, the gradient pass recomputes it into dZ = softmax - onehot in its
+epilogue, and dH = dZ @ W runs on the tcgen05 GEMM. Other dtypes: a matmul chunk of logits, then
+the row kernel (qb_ce_rows) streams each row once and rewrites it with the gradient.
 """
 
 import torch
 
-from . import _common, _lib
+from . import _common, _lib, ops  # noqa: F401 - ops registers the custom operators
 
 IGNORE_INDEX = -100
-CHUNK_ROWS = 4096           # rows of logits alive at a time (4096 x 152064 bf16 = 1.2 GB)
-# dz is stored in the matmul dtype before the dH matmul; it is kept multiplied by GRAD_GAIN
-# (a power of two, exact) so fp16 does not underflow, and divided back in fp32 (:40-44).
+CHUNK_ROWS = 4096           # rows per chunk (the bf16 dZ of a 4096 x 152064 chunk: 1.2 GB)
+# Off the bf16 path dZ is stored in the matmul dtype before the dH matmul, multiplied by
+# GRAD_GAIN (a power of two, exact) so small probabilities survive fp16, and divided back in fp32.
 GRAD_GAIN = 65536.0
-STEP_ATTR = "_soup_chunked_step"
 
 
-# With the gradient wanted, pass 1 also stores the chunk's fp32 logits (rows x vocab x 4 bytes of
-# scratch, 2.5 GB at 4096 x 152064) and dZ comes from them in one streaming pass, instead of
-# recomputing the logits GEMM (2 N H V flops) in pass 2. Same z, same arithmetic, same dZ.
-STORE_LOGITS = True
+# False (the default): the logits exist only in TMEM - pass 1 reduces each tile to row
+# statistics, and the gradient pass recomputes the tile and turns it into dZ in its epilogue
+# (6 N H V flops executed for the algorithmic 4 N H V). True: pass 1 also stores the chunk's fp32
+# logits (rows x vocab x 4 bytes, 2.5 GB at 4096 x 152064) and dZ comes from them in one
+# streaming pass instead of the second logits GEMM. Same z, same arithmetic, same dZ.
+STORE_LOGITS = False
 
 
 def linear_ce_tc(h2, w, tgt, token_loss, entropy, pred, grad_h, scale_dev, chunk_rows,
                  store_logits=None):
     """The tcgen05 path for bf16 hidden states and head: per chunk of rows, pass 1 (logits in
     TMEM -> per-tile row statistics, and the fp32 logits when `store_logits`), the reduction,
-    and with grad_h the dZ pass (from the stored logits, or a second logits GEMM with dZ in its
-    epilogue) followed by dH = dZ @ W into grad_h (fp32)."""
+    and with grad_h the dZ pass (dZ = (softmax - onehot) * scale_dev, from the stored logits or a
+    second logits GEMM with dZ in its epilogue) followed by dH = dZ @ W into grad_h (fp32)."""
     from .gemm import gemm
     n, hdim = h2.shape
     vocab = w.shape[0]
@@ -83,16 +85,15 @@ def linear_ce_tc(h2, w, tgt, token_loss, entropy, pred, grad_h, scale_dev, chunk
         gemm(dz[:rows, :vocab], w.t(), out=grad_h[start:stop], out_dtype=torch.float32)
 
 
-def tc_path_ok(h2, w, matmul_dtype):
-    return (matmul_dtype == torch.bfloat16 and h2.is_cuda and w.is_cuda
-            and h2.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
-            and h2.shape[1] % 8 == 0 and w.stride(-1) == 1 and h2.stride(-1) == 1
-            and w.stride(0) % 8 == 0 and h2.stride(0) % 8 == 0)
+def tc_path_ok(h2, w):
+    return (h2.is_cuda and w.is_cuda and h2.dtype == torch.bfloat16
+            and w.dtype == torch.bfloat16 and h2.shape[1] % 8 == 0 and w.stride(-1) == 1
+            and h2.stride(-1) == 1 and w.stride(0) % 8 == 0 and h2.stride(0) % 8 == 0)
 
 
 def ce_rows_inplace(logits, target, token_loss, entropy, pred, grad_scale, write_grad):
-    """Runs the row kernel on a [rows, vocab] logits chunk (rewritten in place with the scaled
-    gradient when write_grad)."""
+    """Runs the row kernel on a [rows, vocab] logits chunk (rewritten in place with
+    (softmax - onehot) * grad_scale when write_grad)."""
     rows, vocab = logits.shape
     _lib.call("qb_ce_rows", logits.data_ptr(), _lib.tag(logits.dtype), logits.stride(0),
               target.data_ptr(), rows, vocab, token_loss.data_ptr(), entropy.data_ptr(),
@@ -101,63 +102,66 @@ def ce_rows_inplace(logits, target, token_loss, entropy, pred, grad_scale, write
               work=(rows * vocab * logits.element_size() * (3 if write_grad else 1), 0))
 
 
-class FusedLinearCrossEntropy(torch.autograd.Function):
-    """loss, per-token loss, entropy, argmax of CE(hidden @ W.T, target), W frozen."""
+def linear_ce_rows(hidden, weight, target, chunk_rows, with_grad):
+    """The body of the custom op qlora_b200::linear_ce. hidden [n, H] and weight [V, H] in the
+    matmul dtype, target [n] int64 (IGNORE_INDEX rows score nothing). Returns per row: the CE
+    loss, the entropy of the softmax, the argmax (first index on ties), and with_grad the
+    gradient of that row's loss w.r.t. its hidden state, (softmax - onehot) @ W in fp32 (zero
+    for unlabelled rows; else an empty [0, H]). Only `chunk_rows` rows of logits exist at a time,
+    on the tcgen05 path none at all (they stay in TMEM)."""
+    _lib.require_cuda(hidden, weight, target, what="fused linear CE")
+    n, hdim = hidden.shape
+    dev = hidden.device
+    tgt = target.to(torch.int64).contiguous()
+    token_loss = torch.empty(n, dtype=torch.float32, device=dev)
+    entropy = torch.empty(n, dtype=torch.float32, device=dev)
+    pred = torch.empty(n, dtype=torch.int64, device=dev)
+    dh = torch.empty((n if with_grad else 0, hdim), dtype=torch.float32, device=dev)
+    if n == 0:
+        return token_loss, entropy, pred, dh
+    h2 = hidden if hidden.stride(-1) == 1 else hidden.contiguous()
+    if tc_path_ok(h2, weight):
+        one = torch.ones(1, dtype=torch.float32, device=dev)   # dZ unscaled: bf16 keeps range
+        linear_ce_tc(h2, weight, tgt, token_loss, entropy, pred, dh if with_grad else None, one,
+                     chunk_rows)
+        return token_loss, entropy, pred, dh
+    # other dtypes: a matmul chunk of logits, then the row kernel streams each row once for the
+    # statistics and rewrites it with (softmax - onehot) * GRAD_GAIN (fp16 keeps small
+    # probabilities), then dH_chunk = dZ W / GRAD_GAIN
+    with torch.autocast(device_type=dev.type, enabled=False):
+        for a in range(0, n, chunk_rows):
+            b = min(a + chunk_rows, n)
+            logits = h2[a:b] @ weight.t()
+            ce_rows_inplace(logits, tgt[a:b], token_loss[a:b], entropy[a:b], pred[a:b],
+                            GRAD_GAIN, with_grad)
+            if with_grad:
+                dh[a:b] = (logits @ weight).float() * (1.0 / GRAD_GAIN)
+            del logits
+    return token_loss, entropy, pred, dh
+
+
+class FusedLinearCrossEntropy:
+    """loss, per-token loss, entropy and argmax of CE(hidden @ W.T, target) with W frozen
+    (cross_entropy.py:93-138): the custom op qlora_b200::linear_ce over the rows, whose
+    registered backward scales each row's precomputed gradient by the incoming gradient of its
+    loss; loss = sum of the per-token losses / denominator (a tensor or a number: no host
+    read)."""
 
     @staticmethod
-    def forward(ctx, hidden, weight, target, denominator, matmul_dtype, chunk_rows):
+    def apply(hidden, weight, target, denominator, matmul_dtype, chunk_rows):
         _lib.require_cuda(hidden, weight, what="fused linear CE")
         shape = hidden.shape
         h2 = hidden.reshape(-1, shape[-1])
-        tgt = target.reshape(-1).to(device=hidden.device, dtype=torch.int64).contiguous()
-        n_rows = h2.shape[0]
-        dev = hidden.device
-        with_grad = ctx.needs_input_grad[0]
-
-        token_loss = torch.empty(n_rows, dtype=torch.float32, device=dev)
-        entropy = torch.empty(n_rows, dtype=torch.float32, device=dev)
-        pred = torch.empty(n_rows, dtype=torch.int64, device=dev)
-        grad_h = torch.empty((n_rows, shape[-1]), dtype=torch.float32, device=dev) \
-            if with_grad else None
-        w_mm = weight if weight.dtype == matmul_dtype else weight.to(matmul_dtype)
-        h_mm = h2 if h2.dtype == matmul_dtype else h2.to(matmul_dtype)
-        if tc_path_ok(h_mm, w_mm, matmul_dtype):
-            # the gradient scale stays on the device: no host sync on the denominator
-            d = torch.as_tensor(denominator, dtype=torch.float32, device=dev).reshape(1)
-            scale_dev = torch.where(d != 0, GRAD_GAIN / d, torch.zeros_like(d))
-            linear_ce_tc(h_mm, w_mm, tgt, token_loss, entropy, pred, grad_h, scale_dev,
-                         chunk_rows)
-            loss = token_loss.sum() / denominator
-            ctx.save_for_backward(grad_h)
-            ctx.shape, ctx.dtype = shape, hidden.dtype
-            ctx.mark_non_differentiable(token_loss, entropy, pred)
-            return (loss, token_loss.view(shape[:-1]), entropy.view(shape[:-1]),
-                    pred.view(shape[:-1]))
-        denom = float(denominator)
-        grad_scale = GRAD_GAIN / denom if denom else 0.0
-        with torch.autocast(device_type=dev.type, enabled=False):
-            w = weight if weight.dtype == matmul_dtype else weight.to(matmul_dtype)
-            for start in range(0, n_rows, chunk_rows):
-                stop = min(start + chunk_rows, n_rows)
-                logits = h2[start:stop].to(matmul_dtype) @ w.t()
-                ce_rows_inplace(logits, tgt[start:stop], token_loss[start:stop],
-                                entropy[start:stop], pred[start:stop], grad_scale, with_grad)
-                if with_grad:
-                    grad_h[start:stop] = logits @ w   # logits now hold dz * GRAD_GAIN / denom
-                del logits
+        h2 = h2 if h2.dtype == matmul_dtype else h2.to(matmul_dtype)
+        w = weight if weight.dtype == matmul_dtype else weight.to(matmul_dtype)
+        tgt = target.reshape(-1).to(device=hidden.device, dtype=torch.int64)
+        with_grad = torch.is_grad_enabled() and hidden.requires_grad
+        token_loss, entropy, pred, _ = torch.ops.qlora_b200.linear_ce(h2, w, tgt,
+                                                                       int(chunk_rows),
+                                                                       with_grad)
         loss = token_loss.sum() / denominator
-        ctx.save_for_backward(grad_h)
-        ctx.shape, ctx.dtype = shape, hidden.dtype
-        ctx.mark_non_differentiable(token_loss, entropy, pred)
-        return loss, token_loss.view(shape[:-1]), entropy.view(shape[:-1]), pred.view(shape[:-1])
-
-    @staticmethod
-    def backward(ctx, grad_loss, _grad_token_loss, _grad_entropy, _grad_pred):
-        (grad_h,) = ctx.saved_tensors
-        if grad_h is None:
-            return None, None, None, None, None, None
-        grad = grad_h * (grad_loss.float() / GRAD_GAIN)
-        return grad.view(ctx.shape).to(ctx.dtype), None, None, None, None, None
+        lead = shape[:-1]
+        return loss, token_loss.view(lead), entropy.view(lead), pred.view(lead)
 
 
 class ChunkedStep:
@@ -195,156 +199,22 @@ def fused_causal_lm_loss(hidden, weight, labels, num_items_in_batch=None, shift_
     return loss, ChunkedStep(entropy, token_loss, pred, target)
 
 
-class _State:
-    armed = False   # set by the patched compute_loss for exactly one model forward
-    step = None
-
-
-STATE = _State()
-
-
-def _head_ok(lm):
-    head = getattr(lm, "lm_head", None)
-    return (type(head) is torch.nn.Linear and head.bias is None
-            and not head.weight.requires_grad and _common.on_gpu(head.weight)
-            and getattr(lm.config, "final_logit_softcapping", None) is None)
-
-
-def _patch_causal_lm():
-    """Qwen2ForCausalLM.forward returns the fused loss and logits=None when armed
-    (cross_entropy.py:190-222)."""
-    from transformers.modeling_outputs import CausalLMOutputWithPast
-    from transformers.models.qwen2 import modeling_qwen2 as m
-
-    original = m.Qwen2ForCausalLM.forward
-    if getattr(original, "_solution_patch", False):
-        return
-
-    def forward(self, input_ids=None, attention_mask=None, position_ids=None,
-                past_key_values=None, inputs_embeds=None, labels=None, use_cache=None,
-                logits_to_keep=0, **kwargs):
-        if not (STATE.armed and labels is not None and _common.on_gpu(labels)
-                and isinstance(logits_to_keep, int) and logits_to_keep == 0
-                and kwargs.get("return_dict", True) is not False and _head_ok(self)):
-            return original(self, input_ids=input_ids, attention_mask=attention_mask,
-                            position_ids=position_ids, past_key_values=past_key_values,
-                            inputs_embeds=inputs_embeds, labels=labels, use_cache=use_cache,
-                            logits_to_keep=logits_to_keep, **kwargs)
-        STATE.armed = False
-        outputs = self.model(input_ids=input_ids, attention_mask=attention_mask,
-                             position_ids=position_ids, past_key_values=past_key_values,
-                             inputs_embeds=inputs_embeds, use_cache=use_cache, **kwargs)
-        loss, STATE.step = fused_causal_lm_loss(
-            outputs.last_hidden_state, self.lm_head.weight, labels,
-            num_items_in_batch=kwargs.get("num_items_in_batch"),
-            shift_labels=kwargs.get("shift_labels"))
-        return CausalLMOutputWithPast(loss=loss, logits=None,
-                                      past_key_values=outputs.past_key_values,
-                                      hidden_states=outputs.hidden_states,
-                                      attentions=outputs.attentions)
-
-    forward._solution_patch = True
-    m.Qwen2ForCausalLM.forward = forward
-
-
-def _causal_lm_of(trainer, model):
-    unwrap = getattr(getattr(trainer, "accelerator", None), "unwrap_model", None)
-    inner = unwrap(model) if callable(unwrap) else model
-    get_base = getattr(inner, "get_base_model", None)
-    return get_base() if callable(get_base) else inner
-
-
-def _can_fuse(trainer, model, inputs):
-    """The trainer-state checks of cross_entropy.py:232-256."""
-    from transformers.models.qwen2.modeling_qwen2 import Qwen2ForCausalLM
-
-    args = getattr(trainer, "args", None)
-    if not (isinstance(model, torch.nn.Module) and isinstance(inputs, dict) and args is not None):
-        return False
-    if not getattr(trainer.model, "training", False):
-        return False
-    if "labels" not in inputs or "shift_labels" in inputs or "attention_mask" not in inputs:
-        return False
-    if not _common.on_gpu(inputs["labels"], inputs["attention_mask"]):
-        return False
-    if getattr(args, "use_liger_kernel", False) or getattr(args, "loss_type", "nll") != "nll":
-        return False
-    if getattr(trainer, "num_virtual_tokens", 0) or getattr(trainer, "aux_loss_enabled", False):
-        return False
-    if getattr(trainer, "compute_loss_func", None) is not None or \
-            getattr(trainer, "label_smoother", None) is not None:
-        return False
-    if getattr(trainer, "_soup_chunked_head_loss", None) is not None:
-        return False
-    if not all(hasattr(trainer, name) for name in ("_metrics", "_total_train_tokens")):
-        return False
-    lm = _causal_lm_of(trainer, model)
-    return isinstance(lm, Qwen2ForCausalLM) and _head_ok(lm)
-
-
-def _log_metrics(trainer, mode, inputs, step):
-    """entropy, num_tokens and mean_token_accuracy by TRL's formulas (cross_entropy.py:259-276)."""
-    gather = trainer.accelerator.gather_for_metrics
-    attention_mask = inputs["attention_mask"]
-    with torch.no_grad():
-        entropy = torch.sum(step.token_entropy * attention_mask) / attention_mask.sum()
-        entropy = gather(entropy).mean().item()
-    trainer._metrics[mode]["entropy"].append(entropy)
-    if mode == "train":
-        trainer._total_train_tokens += gather(attention_mask.sum()).sum().item()
-    trainer._metrics[mode]["num_tokens"] = [trainer._total_train_tokens]
-    with torch.no_grad():
-        correct = gather(step.correct)
-        total = gather(step.labelled)
-        total_sum = total.sum()
-        accuracy = (correct.sum() / total_sum).item() if total_sum > 0 else 0.0
-    trainer._metrics[mode]["mean_token_accuracy"].append(accuracy)
-
-
-def _patch_trainer():
-    """trl.SFTTrainer.compute_loss arms the fused forward and logs TRL's metrics from the kernel
-    outputs (cross_entropy.py:279-316). A no-op when trl is not installed."""
-    try:
-        from trl import SFTTrainer
-    except ImportError:
-        return
-
-    original = SFTTrainer.compute_loss
-    if getattr(original, "_solution_patch", False):
-        return
-
-    def compute_loss(self, model, inputs, return_outputs=False, num_items_in_batch=None):
-        if not _can_fuse(self, model, inputs):
-            return original(self, model, inputs, return_outputs=return_outputs,
-                            num_items_in_batch=num_items_in_batch)
-        mode = "train" if self.model.training else "eval"
-        inputs.pop("_prediction_loss_only", None)
-        labels = inputs["labels"]
-        inputs["use_cache"] = False
-        STATE.armed, STATE.step = True, None
-        try:
-            loss, outputs = super(SFTTrainer, self).compute_loss(
-                model, inputs, return_outputs=True, num_items_in_batch=num_items_in_batch)
-        finally:
-            STATE.armed = False
-        step, STATE.step = STATE.step, None
-        if step is None:
-            from trl.trainer.utils import entropy_from_logits
-
-            with torch.no_grad():
-                logits = outputs.logits
-                step = ChunkedStep(entropy_from_logits(logits), None, logits.argmax(dim=-1),
-                                   shift_labels_of(labels))
-            setattr(self, STEP_ATTR, None)
-        else:
-            setattr(self, STEP_ATTR, step)
-        _log_metrics(self, mode, inputs, step)
-        return (loss, outputs) if return_outputs else loss
-
-    compute_loss._solution_patch = True
-    SFTTrainer.compute_loss = compute_loss
+def _causal_lm_loss(hidden, head_weight, labels, attention_mask, kwargs):
+    """The loss the causal-LM hook computes for cross_entropy.patch(): ForCausalLMLoss with its
+    num_items_in_batch / shift_labels, and the ChunkedStep."""
+    return fused_causal_lm_loss(hidden, head_weight, labels,
+                                num_items_in_batch=kwargs.get("num_items_in_batch"),
+                                shift_labels=kwargs.get("shift_labels"))
 
 
 def patch():
-    _patch_causal_lm()
-    _patch_trainer()
+    """Qwen2ForCausalLM.forward and trl.SFTTrainer.compute_loss on the fused loss
+    (cross_entropy.py:190-321): the trainer arms it for one model forward, which returns the loss
+    with logits=None; the ChunkedStep (per-token loss, entropy, argmax, counts, on the device) is
+    left on the trainer. The trainer half is skipped when trl is not installed."""
+    from . import hooks
+    hooks.install_causal_lm()
+    try:
+        hooks.install_trainer(_causal_lm_loss)
+    except ImportError:
+        pass

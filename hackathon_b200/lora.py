@@ -13,7 +13,7 @@ Triton's tl.rand draws, so masks equal the reference kernel's for the same seed.
 
 import torch
 
-from . import _common, _lib
+from . import _common, _lib, ops  # noqa: F401 - ops registers the custom operators
 
 TORCH_DROPOUT_RNG = False
 
@@ -23,16 +23,39 @@ def _rows(t):
     return t2 if t2.stride(-1) == 1 else t2.contiguous()
 
 
-def _dropout_scale(src, out_dtype, seed, p, scale):
-    _lib.require_cuda(src, what="dropout_scale")
-    s2 = _rows(src)
-    out = torch.empty(s2.shape, dtype=out_dtype, device=src.device)
+def _seed64(seed):
+    """A Philox key as the kernels take it (unsigned 64-bit)."""
+    return int(seed) & 0xFFFFFFFFFFFFFFFF
+
+
+def _seed_arg(seed):
+    """The same key as a signed 64-bit int (what a custom op's int argument holds)."""
+    s = _seed64(seed)
+    return s - (1 << 64) if s >= (1 << 63) else s
+
+
+def dropout_scale_into(src, out, p, seed, scale):
+    """qb_dropout_scale: out = dropout(src) * scale in out's dtype, the mask from the
+    reference's Philox stream keyed by `seed` (p = 0: no mask)."""
+    _lib.require_cuda(src, out, what="dropout_scale")
+    s2, o2 = _rows(src), out.view(-1, out.shape[-1])
     M, N = s2.shape
-    _lib.call("qb_dropout_scale", s2.data_ptr(), _lib.tag(s2.dtype), s2.stride(0), out.data_ptr(),
-              _lib.tag(out_dtype), out.stride(0), M, N, int(seed) & 0xFFFFFFFFFFFFFFFF,
-              float(p), float(scale), _lib.stream(src.device),
-              work=(M * N * (s2.element_size() + out.element_size()), 0))
-    return out.view(src.shape)
+    _lib.call("qb_dropout_scale", s2.data_ptr(), _lib.tag(s2.dtype), s2.stride(0), o2.data_ptr(),
+              _lib.tag(o2.dtype), o2.stride(0), M, N, _seed64(seed), float(p), float(scale),
+              _lib.stream(src.device), work=(M * N * (s2.element_size() + o2.element_size()), 0))
+    return out
+
+
+def scaled_add_into(base, lo, out, scaling):
+    """qb_scaled_add: out = base + lo * scaling in out's dtype."""
+    _lib.require_cuda(base, lo, out, what="scaled_add")
+    b2, l2, o2 = _rows(base), _rows(lo), out.view(-1, out.shape[-1])
+    M, N = b2.shape
+    _lib.call("qb_scaled_add", b2.data_ptr(), _lib.tag(b2.dtype), b2.stride(0), l2.data_ptr(),
+              _lib.tag(l2.dtype), l2.stride(0), o2.data_ptr(), _lib.tag(o2.dtype), o2.stride(0),
+              M, N, float(scaling), _lib.stream(base.device),
+              work=(M * N * (b2.element_size() + l2.element_size() + o2.element_size()), 0))
+    return out
 
 
 def dropout_mask(x2, p, seed, scale, out_dtype=None):
@@ -104,106 +127,95 @@ def dropout_apply(x2, bits, scale, out=None, accumulate=False):
     return out
 
 
-class DropoutCast(torch.autograd.Function):
-    """x -> dropout(x) cast to out_dtype, mask from (seed, flat index) (lora.py:84-93)."""
+class DropoutCast:
+    """x -> dropout(x) * 1/(1-p) cast to out_dtype, the mask a function of (seed, flat index) only
+    (lora.py:84-93): the custom op qlora_b200::dropout_scale, whose registered backward applies
+    the same mask and scale to the gradient."""
 
     @staticmethod
-    def forward(ctx, x, p, seed, out_dtype):
+    def apply(x, p, seed, out_dtype):
+        _lib.require_cuda(x, what="dropout_scale")
         scale = 1.0 / (1.0 - p) if p > 0 else 1.0
-        ctx.p, ctx.seed, ctx.scale, ctx.x_dtype = p, seed, scale, x.dtype
-        return _dropout_scale(x, out_dtype, seed, p, scale)
+        return torch.ops.qlora_b200.dropout_scale(x, float(p), _seed_arg(seed), scale, out_dtype)
+
+
+class ScaledAdd:
+    """out = base + lo * scaling in promote(base, lo) (lora.py:96-112): the custom op
+    qlora_b200::scaled_add; its backward is (g, g * scaling in lo's dtype)."""
 
     @staticmethod
-    def backward(ctx, g):
-        return _dropout_scale(g, ctx.x_dtype, ctx.seed, ctx.p, ctx.scale), None, None, None
-
-
-class ScaledAdd(torch.autograd.Function):
-    """out = base + lo * scaling in promote(base, lo) (lora.py:96-112)."""
-
-    @staticmethod
-    def forward(ctx, base, lo, scaling):
+    def apply(base, lo, scaling):
         _lib.require_cuda(base, lo, what="scaled_add")
-        b2, l2 = _rows(base), _rows(lo)
-        out_dtype = torch.promote_types(base.dtype, lo.dtype)
-        out = torch.empty(b2.shape, dtype=out_dtype, device=base.device)
-        M, N = b2.shape
-        _lib.call("qb_scaled_add", b2.data_ptr(), _lib.tag(b2.dtype), b2.stride(0), l2.data_ptr(),
-                  _lib.tag(l2.dtype), l2.stride(0), out.data_ptr(), _lib.tag(out_dtype),
-                  out.stride(0), M, N, float(scaling), _lib.stream(base.device),
-                  work=(M * N * (b2.element_size() + l2.element_size() + out.element_size()), 0))
-        ctx.scaling, ctx.base_dtype, ctx.lo_dtype = scaling, base.dtype, lo.dtype
-        return out.view(base.shape)
-
-    @staticmethod
-    def backward(ctx, g):
-        d_base = g if g.dtype == ctx.base_dtype else g.to(ctx.base_dtype)
-        d_lo = _dropout_scale(g, ctx.lo_dtype, 0, 0.0, ctx.scaling)  # g * scaling, cast
-        return d_base, d_lo, None
+        return torch.ops.qlora_b200.scaled_add(base, lo, float(scaling))
 
 
-class _Seeds:
-    """Philox seeds from a private generator seeded by the run's torch seed, so no other random
-    stream (data order, init) is disturbed and a run stays reproducible (lora.py:115-124)."""
-    gen = None
+class SeedStream:
+    """Philox keys for the patched peft layers: key i of a process is a SplitMix64 mix of
+    (torch.initial_seed(), i), kept below 2^31 like the reference's. A run with a fixed torch
+    seed draws the same keys, and no torch generator (data order, init) is advanced."""
+
+    count = 0
 
     @classmethod
     def next(cls):
-        if cls.gen is None:
-            cls.gen = torch.Generator().manual_seed(torch.initial_seed() & 0xFFFF_FFFF)
-        return int(torch.randint(0, 2**31 - 1, (1,), generator=cls.gen))
+        cls.count += 1
+        z = (torch.initial_seed() * 0x9E3779B97F4A7C15 + cls.count * 0xBF58476D1CE4E5B9)
+        z &= 0xFFFFFFFFFFFFFFFF
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & 0xFFFFFFFFFFFFFFFF
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & 0xFFFFFFFFFFFFFFFF
+        return (z ^ (z >> 31)) & 0x7FFFFFFF
 
 
-def _single_adapter(layer):
-    """The one active plain-LoRA adapter of a peft layer, or None (lora.py:127-142)."""
+# The reference's name for the seed source.
+_Seeds = SeedStream
+
+
+def _plain_adapter(layer):
+    """The name of the adapter this patch computes for a peft LoRA layer: the only active one,
+    a plain one (no DoRA-style variant) made of bias-free nn.Linear A and B behind an
+    nn.Dropout or nn.Identity, on a layer that is neither disabled nor merged. None sends the
+    call to peft's own forward."""
     if layer.disable_adapters or layer.merged:
         return None
-    active = [a for a in layer.active_adapters if a in layer.lora_A.keys()]
-    if len(active) != 1:
+    names = [n for n in layer.active_adapters if n in layer.lora_A]
+    if len(names) != 1 or names[0] in getattr(layer, "lora_variant", {}):
         return None
-    a = active[0]
-    if a in getattr(layer, "lora_variant", {}):
+    n = names[0]
+    plain = all(type(m) is torch.nn.Linear and m.bias is None
+                for m in (layer.lora_A[n], layer.lora_B[n]))
+    if not plain or not isinstance(layer.lora_dropout[n], (torch.nn.Dropout, torch.nn.Identity)):
         return None
-    lora_a, lora_b = layer.lora_A[a], layer.lora_B[a]
-    if not (type(lora_a) is torch.nn.Linear and type(lora_b) is torch.nn.Linear
-            and lora_a.bias is None and lora_b.bias is None):
-        return None
-    if not isinstance(layer.lora_dropout[a], (torch.nn.Dropout, torch.nn.Identity)):
-        return None
-    return a
+    return n
 
 
 def patch():
-    """Routes peft's lora.bnb.Linear4bit.forward through DropoutCast / ScaledAdd
-    (lora.py:145-176). A no-op when peft is not installed."""
+    """peft's lora.bnb.Linear4bit.forward as base(x) + ScaledAdd(B(A(DropoutCast(x)))), the
+    reference's composition (lora.py:145-176), for calls this package takes: autocast on, a
+    float CUDA input, no extra arguments, one plain adapter. A no-op when peft is absent."""
     try:
         from peft.tuners.lora import bnb as lora_bnb
     except ImportError:
         return
-    cls = getattr(lora_bnb, "Linear4bit", None)
-    if cls is None:
-        return
-    original = cls.forward
-    if getattr(original, "_solution_patch", False):
+    if getattr(lora_bnb, "Linear4bit", None) is None:
         return
 
-    def forward(self, x, *args, **kwargs):
-        compute_dtype = _common.autocast_dtype()
-        adapter = None
-        if not args and not kwargs and compute_dtype is not None and _common.on_gpu(x) \
-                and x.dtype in (torch.float32, torch.float16, torch.bfloat16):
-            adapter = _single_adapter(self)
-        if adapter is None:
-            return original(self, x, *args, **kwargs)
-        result = self.base_layer(x)
-        drop = self.lora_dropout[adapter]
-        p = float(drop.p) if isinstance(drop, torch.nn.Dropout) and drop.training else 0.0
-        if TORCH_DROPOUT_RNG and p > 0:
-            xd = DropoutCast.apply(drop(x), 0.0, 0, compute_dtype)
-        else:
-            xd = DropoutCast.apply(x, p, _Seeds.next() if p > 0 else 0, compute_dtype)
-        lo = self.lora_B[adapter](self.lora_A[adapter](xd))
-        return ScaledAdd.apply(result, lo, self.scaling[adapter])
+    def build(original):
+        def forward(self, x, *args, **kwargs):
+            dtype = _common.autocast_dtype()
+            fits = (not args and not kwargs and dtype is not None and _common.on_gpu(x)
+                    and x.dtype in (torch.float32, torch.float16, torch.bfloat16))
+            name = _plain_adapter(self) if fits else None
+            if name is None:
+                return original(self, x, *args, **kwargs)
+            drop = self.lora_dropout[name]
+            p = float(drop.p) if isinstance(drop, torch.nn.Dropout) and drop.training else 0.0
+            base = self.base_layer(x)
+            if p > 0 and TORCH_DROPOUT_RNG:     # torch's own mask, then the cast
+                xd = DropoutCast.apply(drop(x), 0.0, 0, dtype)
+            else:
+                xd = DropoutCast.apply(x, p, SeedStream.next() if p > 0 else 0, dtype)
+            return ScaledAdd.apply(base, self.lora_B[name](self.lora_A[name](xd)),
+                                   self.scaling[name])
+        return forward
 
-    forward._solution_patch = True
-    cls.forward = forward
+    _common.install(lora_bnb.Linear4bit, "forward", build)

@@ -19,7 +19,7 @@ Every op here runs on the GPU through libqlora_b200.so; there is no CPU path.
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, ops  # noqa: F401 - ops registers the qlora_b200 custom operators
 
 # The NF4 code book of the QLoRA paper (Dettmers et al., 2023, appendix E): quantiles of N(0,1)
 # normalised to [-1, 1], with an exact zero.
@@ -149,35 +149,63 @@ def quantize_nf4(weight, blocksize=64, compress_statistics=True, blocksize2=256)
     return packed, state
 
 
-def dequantize_nf4(packed, quant_state, dtype=torch.float16, out=None):
-    """The weight [out_features, in_features] in `dtype`, rebuilt from the packed NF4 bytes.
-    Bit-exact with the reference kernel: fp32 scale = code2[q]*absmax2 + offset (two roundings),
-    w = nf4[nibble]*scale, rounded to nearest even in `dtype`."""
-    _lib.require_cuda(packed, what="dequantize_nf4")
-    shape = tuple(quant_state.shape)
-    if out is None:
-        out = torch.empty(shape, dtype=dtype, device=packed.device)
+def _scale_args(qs):
+    """(absmax, code2, absmax2, offset, blocksize2) of a quant state as the kernels take them:
+    code2 / absmax2 None for a state without double quantisation."""
+    if qs.nested:
+        return (qs.absmax, qs.state2.code, qs.state2.absmax, float(qs.offset),
+                int(qs.state2.blocksize))
+    return qs.absmax, None, None, 0.0, 2
+
+
+def state_of(absmax, code2, absmax2, offset, blocksize, blocksize2, rows, cols):
+    """A QuantState over the tensors a custom op receives (the inverse of _scale_args)."""
+    state2 = None
+    if code2 is not None:
+        state2 = QuantState(absmax=absmax2, code=code2, blocksize=blocksize2,
+                            quant_type="dynamic", dtype=torch.float32)
+    return QuantState(absmax=absmax, shape=torch.Size((rows, cols)), blocksize=blocksize,
+                      quant_type="nf4", offset=offset if state2 is not None else None,
+                      state2=state2)
+
+
+def dequant_into(out, packed, absmax, code2, absmax2, offset, blocksize, blocksize2):
+    """qb_nf4_dequant into `out` (any float dtype, out.numel() weights); code2 / absmax2 None for
+    single-level scales (fp32 absmax)."""
+    _lib.require_cuda(packed, out, what="dequantize_nf4")
     n = out.numel()
-    if quant_state.nested:
-        absmax = quant_state.absmax.contiguous()
-        code2 = quant_state.state2.code.float().contiguous()
-        absmax2 = quant_state.state2.absmax.float().contiguous()
-        offset = float(quant_state.offset)
-        blocksize2 = int(quant_state.state2.blocksize)
+    nested = code2 is not None
+    if nested:
+        absmax = absmax.contiguous()
+        code2 = code2.float().contiguous()
+        absmax2 = absmax2.float().contiguous()
         c2p, a2p = code2.data_ptr(), absmax2.data_ptr()
     else:
-        absmax = quant_state.absmax.float().contiguous()
+        absmax = absmax.float().contiguous()
         offset, blocksize2, c2p, a2p = 0.0, 2, None, None
     lut = nf4_table(packed.device)
     packed = packed.reshape(-1)
-    n_blocks = absmax.numel()
-    work = (n // 2 + n * out.element_size() + n_blocks * absmax.element_size()
-            + (quant_state.state2.absmax.numel() * 4 if quant_state.nested else 0), 0)
-    _lib.call("qb_nf4_dequant", packed.data_ptr(), n, absmax.data_ptr(),
-              int(bool(quant_state.nested)), c2p, a2p, offset, int(quant_state.blocksize),
-              blocksize2, lut.data_ptr(), out.data_ptr(), _lib.tag(out.dtype),
-              _lib.stream(packed.device), work=work)
+    work = (n // 2 + n * out.element_size() + absmax.numel() * absmax.element_size()
+            + (absmax2.numel() * 4 if nested else 0), 0)
+    _lib.call("qb_nf4_dequant", packed.data_ptr(), n, absmax.data_ptr(), int(nested), c2p, a2p,
+              float(offset), int(blocksize), int(blocksize2), lut.data_ptr(), out.data_ptr(),
+              _lib.tag(out.dtype), _lib.stream(packed.device), work=work)
     return out
+
+
+def dequantize_nf4(packed, quant_state, dtype=torch.float16, out=None):
+    """The weight [out_features, in_features] in `dtype`, rebuilt from the packed NF4 bytes
+    (the custom op qlora_b200::nf4_dequant; with `out`, written into that buffer directly).
+    Bit-exact with the reference kernel: fp32 scale = code2[q]*absmax2 + offset (two roundings),
+    w = nf4[nibble]*scale, rounded to nearest even in `dtype`."""
+    _lib.require_cuda(packed, what="dequantize_nf4")
+    absmax, code2, absmax2, offset, bs2 = _scale_args(quant_state)
+    if out is not None:
+        return dequant_into(out, packed, absmax, code2, absmax2, offset,
+                            int(quant_state.blocksize), bs2)
+    rows, cols = (int(d) for d in quant_state.shape)
+    return torch.ops.qlora_b200.nf4_dequant(packed, absmax, code2, absmax2, offset,
+                                            int(quant_state.blocksize), bs2, rows, cols, dtype)
 
 
 def fused_ok(x, quant_state):
@@ -305,29 +333,19 @@ def nf4_linear_dgrad(dy, packed, qs, v=None, lora_a=None, path=None, weight=None
     return dx.view(*dy.shape[:-1], in_f)
 
 
-class NF4Linear(torch.autograd.Function):
+class NF4Linear:
     """y = x @ W.T + b, W rebuilt from NF4 in forward and again in backward (nothing dense is kept
-    between them). W and b are frozen: the backward returns dX only (nf4.py:95-112)."""
+    between them); W and b are frozen, the backward gives dX only (nf4.py:95-112). The
+    reference's autograd.Function name, over the custom op qlora_b200::nf4_linear (whose
+    registered backward is qlora_b200::nf4_linear_dgrad)."""
 
     @staticmethod
-    def forward(ctx, x, packed, quant_state, bias):
-        ctx.packed, ctx.quant_state = packed, quant_state
-        ctx.fused = fused_ok(x, quant_state)
-        if ctx.fused:   # bf16: the dequant happens inside the tcgen05 GEMM
-            return nf4_linear_fwd(x, packed, quant_state, bias)
-        weight = dequantize_nf4(packed, quant_state, x.dtype)
-        return torch.nn.functional.linear(x, weight, bias)
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        grad_x = None
-        if ctx.needs_input_grad[0]:
-            if ctx.fused and grad_out.dtype == torch.bfloat16:
-                grad_x = nf4_linear_dgrad(grad_out, ctx.packed, ctx.quant_state)
-            else:
-                weight = dequantize_nf4(ctx.packed, ctx.quant_state, grad_out.dtype)
-                grad_x = torch.matmul(grad_out, weight)
-        return grad_x, None, None, None
+    def apply(x, packed, quant_state, bias):
+        absmax, code2, absmax2, offset, bs2 = _scale_args(quant_state)
+        out_f, in_f = (int(d) for d in quant_state.shape)
+        return torch.ops.qlora_b200.nf4_linear(x, packed, absmax, code2, absmax2, offset,
+                                               int(quant_state.blocksize), bs2, out_f, in_f,
+                                               bias)
 
 
 def _prepare(module, x):
@@ -360,36 +378,31 @@ def _prepare(module, x):
     return x, bias, inp_dtype
 
 
-_ORIGINAL = {}
+def _upstream_forward(module):
+    """bitsandbytes' own forward of the module's class (the one patch_linear4bit replaced)."""
+    from ._common import PATCH_MARK
+    fwd = type(module).forward
+    return fwd.__wrapped__ if getattr(fwd, PATCH_MARK, False) else fwd
 
 
 def linear4bit(module, x, keep_compute_dtype=False):
-    """bitsandbytes' Linear4bit.forward on our kernels. With keep_compute_dtype the output stays
-    in the compute dtype instead of being cast back to the input dtype (nf4.py:141-149)."""
+    """bitsandbytes' Linear4bit.forward on our kernels; a layer they do not take runs
+    bitsandbytes' own forward. With keep_compute_dtype the output stays in the compute dtype
+    instead of being cast back to the input dtype (nf4.py:141-149)."""
     prepared = _prepare(module, x)
     if prepared is None:
-        original = _ORIGINAL.get("forward")
-        if original is None:
-            raise RuntimeError("linear4bit: unsupported layer and no original forward to fall back to")
-        return original(module, x)
+        return _upstream_forward(module)(module, x)
     x, bias, inp_dtype = prepared
     out = NF4Linear.apply(x, module.weight, module.weight.quant_state, bias)
     return out if keep_compute_dtype else out.to(inp_dtype)
 
 
 def patch_linear4bit():
-    """Routes bitsandbytes' Linear4bit.forward through linear4bit (nf4.py:155-166)."""
+    """bitsandbytes' Linear4bit.forward through linear4bit (nf4.py:155-166)."""
     import bitsandbytes.nn.modules as bnb_modules
 
-    cls = bnb_modules.Linear4bit
-    if "forward" in _ORIGINAL:
-        return
-    _ORIGINAL["forward"] = cls.forward
-
-    def forward(self, x):
-        return linear4bit(self, x)
-
-    cls.forward = forward
+    from ._common import install
+    install(bnb_modules.Linear4bit, "forward", lambda original: lambda self, x: linear4bit(self, x))
 
 
 def project(layer, x):

@@ -11,7 +11,7 @@ original element-wise ops do.
 
 import torch
 
-from . import _common, _lib
+from . import _common, _lib, ops  # noqa: F401 - ops registers the custom operators
 
 
 def _launch(q, k, cos, sin, q_out, k_out, backward):
@@ -57,31 +57,27 @@ def _unit_last(t):
     return t if t.stride(-1) == 1 else t.contiguous()
 
 
-class CudaRoPE(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, q, k, cos, sin):
-        _lib.require_cuda(q, k, cos, sin, what="rope")
-        B, _, S, _ = q.shape
-        q, k = _unit_last(q), _unit_last(k)
-        cos = _unit_last(cos).expand(B, S, -1)   # (B or 1, S, D) -> (B, S, D), stride 0 on B
-        sin = _unit_last(sin).expand(B, S, -1)
-        q_out = torch.empty_like(q, dtype=torch.promote_types(q.dtype, cos.dtype))
-        k_out = torch.empty_like(k, dtype=torch.promote_types(k.dtype, cos.dtype))
-        _launch(q, k, cos, sin, q_out, k_out, backward=False)
-        ctx.save_for_backward(cos, sin)  # the backward needs no activations
-        ctx.q_dtype, ctx.k_dtype = q.dtype, k.dtype
-        return q_out, k_out
+def apply_into(q, k, cos, sin, q_out, k_out, transpose):
+    """RoPE (transpose=False) or its transpose on q [B, HQ, S, D] and k [B, HK, S, D] (unit last
+    stride, any other strides) into q_out / k_out; cos/sin (B or 1, >= S, D)."""
+    _lib.require_cuda(q, k, cos, sin, what="rope")
+    B = q.shape[0]
+    cos = _unit_last(cos).expand(B, cos.shape[1], -1)   # (B or 1, S, D) -> (B, S, D)
+    sin = _unit_last(sin).expand(B, sin.shape[1], -1)
+    _launch(q, k, cos, sin, q_out, k_out, transpose)
+
+
+class CudaRoPE:
+    """Rotate-half RoPE of q and k in one launch (rope.py:82-104): the custom op qlora_b200::rope,
+    whose registered backward is the same op with the transposed rotation. Outputs are in
+    promote(q, cos) / promote(k, cos) and keep q's / k's layout."""
 
     @staticmethod
-    def backward(ctx, dq_out, dk_out):
-        cos, sin = ctx.saved_tensors
-        dq_out, dk_out = _unit_last(dq_out), _unit_last(dk_out)
-        if dq_out.dtype != dk_out.dtype:
-            dk_out = dk_out.to(dq_out.dtype)
-        dq = torch.empty_like(dq_out, dtype=ctx.q_dtype)
-        dk = torch.empty_like(dk_out, dtype=ctx.k_dtype)
-        _launch(dq_out, dk_out, cos, sin, dq, dk, backward=True)
-        return dq, dk, None, None
+    def apply(q, k, cos, sin):
+        _lib.require_cuda(q, k, cos, sin, what="rope")
+        return torch.ops.qlora_b200.rope(q, k, cos, sin, False,
+                                         torch.promote_types(q.dtype, cos.dtype),
+                                         torch.promote_types(k.dtype, cos.dtype))
 
 
 # The reference's class name (rope.py:82) and the alias its stale test imports
@@ -106,20 +102,17 @@ def _supported(q, k, cos, sin, unsqueeze_dim):
 
 
 def patch():
-    """Sends modeling_qwen2.apply_rotary_pos_emb through CudaRoPE when the inputs fit
-    (rope.py:120-135)."""
+    """modeling_qwen2.apply_rotary_pos_emb through CudaRoPE for the calls `_supported` admits
+    (rope.py:120-135); anything else, extra arguments included, goes to the original."""
     from transformers.models.qwen2 import modeling_qwen2 as m
 
-    original = m.apply_rotary_pos_emb
-    if getattr(original, "_solution_patch", False):
-        return
-
-    def apply_rotary_pos_emb(q, k, cos, sin, *args, **kwargs):
-        unsqueeze_dim = kwargs.get("unsqueeze_dim", args[0] if args else 1)
-        if len(args) > 1 or set(kwargs) - {"unsqueeze_dim"} or \
-                not _supported(q, k, cos, sin, unsqueeze_dim):
+    def build(original):
+        def apply_rotary_pos_emb(q, k, cos, sin, *args, **kwargs):
+            dim = kwargs.get("unsqueeze_dim", args[0] if args else 1)
+            if len(args) <= 1 and set(kwargs) <= {"unsqueeze_dim"} and \
+                    _supported(q, k, cos, sin, dim):
+                return CudaRoPE.apply(q, k, cos, sin)
             return original(q, k, cos, sin, *args, **kwargs)
-        return CudaRoPE.apply(q, k, cos, sin)
+        return apply_rotary_pos_emb
 
-    apply_rotary_pos_emb._solution_patch = True
-    m.apply_rotary_pos_emb = apply_rotary_pos_emb
+    _common.install(m, "apply_rotary_pos_emb", build)
