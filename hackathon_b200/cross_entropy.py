@@ -19,9 +19,11 @@ from . import _common, _lib, ops  # noqa: F401 - ops registers the custom operat
 
 IGNORE_INDEX = -100
 CHUNK_ROWS = 4096           # rows per chunk (the bf16 dZ of a 4096 x 152064 chunk: 1.2 GB)
-# Off the bf16 path dZ is stored in the matmul dtype before the dH matmul, multiplied by
-# GRAD_GAIN (a power of two, exact) so small probabilities survive fp16, and divided back in fp32.
-GRAD_GAIN = 65536.0
+# Off the bf16 path dZ = softmax - onehot is stored in the matmul dtype before the dH matmul. In
+# fp16 it is multiplied by GRAD_GAIN (a power of two, exact) so probabilities below fp16's
+# smallest subnormal survive, with |dZ| <= GRAD_GAIN far below fp16's largest value, and
+# divided back in fp32.
+GRAD_GAIN = 1024.0
 
 
 # False (the default): the logits exist only in TMEM - pass 1 reduces each tile to row
@@ -126,16 +128,16 @@ def linear_ce_rows(hidden, weight, target, chunk_rows, with_grad):
                      chunk_rows)
         return token_loss, entropy, pred, dh
     # other dtypes: a matmul chunk of logits, then the row kernel streams each row once for the
-    # statistics and rewrites it with (softmax - onehot) * GRAD_GAIN (fp16 keeps small
-    # probabilities), then dH_chunk = dZ W / GRAD_GAIN
+    # statistics and rewrites it with (softmax - onehot) * gain, then dH_chunk = dZ W / gain
+    gain = GRAD_GAIN if weight.dtype == torch.float16 else 1.0
     with torch.autocast(device_type=dev.type, enabled=False):
         for a in range(0, n, chunk_rows):
             b = min(a + chunk_rows, n)
             logits = h2[a:b] @ weight.t()
-            ce_rows_inplace(logits, tgt[a:b], token_loss[a:b], entropy[a:b], pred[a:b],
-                            GRAD_GAIN, with_grad)
+            ce_rows_inplace(logits, tgt[a:b], token_loss[a:b], entropy[a:b], pred[a:b], gain,
+                            with_grad)
             if with_grad:
-                dh[a:b] = (logits @ weight).float() * (1.0 / GRAD_GAIN)
+                dh[a:b] = (logits @ weight).float() * (1.0 / gain)
             del logits
     return token_loss, entropy, pred, dh
 

@@ -9,7 +9,7 @@
 //   reduce  qb_ce_reduce: merges the per-tile partials of every row into lse, loss =
 //           lse - z[label], entropy = lse - t/s, argmax, correct.
 //   pass 2  qb_linear_ce_grad: the logits tile again, epilogue dZ = (e^(z - lse) - onehot) *
-//           scale in bf16 (scale = GRAD_GAIN / denominator read on the device; 0 for unlabelled
+//           scale in bf16 (scale a device scalar, the caller's gradient factor; 0 for unlabelled
 //           rows) — the gradient, not the logits.
 //   then    dH = dZ W (qb_gemm_bf16 with W read MN-major), fp32.
 // Executed flops: 3 x 2 N H V against the algorithmic 4 N H V (logits + dH).
@@ -26,7 +26,7 @@ struct EpiGrad {
   int64_t ldz;
   const int64_t* target;
   const float* lse;        // [rows]
-  const float* scale_dev;  // device scalar: GRAD_GAIN / denominator
+  const float* scale_dev;  // device scalar: the factor dZ carries
   int rows, vocab;
   bool vec;
 

@@ -15,29 +15,77 @@ IGNORE_INDEX = -100
 
 class AdapterGradSync:
     """Points every adapter parameter's .grad at a slice of one flat fp32 buffer and all-reduces
-    that buffer (in `bucket_bytes` pieces) after the backward."""
+    it in buckets of about `bucket_bytes`, overlapped with the backward: each bucket is a run
+    of consecutive parameters (whole parameters, in their order), and once the backward has
+    accumulated the gradient of every parameter of a bucket (a post-accumulate-grad hook per
+    parameter), its all-reduce is issued asynchronously - NCCL orders it after the gradient
+    kernels on the current stream and runs it on its own stream while the backward goes on
+    with earlier layers. Calling the object after the backward issues what is still pending
+    (buckets whose parameters got no gradient) and makes the current stream wait for every
+    reduction, so the optimizer reads the summed gradients.
 
-    def __init__(self, params, group=None, bucket_bytes=256 << 20):
+    Each parameter must receive one gradient accumulation per backward (as the step's adapters
+    do); a second one after its bucket was reduced raises. overlap=False reduces everything
+    after the backward instead."""
+
+    def __init__(self, params, group=None, bucket_bytes=32 << 20, overlap=True):
         params = [p for p in params if p.requires_grad]
         if not params:
             raise ValueError("AdapterGradSync: no trainable parameters")
         dev = params[0].device
         total = sum(p.numel() for p in params)
         self.flat = torch.zeros(total, dtype=torch.float32, device=dev)
-        off = 0
+        self.group = group
+        self.buckets = []           # (flat slice, number of parameters)
+        bucket_of = {}
+        off = start = count = 0
+        limit = max(1, bucket_bytes // 4)
         for p in params:
             if p.dtype != torch.float32:
                 raise TypeError("AdapterGradSync: adapters must be fp32 (master weights)")
             p.grad = self.flat[off: off + p.numel()].view_as(p)
             off += p.numel()
-        self.group = group
-        n = max(1, bucket_bytes // 4)
-        self.buckets = [self.flat[i: i + n] for i in range(0, total, n)]
+            bucket_of[p] = len(self.buckets)
+            count += 1
+            if off - start >= limit:
+                self.buckets.append((self.flat[start:off], count))
+                start, count = off, 0
+        if count:
+            self.buckets.append((self.flat[start:off], count))
+        self.overlap = overlap and self._world() > 1
+        self._seen = [0] * len(self.buckets)
+        self._work = [None] * len(self.buckets)
+        if self.overlap:
+            for p in params:
+                p.register_post_accumulate_grad_hook(self._hook(bucket_of[p]))
+
+    def _world(self):
+        return dist.get_world_size(self.group) if dist.is_initialized() else 1
+
+    def _launch(self, i):
+        self._work[i] = dist.all_reduce(self.buckets[i][0], op=dist.ReduceOp.SUM,
+                                        group=self.group, async_op=True)
+
+    def _hook(self, i):
+        def on_grad(param):
+            if self._work[i] is not None:
+                raise RuntimeError("AdapterGradSync: a gradient accumulated into bucket "
+                                   f"{i} after its all-reduce was issued")
+            self._seen[i] += 1
+            if self._seen[i] == self.buckets[i][1]:
+                self._launch(i)
+        return on_grad
 
     def __call__(self):
-        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
-            for b in self.buckets:
-                dist.all_reduce(b, op=dist.ReduceOp.SUM, group=self.group)
+        if self._world() <= 1:
+            return
+        for i in range(len(self.buckets)):
+            if self._work[i] is None:
+                self._launch(i)
+        for i, w in enumerate(self._work):
+            w.wait()
+            self._work[i] = None
+            self._seen[i] = 0
 
 
 def global_label_count(labels, group=None):

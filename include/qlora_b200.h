@@ -346,7 +346,7 @@ int qb_ce_reduce(const void* partials, int64_t n_vtiles, int64_t rows, int64_t v
                  int64_t* pred, int32_t* correct, float* lse, cudaStream_t stream);
 
 /* Pass 2: dz[rows, vocab] (bf16, row stride ldz) = (exp(z - lse) - onehot(label)) * scale, with
- * scale = *scale_dev (a device scalar, e.g. GRAD_GAIN / denominator) for labelled rows and 0
+ * scale = *scale_dev (a device scalar, e.g. 1 / denominator) for labelled rows and 0
  * otherwise (solution/cross_entropy.py:83-90). dH = dz @ weight follows with qb_gemm_bf16. */
 int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight, int64_t ldw,
                       const int64_t* target, int64_t rows, int64_t vocab, int64_t hdim,

@@ -16,20 +16,25 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out):
+def _model():
+    return torch.nn.Sequential(torch.nn.Linear(8, 5), torch.nn.Linear(5, 3))
+
+
+def _worker(rank, world, port, out, overlap=True, bucket_bytes=64):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from hackathon_b200.dp import AdapterGradSync, global_label_count, shard_rows
         torch.manual_seed(0)
-        model = torch.nn.Linear(8, 3, bias=False)
+        model = _model()
         xs = torch.randn(10, 6, 8)
         labels = torch.randint(0, 3, (10, 6))
         labels[labels == 2] = -100
         lo, hi = shard_rows(10, rank, world)
         x, lb = xs[lo:hi], labels[lo:hi]
-        sync = AdapterGradSync(model.parameters())
+        sync = AdapterGradSync(model.parameters(), bucket_bytes=bucket_bytes, overlap=overlap)
+        out[f"buckets{rank}"] = len(sync.buckets)
         n = global_label_count(lb)
         logits = model(x)[:, :-1]
         tgt = lb[:, 1:]
@@ -37,19 +42,24 @@ def _worker(rank, world, port, out):
                                                  ignore_index=-100, reduction="sum") / n
         loss.backward()
         sync()
-        out[rank] = (model.weight.grad.clone(), float(n))
+        out[rank] = ([p.grad.clone() for p in model.parameters()], float(n))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.timeout(120)
-def test_dp_gradient_equals_global_mean_gradient():
+@pytest.mark.timeout(180)
+@pytest.mark.parametrize("overlap", [True, False])
+def test_dp_gradient_equals_global_mean_gradient(overlap):
+    """Two gloo ranks, four parameters (40, 5, 15 and 3 values) in three buckets under a 64-byte
+    limit: reduced from the backward's gradient hooks as each bucket completes (overlap) or all
+    after the backward - either way every rank ends with the gradient of the global mean
+    loss."""
     world = 2
     mgr = mp.get_context("spawn").Manager()   # no fork of this (possibly threaded) process
     out = mgr.dict()
-    mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), out, overlap), nprocs=world, join=True)
     torch.manual_seed(0)
-    model = torch.nn.Linear(8, 3, bias=False)
+    model = _model()
     xs = torch.randn(10, 6, 8)
     labels = torch.randint(0, 3, (10, 6))
     labels[labels == 2] = -100
@@ -58,9 +68,11 @@ def test_dp_gradient_equals_global_mean_gradient():
                                              ignore_index=-100)
     loss.backward()
     for r in range(world):
+        assert out[f"buckets{r}"] == 3
         g, n = out[r]
         assert n == float((labels[:, 1:] != -100).sum())
-        torch.testing.assert_close(g, model.weight.grad, rtol=1e-5, atol=1e-6)
+        for a, b in zip(g, model.parameters()):
+            torch.testing.assert_close(a, b.grad, rtol=1e-5, atol=1e-6)
 
 
 def test_shard_rows_cover_everything():
