@@ -329,11 +329,11 @@ def run_reference(args, rank, world):
 
 
 KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
-           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "linear_ce", "mask_acc",
-           "gateup_swiglu", "gemm2_dgrad_pair", "gemm2_rope", "dropout_bits", "lora_xa",
-           "lora_xa_xd")
+           "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "rmsnorm_bwd",
+           "rope_bwd", "linear_ce", "mask_acc", "gateup_swiglu", "gemm2_dgrad_pair",
+           "gemm2_rope", "dropout_bits", "lora_xa", "lora_xa_xd", "lora_grads")
 GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd",
-             "dropout_bits")
+             "rmsnorm_bwd", "rope_bwd", "dropout_bits")
 
 
 def kernel_case(args):
@@ -429,6 +429,13 @@ def kernel_case(args):
         cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
         fn = lambda: gemm2_rope(x, w, u, sb, cos, sin)  # noqa: E731
         flops = 2 * T * fo * (fi + r)
+    elif name == "lora_grads":
+        # the LoRA branch's backward products of one projection: V = g (s B), dA = V^T xd,
+        # dB = s g^T U (tcgen05 GEMMs, dA / dB split over the tokens)
+        from hackathon_b200.gemm import lora_products
+        gy, u, xd, sb = rnd(T, fo), rnd(T, r), rnd(T, fi), rnd(fo, r, s=0.05)
+        fn = lambda: lora_products(gy, u, xd, sb, (r, fi), 2.0)  # noqa: E731
+        flops = 2 * T * fo * r + 2 * r * fi * T + 2 * fo * r * T
     elif name == "mask_acc":
         # the backward LoRA input-gradient term: dx[T, in] += s * mask .* (V[T, r] A[r, in])
         from hackathon_b200.gemm import gemm_mask_acc
@@ -444,6 +451,26 @@ def kernel_case(args):
         labels[torch.rand((1, T), device=dev, generator=g) < 0.1] = -100
         fn = lambda: fused_causal_lm_loss(h.view(1, T, fi), wv, labels)  # noqa: E731
         flops = 4 * T * fi * fo        # algorithmic: logits + dH (executed: 6 N H V)
+    elif name == "rmsnorm_bwd":
+        # dx from dy, x, w and the saved rstd (the C-ABI call the backward makes)
+        from hackathon_b200.rmsnorm import bwd_into
+        x, wn, dy = rnd(T, fi), rnd(fi), rnd(T, fi)
+        rstd = torch.rsqrt(x.float().pow(2).mean(-1) + 1e-6)
+        dx = torch.empty_like(x)
+        fn = lambda: bwd_into(dy, x, wn, rstd, dx)  # noqa: E731
+        nbytes = 3 * T * fi * 2 + fi * 2 + T * 4
+    elif name == "rope_bwd":
+        # the transposed rotation of the q/k projection outputs as the step applies it (rows of
+        # tokens, 128-dim heads, one [S, 128] table; --out-features = heads x 128)
+        from hackathon_b200.rope import rope_rows
+        S = 4096
+        pos = torch.arange(S, device=dev, dtype=torch.float32)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=dev, dtype=torch.float32) / 128))
+        emb = torch.cat([torch.outer(pos, inv)] * 2, dim=-1)
+        cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+        g2 = rnd(T, fo)
+        fn = lambda: rope_rows(g2, cos, sin, backward=True)  # noqa: E731
+        nbytes = 2 * T * fo * 2 + 2 * S * 128 * 2
     else:
         x, wn = rnd(T, fi), rnd(fi)
         fn = lambda: rmsnorm(x, wn, 1e-6)  # noqa: E731
@@ -506,6 +533,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="print every kernel of one step with its device time (torch.profiler)")
+    ap.add_argument("--step-deadline", type=float, default=STEP_DEADLINE_S,
+                    help="seconds a step may take before the watchdog ends the run (raise it "
+                         "under a profiler, which serialises every launch)")
     ap.add_argument("--kernel", default=None, choices=KERNELS,
                     help="time one op of the step alone at a projection shape")
     ap.add_argument("--graph", action="store_true",
@@ -583,7 +613,7 @@ def main():
     _phase(f"{args.warmup} warm-up steps")
     try:
         for i in range(args.warmup):
-            run_checked(dog.watched(f"warm-up step {i}", STEP_DEADLINE_S,
+            run_checked(dog.watched(f"warm-up step {i}", args.step_deadline,
                                   lambda: synced_step(i)), device_error, f"warm-up step {i}")
             _phase(f"warm-up step {i} done")
     except RunFailed as e:
@@ -619,15 +649,17 @@ def main():
             barrier()
             torch.cuda.synchronize()
             start.record()
+            torch.cuda.nvtx.range_push("timed_steps")   # selects these launches in a profiler
             for i in range(args.steps):
                 step(i)
+            torch.cuda.nvtx.range_pop()
             end.record()
             torch.cuda.synchronize()
             barrier()
         return clocks
 
     try:
-        clocks = run_checked(dog.watched("timed steps", STEP_DEADLINE_S * (1 + args.steps / 4),
+        clocks = run_checked(dog.watched("timed steps", args.step_deadline * (1 + args.steps / 4),
                                        timed_steps), device_error, "timed steps")
     except RunFailed as e:
         fail(args, world, str(e), monitor_report(lib, local))
@@ -649,7 +681,7 @@ def main():
         return kt.summary()
 
     try:
-        ksum = run_checked(dog.watched("instrumented step", STEP_DEADLINE_S, instrumented_step),
+        ksum = run_checked(dog.watched("instrumented step", args.step_deadline, instrumented_step),
                          device_error, "instrumented step")
     except RunFailed as e:
         fail(args, world, str(e), monitor_report(lib, local))
@@ -679,7 +711,7 @@ def main():
 
     try:
         loss_value = run_checked(dog.watched("end-to-end steps",
-                                           STEP_DEADLINE_S * (1 + args.steps / 4), e2e_steps),
+                                           args.step_deadline * (1 + args.steps / 4), e2e_steps),
                                device_error, "end-to-end steps")
     except RunFailed as e:
         fail(args, world, str(e), monitor_report(lib, local))

@@ -18,7 +18,11 @@ import torch
 from . import _common, _lib, ops  # noqa: F401 - ops registers the custom operators
 
 IGNORE_INDEX = -100
-CHUNK_ROWS = 4096           # rows per chunk (the bf16 dZ of a 4096 x 152064 chunk: 1.2 GB)
+CHUNK_ROWS = 4096           # rows per chunk of materialised logits (the matmul fallback)
+# Rows per chunk on the tcgen05 path, where only dZ (bf16) is materialised: 16384 x 152064 is
+# 5 GB, and the dH GEMM's 1792 output tiles of a 16384-row chunk fill 12.1 waves of the 148 SMs
+# (a 4096-row chunk's 448 tiles: 3.03 waves, the last one nearly empty).
+TC_CHUNK_ROWS = 16384
 # Off the bf16 path dZ = softmax - onehot is stored in the matmul dtype before the dH matmul. In
 # fp16 it is multiplied by GRAD_GAIN (a power of two, exact) so probabilities below fp16's
 # smallest subnormal survive, with |dZ| <= GRAD_GAIN far below fp16's largest value, and
@@ -110,7 +114,8 @@ def linear_ce_rows(hidden, weight, target, chunk_rows, with_grad):
     loss, the entropy of the softmax, the argmax (first index on ties), and with_grad the
     gradient of that row's loss w.r.t. its hidden state, (softmax - onehot) @ W in fp32 (zero
     for unlabelled rows; else an empty [0, H]). Only `chunk_rows` rows of logits exist at a time,
-    on the tcgen05 path none at all (they stay in TMEM)."""
+    on the tcgen05 path none at all (they stay in TMEM; it runs chunks of at least TC_CHUNK_ROWS
+    rows, its bf16 dZ the one [rows, vocab] buffer)."""
     _lib.require_cuda(hidden, weight, target, what="fused linear CE")
     n, hdim = hidden.shape
     dev = hidden.device
@@ -125,7 +130,7 @@ def linear_ce_rows(hidden, weight, target, chunk_rows, with_grad):
     if tc_path_ok(h2, weight):
         one = torch.ones(1, dtype=torch.float32, device=dev)   # dZ unscaled: bf16 keeps range
         linear_ce_tc(h2, weight, tgt, token_loss, entropy, pred, dh if with_grad else None, one,
-                     chunk_rows)
+                     max(chunk_rows, TC_CHUNK_ROWS))
         return token_loss, entropy, pred, dh
     # other dtypes: a matmul chunk of logits, then the row kernel streams each row once for the
     # statistics and rewrites it with (softmax - onehot) * gain, then dH_chunk = dZ W / gain

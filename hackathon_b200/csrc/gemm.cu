@@ -1,6 +1,8 @@
 // Plain bf16 GEMMs on the tcgen05 kernel, fp32 accumulation, fp32 or bf16 output:
 //   qb_gemm_bf16    C[M,N] = A[M,K] * B[N,K]^T (+ bias[N])
 //   qb_gemm2_bf16   C[M,N] = A0[M,K0] * B0[N,K0]^T + A1[M,K1] * B1[N,K1]^T (+ bias[N])
+//   qb_gemm_bf16_acc_f32   C[M,N] (fp32) += alpha * A[M,K] * B[N,K]^T, K split over the SMs
+//                          (partials in a workspace, summed in a fixed order: deterministic)
 // Each operand may be K-major or MN-major in HBM (qb_gemm_bf16: every orientation the suite
 // needs — logits = H W^T, dH = dZ W, LoRA products; qb_gemm2_bf16: the two layouts of a
 // projection with its LoRA term as extra K, forward and input gradient).
@@ -60,6 +62,113 @@ struct EpiStoreRow {
     }
   }
 };
+
+// C += alpha * the tile, fp32 (C += alpha A B^T in one work item per tile): each element is
+// read and written by the one thread that owns its row.
+struct EpiAccF32 {
+  float* c;
+  int64_t ldc;
+  int M, N;
+  float alpha;
+  bool vec;   // 16-byte aligned rows
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
+    const int m = m0 + row;
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      float v[32];
+      tc::tmem_ld32(taddr + ch * 32, v);
+      const int n = n0 + ch * 32;
+      if (m >= M || n >= N) continue;
+      float* dst = c + static_cast<int64_t>(m) * ldc + n;
+      if (vec && n + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          float4 o = *reinterpret_cast<const float4*>(dst + i);
+          o.x += alpha * v[i];
+          o.y += alpha * v[i + 1];
+          o.z += alpha * v[i + 2];
+          o.w += alpha * v[i + 3];
+          *reinterpret_cast<float4*>(dst + i) = o;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < N) dst[i] += alpha * v[i];
+      }
+    }
+  }
+};
+
+// The raw fp32 partial product of one split-K work item into the workspace: row m0 + row of
+// [splits x Mp, ldw] (the kernel passes m0 already offset by split x Mp; Mp = M padded to whole
+// tiles), columns below N. split_reduce_kernel then sums the splits in order.
+struct EpiPartialF32 {
+  float* ws;
+  int64_t ldw;   // a multiple of 4: 16-byte rows
+  int N;
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
+    const int64_t m = static_cast<int64_t>(m0) + row;
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      float v[32];
+      tc::tmem_ld32(taddr + ch * 32, v);
+      const int n = n0 + ch * 32;
+      if (n >= N) continue;
+      float* dst = ws + m * ldw + n;
+      if (n + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < N) dst[i] = v[i];
+      }
+    }
+  }
+};
+
+// C[m, n] += alpha * (((P_0 + P_1) + P_2) + ...) over the splits' partials P_s (rows s x Mp of
+// the workspace): a fixed summation order, so a split launch gives the same bits every time.
+// VEC: four columns per thread (N, ldc and ldw multiples of 4, C 16-byte aligned).
+template <bool VEC>
+__global__ void __launch_bounds__(256)
+split_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int64_t split_stride, int splits,
+                    float alpha, float* __restrict__ c, int64_t ldc, int M, int N) {
+  const int per_row = VEC ? N / 4 : N;
+  const int64_t total = static_cast<int64_t>(M) * per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / per_row;
+    const int n = static_cast<int>(i - m * per_row) * (VEC ? 4 : 1);
+    const float* p = ws + m * ldw + n;
+    float* dst = c + m * ldc + n;
+    if (VEC) {
+      float4 acc = __ldg(reinterpret_cast<const float4*>(p));
+      for (int sp = 1; sp < splits; ++sp) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(p + sp * split_stride));
+        acc.x += q.x;
+        acc.y += q.y;
+        acc.z += q.z;
+        acc.w += q.w;
+      }
+      float4 o = *reinterpret_cast<const float4*>(dst);
+      o.x += alpha * acc.x;
+      o.y += alpha * acc.y;
+      o.z += alpha * acc.z;
+      o.w += alpha * acc.w;
+      *reinterpret_cast<float4*>(dst) = o;
+    } else {
+      float acc = __ldg(p);
+      for (int sp = 1; sp < splits; ++sp) acc += __ldg(p + sp * split_stride);
+      *dst += alpha * acc;
+    }
+  }
+}
 
 // Gate / up pair with SwiGLU: the tile's first BN/2 accumulator columns are gate features
 // j0..j0+BN/2-1 (j0 = n0 / 2), the last BN/2 the same up features. Each is rounded to bf16 — the
@@ -266,6 +375,24 @@ int run_dtype(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_
   return run<A0, B0, A1, B1, kBN, __nv_bfloat16>(m, pb, c, ldc, bias, resid, ldr, vec, s, what);
 }
 
+// run_dtype for a single-segment GEMM whose output tiles are `bn` wide (narrow_bn).
+template <int A0, int B0>
+int run_narrow(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
+               int c_dtype, const float* bias, bool vec, cudaStream_t s, const char* what,
+               int bn) {
+  using tcg::kTmaK;
+  if (bn == 64) {
+    if (c_dtype == QB_F32)
+      return run<A0, B0, kTmaK, kTmaK, 64, float>(m, pb, c, ldc, bias, nullptr, 0, vec, s, what);
+    return run<A0, B0, kTmaK, kTmaK, 64, __nv_bfloat16>(m, pb, c, ldc, bias, nullptr, 0, vec, s,
+                                                       what);
+  }
+  if (c_dtype == QB_F32)
+    return run<A0, B0, kTmaK, kTmaK, 128, float>(m, pb, c, ldc, bias, nullptr, 0, vec, s, what);
+  return run<A0, B0, kTmaK, kTmaK, 128, __nv_bfloat16>(m, pb, c, ldc, bias, nullptr, 0, vec, s,
+                                                      what);
+}
+
 int check_common(const void* C, int c_dtype, int64_t M, int64_t N, const char* what) {
   if (M < 0 || N < 0 || M > (1 << 30) || N > (1 << 30))
     return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
@@ -275,11 +402,15 @@ int check_common(const void* C, int c_dtype, int64_t M, int64_t N, const char* w
   return QB_OK;
 }
 
-tcg::Problem problem(int64_t M, int64_t N, int64_t K0, int64_t K1) {
+tcg::Problem problem(int64_t M, int64_t N, int64_t K0, int64_t K1, int bn = kBN) {
   return tcg::Problem{static_cast<int>(M), static_cast<int>(N), static_cast<int>((K0 + 63) / 64),
                       static_cast<int>((K1 + 63) / 64), static_cast<int>((M + 127) / 128),
-                      static_cast<int>((N + kBN - 1) / kBN)};
+                      static_cast<int>((N + bn - 1) / bn), 1};
 }
+
+// Output tile width of a single-segment GEMM: skinny outputs (the rank-64 LoRA products) take
+// 64- or 128-wide tiles instead of paying 256-wide MMAs for columns that do not exist.
+int narrow_bn(int64_t N) { return N <= 64 ? 64 : (N <= 128 ? 128 : kBN); }
 
 bool vec_ok(const void* C, int64_t ldc, int c_dtype) {
   return qb::aligned16(C) && (ldc * (c_dtype == QB_F32 ? 4 : 2)) % 16 == 0;
@@ -298,14 +429,25 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const vo
   if (K == 0) return qb::fail(QB_ERR_UNSUPPORTED, "%s: K == 0", what);
   if (!A || !B) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
   CUtensorMap m[4];
+  const bool pair = use_pair(!a_mn_major, M, N);
+  const int bn = pair ? kBN : narrow_bn(N);
   if (int s = map_operand(&m[0], A, lda, a_mn_major != 0, M, K, tcg::BM)) return s;
-  if (int s = map_operand(&m[1], B, ldb, b_mn_major != 0, N, K, kBN)) return s;
+  if (int s = map_operand(&m[1], B, ldb, b_mn_major != 0, N, K, bn)) return s;
   m[2] = m[0];
   m[3] = m[1];
-  const tcg::Problem pb = problem(M, N, K, 0);
+  const tcg::Problem pb = problem(M, N, K, 0, bn);
   const bool vec = vec_ok(C, ldc, c_dtype);
+  if (bn != kBN) {
+    using namespace tcg;
+    if (!a_mn_major && !b_mn_major)
+      return run_narrow<kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what, bn);
+    if (!a_mn_major && b_mn_major)
+      return run_narrow<kTmaK, kTmaMN>(m, pb, C, ldc, c_dtype, bias, vec, stream, what, bn);
+    if (a_mn_major && !b_mn_major)
+      return run_narrow<kTmaMN, kTmaK>(m, pb, C, ldc, c_dtype, bias, vec, stream, what, bn);
+    return run_narrow<kTmaMN, kTmaMN>(m, pb, C, ldc, c_dtype, bias, vec, stream, what, bn);
+  }
   CUtensorMap mp[4] = {m[0], m[1], m[2], m[3]};
-  const bool pair = use_pair(!a_mn_major, M, N);
   if (pair) {
     if (int s = pair_maps(mp, B, ldb, b_mn_major != 0, K, B, ldb, b_mn_major != 0, K, N)) return s;
   }
@@ -322,6 +464,121 @@ extern "C" int qb_gemm_bf16(const void* A, int64_t lda, int a_mn_major, const vo
                                                   stream, what);
   return run_dtype<kTmaMN, kTmaMN, kTmaK, kTmaK>(m, pb, C, ldc, c_dtype, bias, nullptr, 0, vec,
                                                  stream, what);
+}
+
+namespace {
+
+// Split-K factor for `tiles` output tiles of `nk` k-blocks on `sms` persistent CTAs: the one that
+// minimises waves x (k-blocks per item + a per-item cost of kItemCostKb k-blocks - the pipeline
+// ramp and the partial tile's store), keeping 4 k-blocks per item at least. Few tiles (the LoRA
+// weight gradients: 28 tiles over 256 k-blocks -> 5 splits, one wave) spread over the SMs.
+constexpr int64_t kItemCostKb = 8;
+
+int k_splits(int64_t tiles, int64_t nk, int64_t sms) {
+  int64_t best = 1, best_cost = -1;
+  const int64_t max_splits = nk / 4 > 1 ? (nk / 4 < 64 ? nk / 4 : 64) : 1;
+  for (int64_t s = 1; s <= max_splits; ++s) {
+    const int64_t waves = (tiles * s + sms - 1) / sms;
+    const int64_t cost = waves * ((nk + s - 1) / s + kItemCostKb);
+    if (best_cost < 0 || cost * 100 < best_cost * 99) {   // a split more must gain 1%
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return static_cast<int>(best);
+}
+
+struct AccPlan {
+  tcg::Problem pb;
+  int bn;
+  int64_t ldw;         // workspace row stride (floats)
+  int64_t ws_floats;   // 0 without split-K
+};
+
+AccPlan acc_plan(int64_t M, int64_t N, int64_t K) {
+  AccPlan p;
+  p.bn = narrow_bn(N);
+  p.pb = problem(M, N, K, 0, p.bn);
+  p.pb.splits = k_splits(static_cast<int64_t>(p.pb.num_m) * p.pb.num_n, p.pb.nk0,
+                         tc_host::sm_count());
+  p.ldw = (N + 3) / 4 * 4;
+  p.ws_floats = p.pb.splits > 1
+                    ? static_cast<int64_t>(p.pb.splits) * p.pb.num_m * tcg::BM * p.ldw : 0;
+  return p;
+}
+
+template <int A0, int B0, int BN>
+int run_acc(const CUtensorMap (&m)[4], const AccPlan& p, float* c, int64_t ldc, float alpha,
+            float* ws, cudaStream_t s, const char* what) {
+  const bool vec = qb::aligned16(c) && ldc % 4 == 0;
+  if (p.pb.splits <= 1) {
+    EpiAccF32 epi{c, ldc, p.pb.M, p.pb.N, alpha, vec};
+    return tcg::launch<A0, B0, tcg::kTmaK, tcg::kTmaK, BN>(m[0], m[1], m[2], m[3], p.pb, epi, s,
+                                                           what);
+  }
+  EpiPartialF32 epi{ws, p.ldw, p.pb.N};
+  if (int e = tcg::launch<A0, B0, tcg::kTmaK, tcg::kTmaK, BN>(m[0], m[1], m[2], m[3], p.pb, epi,
+                                                              s, what))
+    return e;
+  const bool rvec = vec && p.pb.N % 4 == 0;
+  const int64_t per_row = rvec ? p.pb.N / 4 : p.pb.N;
+  int64_t blocks = (static_cast<int64_t>(p.pb.M) * per_row + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(tc_host::sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  const int64_t split_stride = static_cast<int64_t>(p.pb.num_m) * tcg::BM * p.ldw;
+  if (rvec)
+    split_reduce_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        ws, p.ldw, split_stride, p.pb.splits, alpha, c, ldc, p.pb.M, p.pb.N);
+  else
+    split_reduce_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        ws, p.ldw, split_stride, p.pb.splits, alpha, c, ldc, p.pb.M, p.pb.N);
+  return qb::check_launch(what);
+}
+
+template <int A0, int B0>
+int run_acc_bn(const CUtensorMap (&m)[4], const AccPlan& p, float* c, int64_t ldc, float alpha,
+               float* ws, cudaStream_t s, const char* what) {
+  if (p.bn == 64) return run_acc<A0, B0, 64>(m, p, c, ldc, alpha, ws, s, what);
+  if (p.bn == 128) return run_acc<A0, B0, 128>(m, p, c, ldc, alpha, ws, s, what);
+  return run_acc<A0, B0, kBN>(m, p, c, ldc, alpha, ws, s, what);
+}
+
+}  // namespace
+
+extern "C" int64_t qb_gemm_bf16_acc_f32_workspace(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return 0;
+  return acc_plan(M, N, K).ws_floats;
+}
+
+extern "C" int qb_gemm_bf16_acc_f32(const void* A, int64_t lda, int a_mn_major, const void* B,
+                                    int64_t ldb, int b_mn_major, float alpha, float* C,
+                                    int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                    float* workspace, int64_t workspace_floats,
+                                    cudaStream_t stream) {
+  const char* what = "gemm_bf16_acc_f32";
+  if (int s = check_common(C, QB_F32, M, N, what)) return s;
+  if (K < 0 || K > (1 << 30)) return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
+  if (ldc < N) return qb::fail(QB_ERR_INVALID, "%s: output row stride", what);
+  if (M == 0 || N == 0 || K == 0) return QB_OK;     // adds nothing
+  if (!A || !B) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  const AccPlan plan = acc_plan(M, N, K);
+  if (plan.ws_floats > 0 &&
+      (!workspace || workspace_floats < plan.ws_floats || !qb::aligned16(workspace)))
+    return qb::fail(QB_ERR_INVALID, "%s: workspace of %lld floats (16-byte aligned) needed",
+                    what, static_cast<long long>(plan.ws_floats));
+  CUtensorMap m[4];
+  if (int s = map_operand(&m[0], A, lda, a_mn_major != 0, M, K, tcg::BM)) return s;
+  if (int s = map_operand(&m[1], B, ldb, b_mn_major != 0, N, K, plan.bn)) return s;
+  m[2] = m[0];
+  m[3] = m[1];
+  using namespace tcg;
+  if (!a_mn_major && !b_mn_major)
+    return run_acc_bn<kTmaK, kTmaK>(m, plan, C, ldc, alpha, workspace, stream, what);
+  if (!a_mn_major && b_mn_major)
+    return run_acc_bn<kTmaK, kTmaMN>(m, plan, C, ldc, alpha, workspace, stream, what);
+  if (a_mn_major && !b_mn_major)
+    return run_acc_bn<kTmaMN, kTmaK>(m, plan, C, ldc, alpha, workspace, stream, what);
+  return run_acc_bn<kTmaMN, kTmaMN>(m, plan, C, ldc, alpha, workspace, stream, what);
 }
 
 extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,

@@ -38,7 +38,21 @@ struct Problem {
   int M, N;
   int nk0, nk1;   // k-blocks of 64 in segment 0 / segment 1
   int num_m, num_n;
+  int splits;     // split-K: each tile's k-blocks in this many consecutive ranges (0 or 1: none)
 };
+
+// Work item `item` of a launch -> (tile, first k-block, end k-block): with split-K the items are
+// the tiles times the splits, split fastest, each a contiguous range of the tile's k-blocks (the
+// epilogue then stores its partial product, `split` x the padded M rows down).
+__device__ __forceinline__ void item_range(const Problem& pb, int item, int& tile, int& kb0,
+                                           int& kb1) {
+  const int splits = pb.splits > 1 ? pb.splits : 1;
+  const int nk = pb.nk0 + pb.nk1;
+  tile = item / splits;
+  const int sp = item - tile * splits;
+  kb0 = static_cast<int>(static_cast<int64_t>(nk) * sp / splits);
+  kb1 = static_cast<int>(static_cast<int64_t>(nk) * (sp + 1) / splits);
+}
 
 // Output tile `tile` -> (m-block, n-block) in the grouped order described above.
 __device__ __forceinline__ void tile_blocks(const Problem& pb, int tile, int& mb, int& nb) {
@@ -120,8 +134,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
   tc::fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_tiles = pb.num_m * pb.num_n;
-  const int nk = pb.nk0 + pb.nk1;
+  const int num_items = pb.num_m * pb.num_n * (pb.splits > 1 ? pb.splits : 1);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -129,11 +142,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       int stage = 0;
       uint32_t phase = 0;
       long issued = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !tc::failed(err); tile += gridDim.x) {
-        int mb, nb;
+      for (int item = blockIdx.x; item < num_items && !tc::failed(err); item += gridDim.x) {
+        int tile, kb0, kb1, mb, nb;
+        item_range(pb, item, tile, kb0, kb1);
         tile_blocks(pb, tile, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, err, 1)) break;
           uint8_t* sA = smem + stage * C::STAGE;
           uint8_t* sB = sA + C::A_BYTES;
@@ -177,13 +191,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !tc::failed(err); tile += gridDim.x, ++t) {
+      for (int item = blockIdx.x; item < num_items && !tc::failed(err); item += gridDim.x, ++t) {
+        int tile, kb0, kb1;
+        item_range(pb, item, tile, kb0, kb1);
         const int buf = t & 1;
         if (!tc::mbar_wait(&tempty[buf], ((t >> 1) & 1) ^ 1, err, 2)) break;
         tc::fence_after_sync();
         const uint32_t d = tmem_base + buf * C::BUF_COLS;
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           const bool seg1 = kb >= pb.nk0;
           const int asrc = seg1 ? A1 : A0, bsrc = seg1 ? B1 : B0;
           if (!tc::mbar_wait(&full[stage], phase, err, 3)) { ok = false; break; }
@@ -197,7 +213,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
                                            : tc::sdesc_sw128(sA + kk * 32, 16, 1024);
             const uint64_t b = is_mn(bsrc) ? tc::sdesc_sw128(sB + kk * 2048, 8192, 1024)
                                            : tc::sdesc_sw128(sB + kk * 32, 16, 1024);
-            tc::mma_bf16(d, a, b, idesc, (kb | kk) != 0);
+            tc::mma_bf16(d, a, b, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           tc::mma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -215,7 +231,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
     const int row = quarter * 32 + lane;
     int t = 0;
     // the loop condition and the break are warp-uniform: tcgen05.ld below is warp-collective
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+    for (int item = blockIdx.x; item < num_items; item += gridDim.x, ++t) {
+      int tile, kb0, kb1;
+      item_range(pb, item, tile, kb0, kb1);
       const int buf = t & 1;
       const bool ready = tc::mbar_wait(&tfull[buf], (t >> 1) & 1, err, 5);
       if (!__all_sync(0xffffffffu, ready)) break;
@@ -224,7 +242,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       tile_blocks(pb, tile, mb, nb);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::BUF_COLS;
-      epi.template tile<BN>(mb * BM, nb * BN, row, taddr);
+      // with split-K, split sp's partial tile lands sp x (padded M) rows further down: the
+      // epilogue of a split launch writes partial products that a reduction sums in split order
+      const int m_off = (item - tile * (pb.splits > 1 ? pb.splits : 1)) * pb.num_m * BM;
+      epi.template tile<BN>(mb * BM + m_off, nb * BN, row, taddr);
       tc::fence_before_sync();
       tc::mbar_arrive(&tempty[buf]);
     }
@@ -258,8 +279,10 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
     if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
     configured[dev] = true;
   }
-  const int tiles = pb.num_m * pb.num_n;
+  const int tiles = pb.num_m * pb.num_n * (pb.splits > 1 ? pb.splits : 1);
   if (tiles == 0) return QB_OK;
+  if (pb.splits > pb.nk0 + pb.nk1)
+    return qb::fail(QB_ERR_INVALID, "%s: more k-splits (%d) than k-blocks", what, pb.splits);
   int grid = tc_host::sm_count();
   if (grid > tiles) grid = tiles;
   if ((B0 == kTmaKDual && !mB0b) || (B1 == kTmaKDual && !mB1b))

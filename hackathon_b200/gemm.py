@@ -6,13 +6,22 @@ from . import _lib
 
 
 def _operand(t):
-    """(tensor, leading dim, mn_major) of a 2-D operand that is row-major or a transposed view."""
-    if t.stride(-1) == 1:
-        return t, t.stride(0), False
-    if t.stride(0) == 1:
-        return t, t.stride(1), True
-    t = t.contiguous()
-    return t, t.stride(0), False
+    """(tensor, leading dim, mn_major) of a 2-D operand that is row-major or a transposed view.
+    A tensor map needs a 16-byte aligned base and a leading dimension of whole 16-byte units (8
+    bf16): other operands are copied into a row-major buffer with padded rows. A single row may
+    take any leading dimension (only row 0 is read)."""
+    rows, cols = t.shape
+    if t.data_ptr() % 16 == 0:
+        if t.stride(-1) == 1 or cols == 1:
+            ld = t.stride(0) if rows > 1 else (cols + 7) // 8 * 8
+            if ld % 8 == 0 and ld >= cols:
+                return t, ld, False
+        if t.stride(0) == 1 and rows > 1 and t.stride(1) % 8 == 0 and t.stride(1) >= rows:
+            return t, t.stride(1), True
+    ld = (cols + 7) // 8 * 8
+    buf = torch.empty((rows, ld), dtype=t.dtype, device=t.device)[:, :cols]
+    buf.copy_(t)
+    return buf, ld, False
 
 
 def gemm(a, b_t, out=None, out_dtype=torch.bfloat16, bias=None):
@@ -37,6 +46,46 @@ def gemm(a, b_t, out=None, out_dtype=torch.bfloat16, bias=None):
               out.data_ptr(), out.stride(0), _lib.tag(out.dtype), _lib.ptr(bias), M, N, K,
               _lib.stream(a.device), work=(0, 2 * M * N * K))
     return out
+
+
+def gemm_acc_f32(a, b_t, out, alpha=1.0):
+    """out[M, N] (fp32, in place) += alpha * a[M, K] @ b_t[N, K].T on the tcgen05 GEMM, K split
+    across the SMs when the output has too few tiles (C-ABI qb_gemm_bf16_acc_f32; the partial
+    products meet in a workspace and are summed in a fixed order, so the result is the same on
+    every run): the skinny LoRA weight gradients, whose K is the token count. Operands bf16,
+    row-major or transposed views."""
+    _lib.require_cuda(a, b_t, out, what="gemm_acc_f32")
+    if a.dtype != torch.bfloat16 or b_t.dtype != torch.bfloat16 or out.dtype != torch.float32:
+        raise TypeError("gemm_acc_f32: bf16 operands, fp32 output")
+    M, K = a.shape
+    N, K2 = b_t.shape
+    if K != K2 or out.shape != (M, N) or out.stride(-1) != 1:
+        raise ValueError("gemm_acc_f32: shapes do not match")
+    a, lda, a_mn = _operand(a)
+    b_t, ldb, b_mn = _operand(b_t)
+    nws = int(_lib.load().qb_gemm_bf16_acc_f32_workspace(M, N, K)) if M and N and K else 0
+    ws = torch.empty(nws, dtype=torch.float32, device=a.device) if nws else None
+    _lib.call("qb_gemm_bf16_acc_f32", a.data_ptr(), lda, int(a_mn), b_t.data_ptr(), ldb,
+              int(b_mn), float(alpha), out.data_ptr(), out.stride(0), M, N, K, _lib.ptr(ws),
+              nws, _lib.stream(a.device), work=(0, 2 * M * N * K))
+    return out
+
+
+def lora_products(g, u, xd, b_scaled, a_shape, scaling, need_a=True, need_b=True):
+    """The LoRA branch's backward products for one projection, all on the tcgen05 GEMM:
+    V = g (s B) [T, r] (bf16; the input gradient's term), and when wanted dA = V^T xd [r, in]
+    and dB = s g^T U [out, r] (fp32, the tokens split across the SMs). g [T, out],
+    u = xd A^T [T, r], xd [T, in], b_scaled = s B [out, r], all bf16 (row-major, or column
+    slices of a wider buffer). Returns (V, dA or None, dB or None)."""
+    v = gemm(g, b_scaled.t())
+    da = db = None
+    if need_a:
+        da = torch.zeros(a_shape, dtype=torch.float32, device=g.device)
+        gemm_acc_f32(v.t(), xd.t(), da)
+    if need_b:
+        db = torch.zeros((g.shape[1], u.shape[1]), dtype=torch.float32, device=g.device)
+        gemm_acc_f32(g.t(), u.t(), db, alpha=scaling)
+    return v, da, db
 
 
 def gemm2(a0, b0_t, a1, b1_t, out=None, out_dtype=torch.bfloat16, bias=None, residual=None):

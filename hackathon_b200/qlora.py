@@ -178,7 +178,7 @@ class GateUpSwiGLU(torch.autograd.Function):
                                          stored only when a backward will read them)
         backward  dg, du = SwiGLU'(dh; g, u)
                   dx = dg W_g + du W_u  (+= s mask_* .* (V_* A_*))      V_* = d* (s B_*)
-                  dA_* = V_*^T xd_*, dB_* = s d*^T U_*
+                  dA_* = V_*^T xd_*, dB_* = s d*^T U_*   (tcgen05 GEMMs, split over the tokens)
     The recompute keeps the two rebuilt bf16 weights for the backward of the same layer."""
 
     @staticmethod
@@ -226,7 +226,7 @@ class GateUpSwiGLU(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dh):
         from . import _lib
-        from .gemm import gemm2, gemm_mask_acc
+        from .gemm import gemm2, gemm_mask_acc, lora_products
         from .nf4 import _weight_workspace, dequantize_nf4
         (xd_g, xd_u, u_g, u_u, a_g, b_g, a_u, b_u, bits_g, bits_u, w_g, w_u, g, u) = \
             ctx.saved_tensors
@@ -239,8 +239,11 @@ class GateUpSwiGLU(torch.autograd.Function):
                   du.data_ptr(), _lib.tag(g.dtype), g.numel(), _lib.stream(g.device),
                   work=(5 * g.numel() * g.element_size(), 0))
         a16_g, a16_u = a_g.to(g.dtype), a_u.to(g.dtype)
-        v_g = dg @ (b_g * gate.scaling).to(g.dtype)                    # [T, r]
-        v_u = du @ (b_u * up.scaling).to(g.dtype)
+        need = ctx.needs_input_grad
+        v_g, da_g, db_g = lora_products(dg, u_g, xd_g, (b_g * gate.scaling).to(g.dtype),
+                                        a_g.shape, gate.scaling, need[1], need[2])
+        v_u, da_u, db_u = lora_products(du, u_u, xd_u, (b_u * up.scaling).to(g.dtype),
+                                        a_u.shape, up.scaling, need[3], need[4])
         for mod, seed in zip((gate, up), ctx.seeds):
             MASKS.pop((id(mod), seed), None)
         dx = None
@@ -255,14 +258,9 @@ class GateUpSwiGLU(torch.autograd.Function):
             if p > 0:
                 gemm_mask_acc(v_g, a16_g.t(), bits_g, ctx.scale, dx)
                 gemm_mask_acc(v_u, a16_u.t(), bits_u, ctx.scale, dx)
-            else:
-                dx.addmm_(v_g, a16_g)
-                dx.addmm_(v_u, a16_u)
+            else:   # no mask: both adapter terms as one more tcgen05 GEMM over dx in place
+                gemm2(v_g, a16_g.t(), v_u, a16_u.t(), out=dx, residual=dx)
             dx = dx.view(ctx.shape)
-        da_g = (v_g.t() @ xd_g).float() if ctx.needs_input_grad[1] else None
-        db_g = (dg.t() @ u_g).float() * gate.scaling if ctx.needs_input_grad[2] else None
-        da_u = (v_u.t() @ xd_u).float() if ctx.needs_input_grad[3] else None
-        db_u = (du.t() @ u_u).float() * up.scaling if ctx.needs_input_grad[4] else None
         return dx, da_g, db_g, da_u, db_u, None, None, None, None, None, None
 
 
@@ -273,11 +271,12 @@ class LoRANF4Proj(torch.autograd.Function):
                   U  = xd A^T            (qb_lora_xa: from x and the bits in one tcgen05 kernel;
                                           xd itself is stored only when the backward reads it)
                   y  = h + x deq(W)^T + b + U (s B)^T                   (one tcgen05 GEMM)
-        backward  V  = g (s B)                                          (skinny GEMM)
+        backward  V  = g (s B)                                (skinny tcgen05 GEMM, 64-wide tiles)
                   dx = g deq(W)  [+= s mask .* (V A)]                   (tcgen05 GEMM, then the
                                                                          masked-accumulate GEMM;
                                                                          V A as extra K if p = 0)
-                  dA = V^T xd,  dB = s g^T U,  dh = g                   (fp32 adapter grads)
+                  dA = V^T xd,  dB = s g^T U,  dh = g   (fp32 adapter grads: tcgen05 GEMMs with the
+                                                         tokens split across the SMs)
     Under activation checkpointing the recompute keeps xd and, on the long-token path, the bf16
     weight it rebuilt, so the backward of the same layer neither replays the mask on x nor
     rebuilds W (both live only from the layer's recompute to its backward). output_dead: the
@@ -314,7 +313,7 @@ class LoRANF4Proj(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
-        from .gemm import gemm_mask_acc
+        from .gemm import gemm_mask_acc, lora_products
         from .nf4 import nf4_linear_dgrad
         xd, u, lora_a, lora_b, bits, w_keep = ctx.saved_tensors
         mod, p = ctx.mod, ctx.p
@@ -326,7 +325,8 @@ class LoRANF4Proj(torch.autograd.Function):
             g2 = rope_rows(g2, ctx.rope[0], ctx.rope[1], backward=True)
         a16 = lora_a.to(xd.dtype)
         sb16 = (lora_b * mod.scaling).to(xd.dtype)
-        v = g2 @ sb16                                              # [T, r]
+        v, da, db = lora_products(g2, u, xd, sb16, lora_a.shape, mod.scaling,
+                                  ctx.needs_input_grad[1], ctx.needs_input_grad[2])
         if p > 0:
             MASKS.pop((id(mod), ctx.seed), None)
         dx = None
@@ -339,8 +339,6 @@ class LoRANF4Proj(torch.autograd.Function):
         else:
             dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, v, a16, weight=w_keep)
             dx = dx.view(ctx.shape)
-        da = (v.t() @ xd).float() if ctx.needs_input_grad[1] else None
-        db = (g2.t() @ u).float() * mod.scaling if ctx.needs_input_grad[2] else None
         dres = g if ctx.has_residual and ctx.needs_input_grad[6] else None
         return dx, da, db, None, None, None, dres, None, None, None
 

@@ -353,6 +353,22 @@ int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight, int64
                       const float* lse, const float* scale_dev, void* dz, int64_t ldz,
                       cudaStream_t stream);
 
+/* Floats of workspace qb_gemm_bf16_acc_f32 needs for this shape on the current device (0: the
+ * launch runs unsplit and needs none). */
+int64_t qb_gemm_bf16_acc_f32_workspace(int64_t M, int64_t N, int64_t K);
+
+/* C[M,N] (fp32, row stride ldc) += alpha * A[M,K] * B[N,K]^T on the tcgen05 GEMM. When there are
+ * too few output tiles to fill the SMs the k-blocks are split into ranges: each range's partial
+ * product goes to `workspace` (at least qb_gemm_bf16_acc_f32_workspace floats, 16-byte aligned)
+ * and a second kernel adds alpha * their sum, taken in range order, into C - the same bits on
+ * every run. Operand layouts as qb_gemm_bf16. The LoRA weight gradients of lora.py:172
+ * (nn.Linear backward under autocast): dA = V^T xd and dB = s g^T U, skinny outputs whose K is
+ * the token count. */
+int qb_gemm_bf16_acc_f32(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
+                         int b_mn_major, float alpha, float* C, int64_t ldc, int64_t M,
+                         int64_t N, int64_t K, float* workspace, int64_t workspace_floats,
+                         cudaStream_t stream);
+
 /* Reads and clears this device's tensor-core error flag (synchronises `stream`): QB_OK, or
  * QB_ERR_TIMEOUT when a kernel gave up one of its bounded waits (its output is then invalid). */
 int qb_device_error(cudaStream_t stream);

@@ -35,6 +35,7 @@ class FakeEvent:
 
 class FakeCuda:
     Event = FakeEvent
+    nvtx = types.SimpleNamespace(range_push=lambda name: 0, range_pop=lambda: 0)
 
     @staticmethod
     def Stream(device=None):

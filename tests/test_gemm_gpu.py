@@ -68,12 +68,20 @@ def test_gemm_step_shapes(cuda, shape):
     torch.testing.assert_close(out[rows].float(), ref, rtol=1.6e-2, atol=2e-2)
 
 
-def test_gemm_rejects_misaligned_rows(cuda):
-    from hackathon_b200.gemm import gemm
+def test_gemm_misaligned_rows(cuda):
+    """Rows that are not whole 16-byte units: the C-ABI refuses them (a tensor map's row stride),
+    the Python wrapper copies such operands into padded rows and computes the product."""
+    from hackathon_b200 import _lib
+    from hackathon_b200.gemm import device_error, gemm
     a = torch.randn(64, 67, device=cuda).to(torch.bfloat16)   # 134-byte rows
     b = torch.randn(64, 67, device=cuda).to(torch.bfloat16)
+    c = torch.empty(64, 64, device=cuda, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="16"):
-        gemm(a, b)
+        _lib.call("qb_gemm_bf16", a.data_ptr(), 67, 0, b.data_ptr(), 67, 0, c.data_ptr(), 64,
+                  _lib.tag(c.dtype), None, 64, 64, 67, _lib.stream(a.device))
+    out = gemm(a, b)
+    device_error()
+    torch.testing.assert_close(out.float(), a.float() @ b.float().t(), rtol=1.6e-2, atol=2e-2)
 
 
 @pytest.mark.parametrize("b_t", [False, True])
@@ -205,3 +213,68 @@ def test_gemm2_residual_epilogue(cuda, lora):
     if lora:
         ref = ref + u.float() @ sb.float().t()
     torch.testing.assert_close(out.float(), ref, rtol=1.6e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("shape", [(3584, 64, 16384), (64, 3584, 16384), (512, 64, 16384),
+                                   (200, 100, 1000), (129, 130, 200), (1, 64, 64),
+                                   (300, 257, 4096)])
+def test_gemm_acc_f32_split_k(cuda, shape, a_t, b_t):
+    """C (fp32) += alpha A B^T with the tokens split across the SMs (the LoRA weight gradients:
+    [in, r] / [r, in] / [out, r] outputs, K = 16384), every orientation, ragged shapes and narrow
+    tiles, accumulating into a C that already holds values, against fp32 torch; a second run
+    gives the same bits (the splits are summed in a fixed order)."""
+    from hackathon_b200 import _lib
+    from hackathon_b200.gemm import device_error, gemm_acc_f32
+    M, N, K = shape
+    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    a = torch.randn(K, M, device=cuda, generator=g).to(torch.bfloat16).t() if a_t else \
+        torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    b = torch.randn(K, N, device=cuda, generator=g).to(torch.bfloat16).t() if b_t else \
+        torch.randn(N, K, device=cuda, generator=g).to(torch.bfloat16)
+    c0 = torch.randn(M, N, device=cuda, generator=g)
+    out = gemm_acc_f32(a, b, c0.clone(), alpha=0.5)
+    again = gemm_acc_f32(a, b, c0.clone(), alpha=0.5)
+    device_error()
+    ref = c0 + 0.5 * (a.float() @ b.float().t())
+    torch.testing.assert_close(out, ref, rtol=1e-3, atol=2e-3 * (K ** 0.5) / 8)
+    assert torch.equal(out, again)
+    if shape == (3584, 64, 16384):     # 28 tiles of a 256-k-block K: the split path ran
+        assert _lib.load().qb_gemm_bf16_acc_f32_workspace(M, N, K) > 0
+
+
+@pytest.mark.parametrize("shape", [(16384, 64, 3584), (16384, 64, 18944), (300, 64, 200),
+                                   (1000, 100, 96), (16384, 128, 512)])
+def test_gemm_narrow_tiles(cuda, shape):
+    """Outputs of at most 64 / 128 columns run 64- / 128-wide tiles (V = g (s B), U = xd A^T):
+    the same products as the 256-wide kernel, against fp32 torch."""
+    from hackathon_b200.gemm import device_error, gemm
+    M, N, K = shape
+    g = torch.Generator(device=cuda).manual_seed(N + K)
+    a = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    b = torch.randn(K, N, device=cuda, generator=g).to(torch.bfloat16)
+    out = gemm(a, b.t())                      # b.t(): the MN-major view the step passes
+    device_error()
+    _check(out, _ref(a, b.t()), torch.bfloat16)
+
+
+def test_lora_products_match_torch(cuda):
+    """The LoRA branch's backward products of one projection (V, dA, dB) on the tcgen05 GEMMs
+    against the fp32 torch products, at the 7B o-projection shape (T = 16384, r = 64)."""
+    from hackathon_b200.gemm import device_error, lora_products
+    T, out_f, in_f, r, s = 16384, 3584, 3584, 64, 2.0
+    g = torch.Generator(device=cuda).manual_seed(7)
+    gy = torch.randn(T, out_f, device=cuda, generator=g).to(torch.bfloat16)
+    u = torch.randn(T, 2 * r, device=cuda, generator=g).to(torch.bfloat16)[:, r:]   # a slice
+    xd = torch.randn(T, in_f, device=cuda, generator=g).to(torch.bfloat16)
+    sb = (torch.randn(out_f, r, device=cuda, generator=g) * 0.05).to(torch.bfloat16)
+    v, da, db = lora_products(gy, u, xd, sb, (r, in_f), s)
+    device_error()
+    v_ref = gy.float() @ sb.float()
+    torch.testing.assert_close(v.float(), v_ref, rtol=1.6e-2, atol=5e-2)
+    da_ref = v.float().t() @ xd.float()
+    db_ref = s * (gy.float().t() @ u.float())
+    for got, want in ((da, da_ref), (db, db_ref)):
+        assert got.dtype == torch.float32 and got.is_contiguous()
+        assert float((got - want).norm() / want.norm()) < 1e-3
