@@ -343,6 +343,7 @@ def kernel_case(args):
     fused linear cross-entropy (forward + dH) with hidden size --in-features and vocabulary
     --out-features. --graph replays the --steps launches from one CUDA graph (bandwidth kernels
     too short to time behind Python launch gaps)."""
+    from hackathon_b200 import _lib
     from hackathon_b200 import nf4 as nf4m
     from hackathon_b200.gemm import device_error, gemm, gemm2
     from hackathon_b200.lora import dropout_apply, dropout_mask
@@ -517,6 +518,12 @@ def kernel_case(args):
         line.update(achieved=round(gbs, 1), unit="GB/s", peak=pk["hbm_gbs"],
                     frac=round(gbs / pk["hbm_gbs"], 3), bytes_per_launch=nbytes)
     line["peak_source"] = pk["source"] + " (burst)"
+    if not args.graph:
+        # one more launch with events around every C-ABI call: where the op's time goes
+        with _lib.KernelTimer() as kt:
+            fn()
+        line["calls"] = {k: {"launches": v["launches"], "ms": round(v["ms_total"], 4)}
+                         for k, v in kt.summary().items()}
     print(json.dumps(line), flush=True)
 
 
@@ -533,6 +540,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="print every kernel of one step with its device time (torch.profiler)")
+    ap.add_argument("--capture-step", action="store_true",
+                    help="after the warm-up, run one step between cudaProfilerStart/Stop and exit "
+                         "(for ncu --profile-from-start off)")
     ap.add_argument("--step-deadline", type=float, default=STEP_DEADLINE_S,
                     help="seconds a step may take before the watchdog ends the run (raise it "
                          "under a profiler, which serialises every launch)")
@@ -618,6 +628,21 @@ def main():
             _phase(f"warm-up step {i} done")
     except RunFailed as e:
         fail(args, world, str(e), monitor_report(lib, local))
+        return
+
+    if args.capture_step:
+        # one step between cudaProfilerStart / Stop, every thread's launches included (the
+        # autograd engine launches the backward from its own thread): the range that
+        # `ncu --profile-from-start off` captures for the launch list
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        run_checked(dog.watched("captured step", args.step_deadline, lambda: synced_step(0)),
+                    device_error, "captured step")
+        torch.cuda.profiler.stop()
+        if rank == 0:
+            print(json.dumps({"captured_step": workload}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
 
     if args.profile_step:

@@ -52,8 +52,8 @@ _SIGNATURES = {
     "qb_device_error": [_p],
     "qb_monitor_report": [_i32, ctypes.c_char_p, _i64],
     "qb_gemm_bf16": [_p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p],
-    "qb_gemm_bf16_acc_f32": [_p, _i64, _i32, _p, _i64, _i32, _f32, _p, _i64, _i64, _i64, _i64,
-                             _p, _i64, _p],
+    "qb_gemm_bf16_acc_f32": [_p, _i64, _i32, _p, _i64, _i32, _f32, _f32, _p, _i64, _i64, _i64,
+                             _i64, _p, _i64, _p],
     "qb_gemm_bf16_acc_f32_workspace": [_i64, _i64, _i64],
     "qb_gemm2_bf16": [_p, _i64, _i32, _p, _i64, _i32, _i64, _p, _i64, _i32, _p, _i64, _i32, _i64,
                       _p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p],
@@ -74,11 +74,14 @@ _SIGNATURES = {
     "qb_ce_grad_from_logits": [_p, _i64, _p, _i64, _i64, _p, _p, _p, _i64, _p],
     "qb_ce_reduce": [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p],
     "qb_linear_ce_grad": [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p],
+    "qb_pack_segment_size": [],
+    "qb_adapter_pack": [_p, _i32, _i64, _p],
 }
 _RESTYPE = {"qb_last_error": ctypes.c_char_p, "qb_nf4_double_quant_workspace": ctypes.c_int64,
             "qb_nf4_double_quant_noalloc_max_blocks": ctypes.c_int64,
             "qb_linear_ce_vocab_tiles": ctypes.c_int64,
-            "qb_gemm_bf16_acc_f32_workspace": ctypes.c_int64}
+            "qb_gemm_bf16_acc_f32_workspace": ctypes.c_int64,
+            "qb_pack_segment_size": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib = None

@@ -21,7 +21,8 @@ IGNORE_INDEX = -100
 CHUNK_ROWS = 4096           # rows per chunk of materialised logits (the matmul fallback)
 # Rows per chunk on the tcgen05 path, where only dZ (bf16) is materialised: 16384 x 152064 is
 # 5 GB, and the dH GEMM's 1792 output tiles of a 16384-row chunk fill 12.1 waves of the 148 SMs
-# (a 4096-row chunk's 448 tiles: 3.03 waves, the last one nearly empty).
+# (a 4096-row chunk's 448 tiles: 3.03 waves, the last one nearly empty). Splitting dH's K (the
+# vocabulary) to even out the last wave measured slower: the partial tiles' traffic costs more.
 TC_CHUNK_ROWS = 16384
 # Off the bf16 path dZ = softmax - onehot is stored in the matmul dtype before the dH matmul. In
 # fp16 it is multiplied by GRAD_GAIN (a power of two, exact) so probabilities below fp16's

@@ -1,7 +1,8 @@
 // Plain bf16 GEMMs on the tcgen05 kernel, fp32 accumulation, fp32 or bf16 output:
 //   qb_gemm_bf16    C[M,N] = A[M,K] * B[N,K]^T (+ bias[N])
 //   qb_gemm2_bf16   C[M,N] = A0[M,K0] * B0[N,K0]^T + A1[M,K1] * B1[N,K1]^T (+ bias[N])
-//   qb_gemm_bf16_acc_f32   C[M,N] (fp32) += alpha * A[M,K] * B[N,K]^T, K split over the SMs
+//   qb_gemm_bf16_acc_f32   C[M,N] (fp32) = beta * C + alpha * A[M,K] * B[N,K]^T (beta 0 or 1),
+//                          K split over the SMs
 //                          (partials in a workspace, summed in a fixed order: deterministic)
 // Each operand may be K-major or MN-major in HBM (qb_gemm_bf16: every orientation the suite
 // needs — logits = H W^T, dH = dZ W, LoRA products; qb_gemm2_bf16: the two layouts of a
@@ -63,14 +64,15 @@ struct EpiStoreRow {
   }
 };
 
-// C += alpha * the tile, fp32 (C += alpha A B^T in one work item per tile): each element is
+// C = (accumulate ? C : 0) + alpha * the tile, fp32 (one work item per tile): each element is
 // read and written by the one thread that owns its row.
 struct EpiAccF32 {
   float* c;
   int64_t ldc;
   int M, N;
   float alpha;
-  bool vec;   // 16-byte aligned rows
+  bool vec;          // 16-byte aligned rows
+  bool accumulate;   // false: C is written without being read
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -85,7 +87,8 @@ struct EpiAccF32 {
       if (vec && n + 32 <= N) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          float4 o = *reinterpret_cast<const float4*>(dst + i);
+          float4 o = accumulate ? *reinterpret_cast<const float4*>(dst + i)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
           o.x += alpha * v[i];
           o.y += alpha * v[i + 1];
           o.z += alpha * v[i + 2];
@@ -95,7 +98,7 @@ struct EpiAccF32 {
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (n + i < N) dst[i] += alpha * v[i];
+          if (n + i < N) dst[i] = (accumulate ? dst[i] : 0.f) + alpha * v[i];
       }
     }
   }
@@ -132,10 +135,11 @@ struct EpiPartialF32 {
   }
 };
 
-// C[m, n] += alpha * (((P_0 + P_1) + P_2) + ...) over the splits' partials P_s (rows s x Mp of
-// the workspace): a fixed summation order, so a split launch gives the same bits every time.
-// VEC: four columns per thread (N, ldc and ldw multiples of 4, C 16-byte aligned).
-template <bool VEC>
+// C[m, n] = (ACC ? C[m, n] : 0) + alpha * (((P_0 + P_1) + P_2) + ...) over the splits'
+// partials P_s (rows s x Mp of the workspace): a fixed summation order, so a split launch gives
+// the same bits every time. VEC: four columns per thread (N, ldc and ldw multiples of 4, C
+// 16-byte aligned).
+template <bool VEC, bool ACC>
 __global__ void __launch_bounds__(256)
 split_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int64_t split_stride, int splits,
                     float alpha, float* __restrict__ c, int64_t ldc, int M, int N) {
@@ -156,7 +160,7 @@ split_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int64_t split_str
         acc.z += q.z;
         acc.w += q.w;
       }
-      float4 o = *reinterpret_cast<const float4*>(dst);
+      float4 o = ACC ? *reinterpret_cast<const float4*>(dst) : make_float4(0.f, 0.f, 0.f, 0.f);
       o.x += alpha * acc.x;
       o.y += alpha * acc.y;
       o.z += alpha * acc.z;
@@ -165,7 +169,7 @@ split_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int64_t split_str
     } else {
       float acc = __ldg(p);
       for (int sp = 1; sp < splits; ++sp) acc += __ldg(p + sp * split_stride);
-      *dst += alpha * acc;
+      *dst = (ACC ? *dst : 0.f) + alpha * acc;
     }
   }
 }
@@ -507,12 +511,24 @@ AccPlan acc_plan(int64_t M, int64_t N, int64_t K) {
   return p;
 }
 
+template <bool VEC>
+void launch_reduce(const AccPlan& p, float* ws, float alpha, bool acc, float* c, int64_t ldc,
+                   unsigned blocks, cudaStream_t s) {
+  const int64_t split_stride = static_cast<int64_t>(p.pb.num_m) * tcg::BM * p.ldw;
+  if (acc)
+    split_reduce_kernel<VEC, true><<<blocks, 256, 0, s>>>(ws, p.ldw, split_stride, p.pb.splits,
+                                                          alpha, c, ldc, p.pb.M, p.pb.N);
+  else
+    split_reduce_kernel<VEC, false><<<blocks, 256, 0, s>>>(ws, p.ldw, split_stride, p.pb.splits,
+                                                           alpha, c, ldc, p.pb.M, p.pb.N);
+}
+
 template <int A0, int B0, int BN>
 int run_acc(const CUtensorMap (&m)[4], const AccPlan& p, float* c, int64_t ldc, float alpha,
-            float* ws, cudaStream_t s, const char* what) {
+            bool acc, float* ws, cudaStream_t s, const char* what) {
   const bool vec = qb::aligned16(c) && ldc % 4 == 0;
   if (p.pb.splits <= 1) {
-    EpiAccF32 epi{c, ldc, p.pb.M, p.pb.N, alpha, vec};
+    EpiAccF32 epi{c, ldc, p.pb.M, p.pb.N, alpha, vec, acc};
     return tcg::launch<A0, B0, tcg::kTmaK, tcg::kTmaK, BN>(m[0], m[1], m[2], m[3], p.pb, epi, s,
                                                            what);
   }
@@ -525,22 +541,19 @@ int run_acc(const CUtensorMap (&m)[4], const AccPlan& p, float* c, int64_t ldc, 
   int64_t blocks = (static_cast<int64_t>(p.pb.M) * per_row + 255) / 256;
   const int64_t cap = static_cast<int64_t>(tc_host::sm_count()) * 8;
   if (blocks > cap) blocks = cap;
-  const int64_t split_stride = static_cast<int64_t>(p.pb.num_m) * tcg::BM * p.ldw;
   if (rvec)
-    split_reduce_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        ws, p.ldw, split_stride, p.pb.splits, alpha, c, ldc, p.pb.M, p.pb.N);
+    launch_reduce<true>(p, ws, alpha, acc, c, ldc, static_cast<unsigned>(blocks), s);
   else
-    split_reduce_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-        ws, p.ldw, split_stride, p.pb.splits, alpha, c, ldc, p.pb.M, p.pb.N);
+    launch_reduce<false>(p, ws, alpha, acc, c, ldc, static_cast<unsigned>(blocks), s);
   return qb::check_launch(what);
 }
 
 template <int A0, int B0>
 int run_acc_bn(const CUtensorMap (&m)[4], const AccPlan& p, float* c, int64_t ldc, float alpha,
-               float* ws, cudaStream_t s, const char* what) {
-  if (p.bn == 64) return run_acc<A0, B0, 64>(m, p, c, ldc, alpha, ws, s, what);
-  if (p.bn == 128) return run_acc<A0, B0, 128>(m, p, c, ldc, alpha, ws, s, what);
-  return run_acc<A0, B0, kBN>(m, p, c, ldc, alpha, ws, s, what);
+               bool acc, float* ws, cudaStream_t s, const char* what) {
+  if (p.bn == 64) return run_acc<A0, B0, 64>(m, p, c, ldc, alpha, acc, ws, s, what);
+  if (p.bn == 128) return run_acc<A0, B0, 128>(m, p, c, ldc, alpha, acc, ws, s, what);
+  return run_acc<A0, B0, kBN>(m, p, c, ldc, alpha, acc, ws, s, what);
 }
 
 }  // namespace
@@ -551,15 +564,23 @@ extern "C" int64_t qb_gemm_bf16_acc_f32_workspace(int64_t M, int64_t N, int64_t 
 }
 
 extern "C" int qb_gemm_bf16_acc_f32(const void* A, int64_t lda, int a_mn_major, const void* B,
-                                    int64_t ldb, int b_mn_major, float alpha, float* C,
-                                    int64_t ldc, int64_t M, int64_t N, int64_t K,
+                                    int64_t ldb, int b_mn_major, float alpha, float beta,
+                                    float* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
                                     float* workspace, int64_t workspace_floats,
                                     cudaStream_t stream) {
   const char* what = "gemm_bf16_acc_f32";
   if (int s = check_common(C, QB_F32, M, N, what)) return s;
   if (K < 0 || K > (1 << 30)) return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
   if (ldc < N) return qb::fail(QB_ERR_INVALID, "%s: output row stride", what);
-  if (M == 0 || N == 0 || K == 0) return QB_OK;     // adds nothing
+  if (beta != 0.0f && beta != 1.0f) return qb::fail(QB_ERR_INVALID, "%s: beta is 0 or 1", what);
+  if (M == 0 || N == 0) return QB_OK;
+  if (K == 0) {   // C = beta * C: nothing to add; beta 0 clears C
+    if (beta != 0.0f) return QB_OK;
+    const cudaError_t e = cudaMemset2DAsync(C, ldc * sizeof(float), 0, N * sizeof(float), M,
+                                            stream);
+    if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return QB_OK;
+  }
   if (!A || !B) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
   const AccPlan plan = acc_plan(M, N, K);
   if (plan.ws_floats > 0 &&
@@ -572,13 +593,14 @@ extern "C" int qb_gemm_bf16_acc_f32(const void* A, int64_t lda, int a_mn_major, 
   m[2] = m[0];
   m[3] = m[1];
   using namespace tcg;
+  const bool acc = beta != 0.0f;
   if (!a_mn_major && !b_mn_major)
-    return run_acc_bn<kTmaK, kTmaK>(m, plan, C, ldc, alpha, workspace, stream, what);
+    return run_acc_bn<kTmaK, kTmaK>(m, plan, C, ldc, alpha, acc, workspace, stream, what);
   if (!a_mn_major && b_mn_major)
-    return run_acc_bn<kTmaK, kTmaMN>(m, plan, C, ldc, alpha, workspace, stream, what);
+    return run_acc_bn<kTmaK, kTmaMN>(m, plan, C, ldc, alpha, acc, workspace, stream, what);
   if (a_mn_major && !b_mn_major)
-    return run_acc_bn<kTmaMN, kTmaK>(m, plan, C, ldc, alpha, workspace, stream, what);
-  return run_acc_bn<kTmaMN, kTmaMN>(m, plan, C, ldc, alpha, workspace, stream, what);
+    return run_acc_bn<kTmaMN, kTmaK>(m, plan, C, ldc, alpha, acc, workspace, stream, what);
+  return run_acc_bn<kTmaMN, kTmaMN>(m, plan, C, ldc, alpha, acc, workspace, stream, what);
 }
 
 extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, const void* B0,

@@ -374,3 +374,51 @@ extern "C" int qb_scaled_add(const void* base, int base_dtype, int64_t base_row_
   });
   return qb::check_launch("scaled_add");
 }
+
+// ------------------------------------------------------------------------------ adapter pack
+
+namespace {
+
+constexpr int kPackChunk = 2048;   // elements per CTA: 256 threads x 8
+
+__global__ void __launch_bounds__(kThreads)
+adapter_pack_kernel(const qb_pack_segment* __restrict__ segs, int nseg) {
+  __shared__ int s_seg;
+  if (threadIdx.x == 0) {   // the last segment whose first chunk is <= this CTA's chunk
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) / 2;
+      if (segs[mid].first_chunk <= static_cast<int64_t>(blockIdx.x)) lo = mid;
+      else hi = mid - 1;
+    }
+    s_seg = lo;
+  }
+  __syncthreads();
+  const qb_pack_segment sg = segs[s_seg];
+  const int64_t n = static_cast<int64_t>(sg.rows) * sg.cols;
+  const int64_t e0 = (static_cast<int64_t>(blockIdx.x) - sg.first_chunk) * kPackChunk +
+                     threadIdx.x * 8;
+  auto* dst = static_cast<__nv_bfloat16*>(sg.dst);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t e = e0 + j;
+    if (e >= n) break;
+    const int64_t row = e / sg.cols, col = e - row * sg.cols;
+    dst[row * sg.dst_ld + col] = __float2bfloat16_rn(__fmul_rn(sg.src[row * sg.src_ld + col],
+                                                               sg.scale));
+  }
+}
+
+}  // namespace
+
+extern "C" int64_t qb_pack_segment_size(void) { return sizeof(qb_pack_segment); }
+
+extern "C" int qb_adapter_pack(const qb_pack_segment* segs, int nseg, int64_t total_chunks,
+                               cudaStream_t stream) {
+  if (nseg < 0 || total_chunks < 0 || total_chunks > 0x7fffffff)
+    return qb::fail(QB_ERR_INVALID, "adapter_pack: bad sizes");
+  if (nseg == 0 || total_chunks == 0) return QB_OK;
+  if (!segs) return qb::fail(QB_ERR_INVALID, "adapter_pack: null segment table");
+  adapter_pack_kernel<<<static_cast<unsigned>(total_chunks), kThreads, 0, stream>>>(segs, nseg);
+  return qb::check_launch("adapter_pack");
+}

@@ -10,6 +10,9 @@
 // product from TMEM, apply mask and scale to the row in shared memory — with the swizzle, a warp's
 // 16-byte row accesses hit 32 distinct banks per 8 lanes — and one thread TMA-stores the tile.
 // Global traffic is dx read once and written once (coalesced by TMA) plus the mask words.
+// Tiles are 128 x 128 (32 KiB of dx) in a ring of four buffers, so the producer keeps up to three
+// tiles of loads in flight ahead of the epilogue; the storing thread does not wait for its own
+// store: it hands a buffer back once the store issued after it has been read out.
 //
 // Roles (one CTA per SM, persistent over tiles): warp 0 TMA loads (operands, dx tiles),
 // warp 1 TMEM allocation + MMA issue, warps 2-5 epilogue (thread 64 also issues the stores).
@@ -20,14 +23,16 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int BM = 128, BN = 128, BK = 64;
 constexpr int kStages = 2;
 constexpr int kA = BM * 128;          // 16 KiB: V tile, 128 rows x 64 k
-constexpr int kB = BN * 128;          // 32 KiB: B tile, 256 n x 64 k
+constexpr int kB = BN * 128;          // 16 KiB: B tile, 128 n x 64 k
 constexpr int kSlab = BM * 128;       // 16 KiB: 128 rows x 64 columns of dx
-constexpr int kC = 4 * kSlab;         // 64 KiB: one dx tile
+constexpr int kSlabs = BN / 64;
+constexpr int kC = kSlabs * kSlab;    // 32 KiB: one dx tile
+constexpr int kCBufs = 4;             // dx tiles in the ring
 constexpr int kThreads = 192;
-constexpr int kSmem = kStages * (kA + kB) + 2 * kC + 1024 /*barriers*/ + 1024 /*align*/;
+constexpr int kSmem = kStages * (kA + kB) + kCBufs * kC + 1024 /*barriers*/ + 1024 /*align*/;
 
 struct Problem {
   int M, N, nk, num_m, num_n;
@@ -48,14 +53,14 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* ringAB = smem;                           // kStages x (A | B)
-  uint8_t* cbuf = ringAB + kStages * (kA + kB);     // 2 x dx tile
-  uint64_t* bar = reinterpret_cast<uint64_t*>(cbuf + 2 * kC);
+  uint8_t* cbuf = ringAB + kStages * (kA + kB);     // kCBufs x dx tile
+  uint64_t* bar = reinterpret_cast<uint64_t*>(cbuf + kCBufs * kC);
   uint64_t* full = bar;               // [kStages] operands landed
   uint64_t* empty = full + kStages;   // [kStages] MMAs done with the stage
-  uint64_t* cfull = empty + kStages;  // [2] dx tile landed
-  uint64_t* cdone = cfull + 2;        // [2] the 128 epilogue threads rewrote the tile
-  uint64_t* cempty = cdone + 2;       // [2] the store has read the tile out
-  uint64_t* tfull = cempty + 2;       // [2] accumulator ready
+  uint64_t* cfull = empty + kStages;  // [kCBufs] dx tile landed
+  uint64_t* cdone = cfull + kCBufs;   // [kCBufs] the 128 epilogue threads rewrote the tile
+  uint64_t* cempty = cdone + kCBufs;  // [kCBufs] the store has read the tile out
+  uint64_t* tfull = cempty + kCBufs;  // [2] accumulator ready
   uint64_t* tempty = tfull + 2;       // [2] accumulator drained
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -63,10 +68,12 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kCBufs; ++b) {
       tc::mbar_init(&cfull[b], 1);
       tc::mbar_init(&cdone[b], 128);
       tc::mbar_init(&cempty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
       tc::mbar_init(&tempty[b], 128);
     }
@@ -97,11 +104,11 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
       int i = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !tc::failed(err); tile += gridDim.x, ++i) {
         const int m0 = (tile % pb.num_m) * BM, n0 = (tile / pb.num_m) * BN;
-        const int cb = i & 1;
-        if (!tc::mbar_wait(&cempty[cb], ((i >> 1) & 1) ^ 1, err, 41)) break;
+        const int cb = i % kCBufs;
+        if (!tc::mbar_wait(&cempty[cb], ((i / kCBufs) & 1) ^ 1, err, 41)) break;
         tc::mbar_expect_tx(&cfull[cb], kC);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
+        for (int j = 0; j < kSlabs; ++j)
           tc::tma_load_2d(cbuf + cb * kC + j * kSlab, &mC, &cfull[cb], n0 + 64 * j, m0);
         ++c_issued;
         bool ok = true;
@@ -128,8 +135,8 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
           if (--s < 0) { s = kStages - 1; ph ^= 1; }
           tc::mbar_wait_quiet(&full[s], ph);
         }
-        for (long k = c_issued - 1; k >= 0 && k >= c_issued - 2; --k)
-          tc::mbar_wait_quiet(&cfull[k & 1], (k >> 1) & 1);
+        for (long k = c_issued - 1; k >= 0 && k >= c_issued - kCBufs; --k)
+          tc::mbar_wait_quiet(&cfull[k % kCBufs], (k / kCBufs) & 1);
       }
     }
   } else if (warp == 1) {
@@ -174,24 +181,22 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
     int i = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
       const int m0 = (tile % pb.num_m) * BM, n0 = (tile / pb.num_m) * BN;
-      const int buf = i & 1, cb = i & 1;
-      const uint32_t par = (i >> 1) & 1;
-      // the row's 8 mask words, fetched before the waits (they depend on nothing in flight)
+      const int buf = i & 1, cb = i % kCBufs;
+      const uint32_t par = (i >> 1) & 1, cpar = (i / kCBufs) & 1;
+      // the row's 4 mask words, fetched before the waits (they depend on nothing in flight)
       const int m = m0 + row;
-      uint32_t words[8];
+      uint32_t words[BN / 32];
       const int64_t w0 = static_cast<int64_t>(m) * pb.ldbits + (n0 >> 5);
-      if (m < pb.M && pb.bits_vec && (n0 >> 5) + 8 <= pb.ldbits) {
-        const uint4 lo = __ldg(reinterpret_cast<const uint4*>(bits + w0));
-        const uint4 hi = __ldg(reinterpret_cast<const uint4*>(bits + w0 + 4));
-        words[0] = lo.x; words[1] = lo.y; words[2] = lo.z; words[3] = lo.w;
-        words[4] = hi.x; words[5] = hi.y; words[6] = hi.z; words[7] = hi.w;
+      if (m < pb.M && pb.bits_vec && (n0 >> 5) + 4 <= pb.ldbits) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(bits + w0));
+        words[0] = q.x; words[1] = q.y; words[2] = q.z; words[3] = q.w;
       } else {
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
+        for (int c = 0; c < BN / 32; ++c)
           words[c] = (m < pb.M && (n0 >> 5) + c < pb.ldbits) ? __ldg(bits + w0 + c) : 0u;
       }
       const bool ready = tc::mbar_wait(&tfull[buf], par, err, 45) &&
-                         tc::mbar_wait(&cfull[cb], par, err, 46);
+                         tc::mbar_wait(&cfull[cb], cpar, err, 46);
       if (!__all_sync(0xffffffffu, ready)) break;   // warp-uniform: tcgen05.ld is collective
       tc::fence_after_sync();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
@@ -227,15 +232,18 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
       if (warp == 2) {   // the storer's outcome is made warp-uniform before the next tile
         bool stored = true;
         if (storer) {
-          stored = tc::mbar_wait(&cdone[cb], par, err, 47);
+          stored = tc::mbar_wait(&cdone[cb], cpar, err, 47);
           if (stored) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < kSlabs; ++j)
               if (n0 + 64 * j < pb.N)
                 tc::tma_store_2d(&mC, cbuf + cb * kC + j * kSlab, n0 + 64 * j, m0);
             tc::bulk_commit();
-            tc::bulk_wait_read_all();
-            tc::mbar_arrive(&cempty[cb]);
+            // the store before this one has read its buffer out: hand that buffer back
+            if (i > 0) {
+              tc::bulk_wait_read_newest_pending();
+              tc::mbar_arrive(&cempty[(i - 1) % kCBufs]);
+            }
           }
         }
         if (!__shfl_sync(0xffffffffu, stored, 0)) break;

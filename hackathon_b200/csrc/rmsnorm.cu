@@ -1,18 +1,86 @@
-// RMSNorm forward/backward (Qwen2RMSNorm with a frozen weight), one CTA per row.
+// RMSNorm forward/backward (Qwen2RMSNorm with a frozen weight).
 //
 // Forward (solution/rmsnorm.py:25-39): rstd = 1/sqrt(sum(x^2)/N + eps); xn = x*rstd rounded
 // through x's dtype; y = w*xn in the promoted output dtype. Backward (:43-55):
 // g = dy*w, dx = rstd*(g - x*(rstd^2 * sum(g*x)/N)).
 //
-// Each thread owns VPT chunks of 8 contiguous elements (16-byte loads for 2-byte dtypes), kept
-// in registers between the reduction and the write, so x is read from HBM once per pass. Rows
-// whose length or alignment rules out 8-wide chunks take the scalar kernel, which re-reads the
-// row from L2 in its second loop.
+// Forward rows of up to 32 x 16 x 8 = 4096 elements whose rows allow 16-byte accesses take the
+// warp-per-row kernel: a warp issues every 16-byte load of its row before it reduces, keeps the
+// raw bytes in registers (not floats: half the registers for 2-byte dtypes), reduces with
+// shuffles only (no block barrier), and writes the row from the registers - HBM is read once,
+// with up to 16 loads in flight per lane. Longer rows, and the backward, take the CTA-per-row
+// kernels (VPT 16-byte chunks per thread, a block reduction): in the backward, which holds dy and
+// x, a warp-per-row form needs twice the registers and streams slower than the CTA-per-row one.
+// Rows whose length or alignment rules out 16-byte chunks take the scalar kernel, which re-reads
+// the row from L2 in its second loop.
 #include "qb_common.cuh"
 
 namespace {
 
 constexpr int kMaxThreads = 512;
+
+// Eight elements of T as raw bytes (one or two 16-byte words) and their float values.
+template <typename T>
+struct Chunk8 {
+  static constexpr int W = sizeof(T) * 8 / 16;   // 16-byte words: 1 for 2-byte T, 2 for fp32
+  uint4 u[W];
+  __device__ __forceinline__ void load(const T* p) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) u[i] = __ldg(reinterpret_cast<const uint4*>(p) + i);
+  }
+  __device__ __forceinline__ void to_float(float* f) const {
+    const T* v = reinterpret_cast<const T*>(u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = qb::to_f(v[e]);
+  }
+};
+
+constexpr int kRowWarps = 8;      // rows (warps) per CTA of the warp-per-row kernels
+constexpr int kWarpRowMax = 32 * 16 * 8;   // longest row the warp kernels take (CPL <= 16)
+
+// One warp per row; CPL 8-element chunks per lane at most (chunk c of the row is lane c % 32's
+// (c / 32)-th), row length a multiple of 8 and <= 256 * CPL.
+template <typename XT, typename WT, typename YT, int CPL>
+__global__ void __launch_bounds__(kRowWarps * 32)
+rmsnorm_fwd_warp(const XT* __restrict__ x, int64_t xs, const WT* __restrict__ w,
+                 YT* __restrict__ y, int64_t ys, float* __restrict__ rstd, int64_t rows,
+                 int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;                       // whole warps leave: no barrier follows
+  const int nvec = cols / 8;
+  const XT* xr = x + row * xs;
+  Chunk8<XT> c[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j)
+    if (lane + 32 * j < nvec) c[j].load(xr + (lane + 32 * j) * 8);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    if (lane + 32 * j < nvec) {
+      float f[8];
+      c[j].to_float(f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+    }
+  }
+  ss = qb::warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+  if (lane == 0) rstd[row] = r;
+  YT* yr = y + row * ys;
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int idx = lane + 32 * j;
+    if (idx < nvec) {
+      float f[8], wv[8], out[8];
+      c[j].to_float(f);
+      qb::load8<WT>(w + idx * 8, wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) out[e] = wv[e] * qb::round_through<XT>(f[e] * r);
+      qb::store8<YT>(yr + idx * 8, out);
+    }
+  }
+}
 
 template <typename XT, typename WT, typename YT, int VPT>
 __global__ void __launch_bounds__(kMaxThreads)
@@ -163,12 +231,24 @@ int fwd_typed(const void* x, int64_t xs, const void* w, void* y, int64_t ys, flo
               int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
   const bool vec_ok = rows_aligned(x, xs, sizeof(XT)) && rows_aligned(y, ys, sizeof(YT)) &&
                       qb::aligned16(w);
-  const RowPlan p = plan_row(cols, vec_ok);
   const auto* xp = static_cast<const XT*>(x);
   const auto* wp = static_cast<const WT*>(w);
   auto* yp = static_cast<YT*>(y);
-  const dim3 grid(static_cast<unsigned>(rows));
   const int c = static_cast<int>(cols);
+  if constexpr (sizeof(XT) == 2) {
+    if (vec_ok && cols % 8 == 0 && cols <= kWarpRowMax) {
+      const dim3 wgrid(static_cast<unsigned>((rows + kRowWarps - 1) / kRowWarps));
+      if (cols <= 1024)
+        rmsnorm_fwd_warp<XT, WT, YT, 4><<<wgrid, kRowWarps * 32, 0, stream>>>(
+            xp, xs, wp, yp, ys, rstd, rows, c, eps);
+      else
+        rmsnorm_fwd_warp<XT, WT, YT, 16><<<wgrid, kRowWarps * 32, 0, stream>>>(
+            xp, xs, wp, yp, ys, rstd, rows, c, eps);
+      return qb::check_launch("rmsnorm_fwd");
+    }
+  }
+  const RowPlan p = plan_row(cols, vec_ok);
+  const dim3 grid(static_cast<unsigned>(rows));
   switch (p.vpt) {
     case 1: rmsnorm_fwd_vec<XT, WT, YT, 1><<<grid, p.threads, 0, stream>>>(xp, xs, wp, yp, ys, rstd, c, eps); break;
     case 2: rmsnorm_fwd_vec<XT, WT, YT, 2><<<grid, p.threads, 0, stream>>>(xp, xs, wp, yp, ys, rstd, c, eps); break;
@@ -185,13 +265,13 @@ int bwd_typed(const void* dy, int64_t dys, const void* x, int64_t xs, const void
               cudaStream_t stream) {
   const bool vec_ok = rows_aligned(dy, dys, sizeof(DYT)) && rows_aligned(x, xs, sizeof(XT)) &&
                       rows_aligned(dx, dxs, sizeof(XT)) && qb::aligned16(w);
-  const RowPlan p = plan_row(cols, vec_ok);
   const auto* dyp = static_cast<const DYT*>(dy);
   const auto* xp = static_cast<const XT*>(x);
   const auto* wp = static_cast<const WT*>(w);
   auto* dxp = static_cast<XT*>(dx);
-  const dim3 grid(static_cast<unsigned>(rows));
   const int c = static_cast<int>(cols);
+  const RowPlan p = plan_row(cols, vec_ok);
+  const dim3 grid(static_cast<unsigned>(rows));
   switch (p.vpt) {
     case 1: rmsnorm_bwd_vec<DYT, XT, WT, 1><<<grid, p.threads, 0, stream>>>(dyp, dys, xp, xs, wp, rstd, dxp, dxs, c); break;
     case 2: rmsnorm_bwd_vec<DYT, XT, WT, 2><<<grid, p.threads, 0, stream>>>(dyp, dys, xp, xs, wp, rstd, dxp, dxs, c); break;

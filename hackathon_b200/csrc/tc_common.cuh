@@ -222,6 +222,11 @@ __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// every committed store of this thread but the newest one has finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read_newest_pending() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 // every committed store of this thread has completed
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");

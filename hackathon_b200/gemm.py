@@ -48,8 +48,9 @@ def gemm(a, b_t, out=None, out_dtype=torch.bfloat16, bias=None):
     return out
 
 
-def gemm_acc_f32(a, b_t, out, alpha=1.0):
-    """out[M, N] (fp32, in place) += alpha * a[M, K] @ b_t[N, K].T on the tcgen05 GEMM, K split
+def gemm_acc_f32(a, b_t, out, alpha=1.0, accumulate=True):
+    """out[M, N] (fp32, in place) = (out if accumulate else 0) + alpha * a[M, K] @ b_t[N, K].T
+    on the tcgen05 GEMM (without accumulate, out is not read: it may hold anything), K split
     across the SMs when the output has too few tiles (C-ABI qb_gemm_bf16_acc_f32; the partial
     products meet in a workspace and are summed in a fixed order, so the result is the same on
     every run): the skinny LoRA weight gradients, whose K is the token count. Operands bf16,
@@ -66,7 +67,8 @@ def gemm_acc_f32(a, b_t, out, alpha=1.0):
     nws = int(_lib.load().qb_gemm_bf16_acc_f32_workspace(M, N, K)) if M and N and K else 0
     ws = torch.empty(nws, dtype=torch.float32, device=a.device) if nws else None
     _lib.call("qb_gemm_bf16_acc_f32", a.data_ptr(), lda, int(a_mn), b_t.data_ptr(), ldb,
-              int(b_mn), float(alpha), out.data_ptr(), out.stride(0), M, N, K, _lib.ptr(ws),
+              int(b_mn), float(alpha), 1.0 if accumulate else 0.0, out.data_ptr(),
+              out.stride(0), M, N, K, _lib.ptr(ws),
               nws, _lib.stream(a.device), work=(0, 2 * M * N * K))
     return out
 
@@ -80,11 +82,11 @@ def lora_products(g, u, xd, b_scaled, a_shape, scaling, need_a=True, need_b=True
     v = gemm(g, b_scaled.t())
     da = db = None
     if need_a:
-        da = torch.zeros(a_shape, dtype=torch.float32, device=g.device)
-        gemm_acc_f32(v.t(), xd.t(), da)
+        da = torch.empty(a_shape, dtype=torch.float32, device=g.device)
+        gemm_acc_f32(v.t(), xd.t(), da, accumulate=False)
     if need_b:
-        db = torch.zeros((g.shape[1], u.shape[1]), dtype=torch.float32, device=g.device)
-        gemm_acc_f32(g.t(), u.t(), db, alpha=scaling)
+        db = torch.empty((g.shape[1], u.shape[1]), dtype=torch.float32, device=g.device)
+        gemm_acc_f32(g.t(), u.t(), db, alpha=scaling, accumulate=False)
     return v, da, db
 
 

@@ -127,6 +127,89 @@ def dropout_apply(x2, bits, scale, out=None, accumulate=False):
     return out
 
 
+# The C layout of qb_pack_segment (include/qlora_b200.h): a table of these, built once, drives
+# the one launch of qb_adapter_pack.
+PACK_SEGMENT = [("src", "<u8"), ("dst", "<u8"), ("src_ld", "<i8"), ("dst_ld", "<i8"),
+                ("rows", "<i4"), ("cols", "<i4"), ("scale", "<f4"), ("pad", "<i4"),
+                ("first_chunk", "<i8")]
+PACK_CHUNK = 2048
+
+
+def pack_table(segments):
+    """The qb_pack_segment table of (src fp32 [rows, cols] view, dst bf16 view of the same shape,
+    scale) triples, as bytes, and the launch's chunk count."""
+    import numpy as np
+    table = np.zeros(len(segments), dtype=np.dtype(PACK_SEGMENT))
+    chunks = 0
+    for i, (src, dst, scale) in enumerate(segments):
+        if src.dim() != 2 or src.shape != dst.shape:
+            raise ValueError("pack_table: 2-D src and dst of one shape")
+        if src.dtype != torch.float32 or dst.dtype != torch.bfloat16:
+            raise TypeError("pack_table: fp32 src, bf16 dst")
+        if src.stride(1) != 1 or dst.stride(1) != 1:
+            raise ValueError("pack_table: rows with unit column stride")
+        rows, cols = src.shape
+        table[i] = (src.data_ptr(), dst.data_ptr(), src.stride(0), dst.stride(0), rows, cols,
+                    scale, 0, chunks)
+        chunks += (rows * cols + PACK_CHUNK - 1) // PACK_CHUNK
+    return table.tobytes(), chunks
+
+
+class AdapterShadow:
+    """bf16 copies of a model's LoRA operands, rebuilt by one launch per step (qb_adapter_pack)
+    instead of one conversion per projection per use (forward, checkpoint recompute and
+    backward: the lora_A.to(bf16) and (lora_B * scaling).to(bf16) of solution/lora.py:160-172).
+
+    For every module: a16 = bf16(A) [r, in] and sb16 = bf16(s B) [out, r]; for every (gate, up)
+    pair also the [I, 2r] extra-K operands of the fused gate/up GEMM, [s B_g | 0] and [0 | s B_u]
+    (their zero halves written once). The modules read them through `adapter16` while the
+    shadow is attached; refresh() must run after every change of the adapters (the model runs it
+    at the start of each forward) - the optimizer updates them in place, without a version bump
+    under fused AdamW, so nothing else tells the copies are stale."""
+
+    def __init__(self, modules, pairs=()):
+        mods = list(modules)
+        if not mods:
+            raise ValueError("AdapterShadow: no modules")
+        dev = mods[0].lora_A.device
+        sizes = [m.lora_A.numel() + m.lora_B.numel() for m in mods]
+        pair_sizes = [2 * g.lora_B.shape[0] * 2 * g.lora_B.shape[1] for g, _ in pairs]
+        self.buf = torch.zeros(sum(sizes) + sum(pair_sizes), dtype=torch.bfloat16, device=dev)
+        segs, off = [], 0
+        for m in mods:
+            a, b = m.lora_A.detach(), m.lora_B.detach()
+            a16 = self.buf[off: off + a.numel()].view(a.shape)
+            off += a.numel()
+            sb16 = self.buf[off: off + b.numel()].view(b.shape)
+            off += b.numel()
+            segs += [(a, a16, 1.0), (b, sb16, float(m.scaling))]
+            m._shadow16 = (a16, sb16)
+        for g, u in pairs:
+            I, r = g.lora_B.shape
+            b1 = []
+            for k, mod in enumerate((g, u)):
+                t = self.buf[off: off + I * 2 * r].view(I, 2 * r)
+                off += I * 2 * r
+                segs.append((mod.lora_B.detach(), t[:, k * r:(k + 1) * r], float(mod.scaling)))
+                b1.append(t)
+            g._shadow_b1 = u._shadow_b1 = tuple(b1)
+        table, self.chunks = pack_table(segs)
+        self.nseg = len(segs)
+        self.elements = sum(src.numel() for src, _, _ in segs)
+        self.table = torch.frombuffer(bytearray(table), dtype=torch.uint8).to(dev)
+        self.modules, self.pairs = mods, list(pairs)
+
+    def refresh(self):
+        _lib.call("qb_adapter_pack", self.table.data_ptr(), self.nseg, self.chunks,
+                  _lib.stream(self.buf.device), work=(self.elements * 6, 0))
+
+    def detach(self):
+        for m in self.modules:
+            m._shadow16 = None
+        for g, u in self.pairs:
+            g._shadow_b1 = u._shadow_b1 = None
+
+
 class DropoutCast:
     """x -> dropout(x) * 1/(1-p) cast to out_dtype, the mask a function of (seed, flat index) only
     (lora.py:84-93): the custom op qlora_b200::dropout_scale, whose registered backward applies

@@ -188,16 +188,20 @@ class GateUpSwiGLU(torch.autograd.Function):
         x2 = x.reshape(-1, x.shape[-1])
         T, H = x2.shape
         I, r = gate.out_features, a_g.shape[0]
-        a16_g, a16_u = a_g.to(x.dtype), a_u.to(x.dtype)
+        a16_g, _ = gate.adapter16(x.dtype)
+        a16_u, _ = up.adapter16(x.dtype)
         lora_u = torch.empty((T, 2 * r), dtype=x.dtype, device=x.device)   # [U_g | U_u]
         xd_g, u_g, bits_g, scale = _adapter_input(x2, gate, a16_g, p, seed_g, save_gu,
                                                   u_out=lora_u[:, :r])
         xd_u, u_u, bits_u, _ = _adapter_input(x2, up, a16_u, p, seed_u, save_gu,
                                               u_out=lora_u[:, r:])
-        b1_g = torch.zeros((I, 2 * r), dtype=x.dtype, device=x.device)
-        b1_u = torch.zeros_like(b1_g)
-        b1_g[:, :r] = b_g * gate.scaling
-        b1_u[:, r:] = b_u * up.scaling
+        if gate._shadow_b1 is not None and x.dtype == torch.bfloat16:
+            b1_g, b1_u = gate._shadow_b1
+        else:
+            b1_g = torch.zeros((I, 2 * r), dtype=x.dtype, device=x.device)
+            b1_u = torch.zeros_like(b1_g)
+            b1_g[:, :r] = b_g * gate.scaling
+            b1_u[:, r:] = b_u * up.scaling
         # Under activation checkpointing both passes must save the same tensors (the recompute's
         # are unpacked in the first pass's slots): what the first pass would keep for the
         # backward is an empty placeholder there, never None.
@@ -238,12 +242,13 @@ class GateUpSwiGLU(torch.autograd.Function):
         _lib.call("qb_swiglu_bwd", dh2.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(),
                   du.data_ptr(), _lib.tag(g.dtype), g.numel(), _lib.stream(g.device),
                   work=(5 * g.numel() * g.element_size(), 0))
-        a16_g, a16_u = a_g.to(g.dtype), a_u.to(g.dtype)
+        a16_g, sb16_g = gate.adapter16(g.dtype)
+        a16_u, sb16_u = up.adapter16(g.dtype)
         need = ctx.needs_input_grad
-        v_g, da_g, db_g = lora_products(dg, u_g, xd_g, (b_g * gate.scaling).to(g.dtype),
-                                        a_g.shape, gate.scaling, need[1], need[2])
-        v_u, da_u, db_u = lora_products(du, u_u, xd_u, (b_u * up.scaling).to(g.dtype),
-                                        a_u.shape, up.scaling, need[3], need[4])
+        v_g, da_g, db_g = lora_products(dg, u_g, xd_g, sb16_g, a_g.shape, gate.scaling, need[1],
+                                        need[2])
+        v_u, da_u, db_u = lora_products(du, u_u, xd_u, sb16_u, a_u.shape, up.scaling, need[3],
+                                        need[4])
         for mod, seed in zip((gate, up), ctx.seeds):
             MASKS.pop((id(mod), seed), None)
         dx = None
@@ -290,9 +295,8 @@ class LoRANF4Proj(torch.autograd.Function):
                 keep_saved=True):
         from .nf4 import dequantize_nf4, nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
-        a16 = lora_a.to(x.dtype)
+        a16, sb16 = mod.adapter16(x.dtype)
         xd, u, bits, scale = _adapter_input(x2, mod, a16, p, seed, keep_saved)
-        sb16 = (lora_b * mod.scaling).to(x.dtype)
         w_keep = None
         if ctx.needs_input_grad[0] and uses_dequant_path(x2.shape[0]):
             w_keep = dequantize_nf4(mod.packed, mod.quant_state, torch.bfloat16,
@@ -323,8 +327,7 @@ class LoRANF4Proj(torch.autograd.Function):
         if ctx.rope is not None:      # through the RoPE first: its transpose
             from .rope import rope_rows
             g2 = rope_rows(g2, ctx.rope[0], ctx.rope[1], backward=True)
-        a16 = lora_a.to(xd.dtype)
-        sb16 = (lora_b * mod.scaling).to(xd.dtype)
+        a16, sb16 = mod.adapter16(xd.dtype)
         v, da, db = lora_products(g2, u, xd, sb16, lora_a.shape, mod.scaling,
                                   ctx.needs_input_grad[1], ctx.needs_input_grad[2])
         if p > 0:
@@ -368,6 +371,16 @@ class LoRANF4Linear(torch.nn.Module):
         self.p = shape.lora_dropout
         self.in_features, self.out_features = in_features, out_features
         self.fused = True
+        self._shadow16 = None     # (A, s B) in bf16 from an attached lora.AdapterShadow
+        self._shadow_b1 = None    # a gate/up pair's ([s B_g | 0], [0 | s B_u]) from the shadow
+
+    def adapter16(self, dtype):
+        """(A, s B) in `dtype` for the adapter GEMMs: the attached AdapterShadow's copies (bf16,
+        rebuilt once per step) when there is one, else converted here."""
+        if self._shadow16 is not None and dtype == torch.bfloat16:
+            return self._shadow16
+        return (self.lora_A.detach().to(dtype),
+                (self.lora_B.detach() * self.scaling).to(dtype))
 
     def forward(self, x, seed, residual=None, rope=None, output_dead=False, keep_saved=True):
         """residual + this projection of x (the residual add of the decoder layer rides in the
@@ -501,6 +514,11 @@ class QwenQLoRA(torch.nn.Module):
         self.mask_prefetch = False
         self._rope = {}
         self.step_seed = 0
+        # the bf16 adapter operands of every projection, rebuilt by one launch per forward
+        from .lora import AdapterShadow
+        self.adapter_shadow = AdapterShadow(
+            [m for m in self.modules() if isinstance(m, LoRANF4Linear)],
+            [(layer.gate, layer.up) for layer in self.layers])
 
     def rope_tables(self, seq, device):
         key = (seq, device)
@@ -519,6 +537,8 @@ class QwenQLoRA(torch.nn.Module):
         if MASKS and dev in _SIDE_STREAMS:   # masks a side stream may still be writing
             torch.cuda.current_stream(dev).wait_stream(_SIDE_STREAMS[dev])
         MASKS.clear()
+        if self.adapter_shadow is not None:   # the adapters changed since the last forward
+            self.adapter_shadow.refresh()
         cos, sin = self.rope_tables(S, dev)
         h = F.embedding(input_ids, self.embed)
         seeds = [self.layer_seed(i) for i in range(len(self.layers))]
@@ -580,6 +600,8 @@ def train_step(model, opt, input_ids, labels, grad_sync=None, num_items_in_batch
     if grad_sync is not None:
         grad_sync()
     opt.step()
-    opt.zero_grad(set_to_none=False)
+    # with a gradient sync the .grad tensors are views into its flat buffer and stay; without
+    # one, dropping them lets the next backward hand its fresh gradients over without an add
+    opt.zero_grad(set_to_none=grad_sync is None)
     model.step_seed += 1
     return loss.detach()

@@ -190,6 +190,30 @@ int qb_scaled_add(const void* base, int base_dtype, int64_t base_row_stride, con
                   int64_t out_row_stride, int64_t rows, int64_t cols, float scaling,
                   cudaStream_t stream);
 
+/* One segment of qb_adapter_pack: rows x cols fp32 at src (row stride src_ld elements) ->
+ * bf16 at dst (row stride dst_ld), each element multiplied by `scale` in fp32 and rounded to
+ * nearest even - the bits of (src * scale).to(bfloat16). first_chunk: the segment's first
+ * 2048-element chunk in the launch (the running sum of the earlier segments' chunks). */
+typedef struct {
+  const float* src;
+  void* dst;
+  int64_t src_ld, dst_ld;
+  int32_t rows, cols;
+  float scale;
+  int32_t pad;
+  int64_t first_chunk;
+} qb_pack_segment;
+
+/* sizeof(qb_pack_segment): the layout check of a binding that builds the table itself. */
+int64_t qb_pack_segment_size(void);
+
+/* The bf16 operands of every LoRA adapter of a model in one launch (the per-projection
+ * lora_A.to(bf16) and (lora_B * scaling).to(bf16) of solution/lora.py:160-172 under autocast,
+ * once per step instead of once per use): `segs` is a device array of nseg segments sorted by
+ * first_chunk, total_chunks the sum of their chunks (ceil(rows * cols / 2048) each). */
+int qb_adapter_pack(const qb_pack_segment* segs, int nseg, int64_t total_chunks,
+                    cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------
  * Cross-entropy over rows of materialised logits (the chunked path)
  */
@@ -357,17 +381,17 @@ int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* weight, int64
  * launch runs unsplit and needs none). */
 int64_t qb_gemm_bf16_acc_f32_workspace(int64_t M, int64_t N, int64_t K);
 
-/* C[M,N] (fp32, row stride ldc) += alpha * A[M,K] * B[N,K]^T on the tcgen05 GEMM. When there are
- * too few output tiles to fill the SMs the k-blocks are split into ranges: each range's partial
- * product goes to `workspace` (at least qb_gemm_bf16_acc_f32_workspace floats, 16-byte aligned)
- * and a second kernel adds alpha * their sum, taken in range order, into C - the same bits on
- * every run. Operand layouts as qb_gemm_bf16. The LoRA weight gradients of lora.py:172
- * (nn.Linear backward under autocast): dA = V^T xd and dB = s g^T U, skinny outputs whose K is
- * the token count. */
+/* C[M,N] (fp32, row stride ldc) = beta * C + alpha * A[M,K] * B[N,K]^T on the tcgen05 GEMM,
+ * beta 0 (C is written without being read) or 1. When there are too few output tiles to fill
+ * the SMs the k-blocks are split into ranges: each range's partial product goes to `workspace`
+ * (at least qb_gemm_bf16_acc_f32_workspace floats, 16-byte aligned) and a second kernel adds
+ * alpha * their sum, taken in range order - the same bits on every run. Operand layouts as
+ * qb_gemm_bf16. The LoRA weight gradients of lora.py:172 (nn.Linear backward under autocast):
+ * dA = V^T xd and dB = s g^T U, skinny outputs whose K is the token count. */
 int qb_gemm_bf16_acc_f32(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb,
-                         int b_mn_major, float alpha, float* C, int64_t ldc, int64_t M,
-                         int64_t N, int64_t K, float* workspace, int64_t workspace_floats,
-                         cudaStream_t stream);
+                         int b_mn_major, float alpha, float beta, float* C, int64_t ldc,
+                         int64_t M, int64_t N, int64_t K, float* workspace,
+                         int64_t workspace_floats, cudaStream_t stream);
 
 /* Reads and clears this device's tensor-core error flag (synchronises `stream`): QB_OK, or
  * QB_ERR_TIMEOUT when a kernel gave up one of its bounded waits (its output is then invalid). */

@@ -167,7 +167,8 @@ def test_gemm_ragged_bf16_both_b_layouts(cuda, shape, b_t):
     _check(out2, _ref(a, b) + _ref(u, v), torch.bfloat16)
 
 
-@pytest.mark.parametrize("shape", [(300, 1000, 64), (16384, 3584, 64), (129, 200, 16)])
+@pytest.mark.parametrize("shape", [(300, 1000, 64), (16384, 3584, 64), (129, 200, 16),
+                                   (2048, 640, 128), (777, 18944, 64)])
 @pytest.mark.parametrize("b_t", [True, False])
 def test_gemm_mask_acc(cuda, shape, b_t):
     """C += s * mask .* (A B^T) with the dropout bit words (qb_gemm_bf16_mask_acc): against the
@@ -215,16 +216,18 @@ def test_gemm2_residual_epilogue(cuda, lora):
     torch.testing.assert_close(out.float(), ref, rtol=1.6e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("accumulate", [True, False])
 @pytest.mark.parametrize("a_t", [False, True])
 @pytest.mark.parametrize("b_t", [False, True])
 @pytest.mark.parametrize("shape", [(3584, 64, 16384), (64, 3584, 16384), (512, 64, 16384),
                                    (200, 100, 1000), (129, 130, 200), (1, 64, 64),
                                    (300, 257, 4096)])
-def test_gemm_acc_f32_split_k(cuda, shape, a_t, b_t):
-    """C (fp32) += alpha A B^T with the tokens split across the SMs (the LoRA weight gradients:
-    [in, r] / [r, in] / [out, r] outputs, K = 16384), every orientation, ragged shapes and narrow
-    tiles, accumulating into a C that already holds values, against fp32 torch; a second run
-    gives the same bits (the splits are summed in a fixed order)."""
+def test_gemm_acc_f32_split_k(cuda, shape, a_t, b_t, accumulate):
+    """C (fp32) = (C or 0) + alpha A B^T with the tokens split across the SMs (the LoRA weight
+    gradients: [in, r] / [r, in] / [out, r] outputs, K = 16384), every orientation, ragged shapes
+    and narrow tiles, accumulating into a C that already holds values or overwriting one that
+    holds NaN, against fp32 torch; a second run gives the same bits (the splits are summed in a
+    fixed order)."""
     from hackathon_b200 import _lib
     from hackathon_b200.gemm import device_error, gemm_acc_f32
     M, N, K = shape
@@ -233,11 +236,14 @@ def test_gemm_acc_f32_split_k(cuda, shape, a_t, b_t):
         torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
     b = torch.randn(K, N, device=cuda, generator=g).to(torch.bfloat16).t() if b_t else \
         torch.randn(N, K, device=cuda, generator=g).to(torch.bfloat16)
-    c0 = torch.randn(M, N, device=cuda, generator=g)
-    out = gemm_acc_f32(a, b, c0.clone(), alpha=0.5)
-    again = gemm_acc_f32(a, b, c0.clone(), alpha=0.5)
+    c0 = torch.randn(M, N, device=cuda, generator=g) if accumulate else \
+        torch.full((M, N), float("nan"), device=cuda)     # without accumulate C is not read
+    out = gemm_acc_f32(a, b, c0.clone(), alpha=0.5, accumulate=accumulate)
+    again = gemm_acc_f32(a, b, c0.clone(), alpha=0.5, accumulate=accumulate)
     device_error()
-    ref = c0 + 0.5 * (a.float() @ b.float().t())
+    ref = 0.5 * (a.float() @ b.float().t())
+    if accumulate:
+        ref = c0 + ref
     torch.testing.assert_close(out, ref, rtol=1e-3, atol=2e-3 * (K ** 0.5) / 8)
     assert torch.equal(out, again)
     if shape == (3584, 64, 16384):     # 28 tiles of a 256-k-block K: the split path ran

@@ -180,3 +180,25 @@ def test_ctypes_bindings_match_the_header_declarations():
         want = [k for k in map(c_kind, params.split(",")) if k is not None]
         have = [py_kind(t) for t in _lib._SIGNATURES[name]]
         assert have == want, f"{name}: binding {have} vs declaration {want}"
+
+
+def test_pack_segment_layout_and_table():
+    """The Python table of qb_adapter_pack has the C struct's size, and its chunk offsets are the
+    running sum of each segment's 2048-element chunks (host only: no launch)."""
+    import numpy as np
+    import torch
+    from hackathon_b200 import _lib
+    from hackathon_b200.lora import PACK_CHUNK, PACK_SEGMENT, pack_table
+    assert _lib.load().qb_pack_segment_size() == np.dtype(PACK_SEGMENT).itemsize == 56
+    src = [torch.zeros(64, 3584), torch.zeros(512, 64), torch.zeros(0, 64), torch.zeros(3, 5)]
+    dst = [torch.zeros(s.shape, dtype=torch.bfloat16) for s in src]
+    raw, chunks = pack_table([(s, d, 2.0) for s, d in zip(src, dst)])
+    table = np.frombuffer(raw, dtype=np.dtype(PACK_SEGMENT))
+    want = np.cumsum([0] + [(s.numel() + PACK_CHUNK - 1) // PACK_CHUNK for s in src])
+    assert list(table["first_chunk"]) == list(want[:-1]) and chunks == want[-1]
+    assert list(table["rows"]) == [64, 512, 0, 3] and list(table["src_ld"]) == [3584, 64, 64, 5]
+    assert table["src"][0] == src[0].data_ptr() and table["dst"][3] == dst[3].data_ptr()
+    with pytest.raises(TypeError):
+        pack_table([(src[0].double(), dst[0], 1.0)])
+    with pytest.raises(ValueError):
+        pack_table([(src[0], dst[1], 1.0)])

@@ -411,3 +411,49 @@ def test_many_long_token_steps_in_a_row(cuda):
         assert np.isfinite(loss), (i, loss)
         assert lib.qb_monitor_report(cuda.index or 0, buf, len(buf)) == 0
         assert "no CTA of these launches is running" in buf.value.decode(), (i, buf.value)
+
+
+def test_adapter_shadow_matches_per_use_conversion(cuda):
+    """The shadow's bf16 operands (one qb_adapter_pack launch) equal the per-projection
+    conversions bit for bit, follow an optimizer step, and a step with the shadow attached gives
+    the same loss and adapter gradients as one that converts at every use."""
+    from hackathon_b200.qlora import QwenQLoRA, make_optimizer, preset, synthetic_batch
+    bf16 = torch.bfloat16
+    shape = preset("0.5b", layers=2, lora_dropout=0.1)
+    model = QwenQLoRA(shape, cuda, seed=0)
+    ids, labels = synthetic_batch(shape, 1, 128, cuda, seed=3)
+
+    def check_shadow():
+        sh = model.adapter_shadow
+        for m in sh.modules:
+            a16, sb16 = m._shadow16
+            assert torch.equal(a16, m.lora_A.detach().to(bf16))
+            assert torch.equal(sb16, (m.lora_B.detach() * m.scaling).to(bf16))
+        for g, u in sh.pairs:
+            r = g.lora_B.shape[1]
+            b1g, b1u = g._shadow_b1
+            assert torch.equal(b1g[:, :r], (g.lora_B.detach() * g.scaling).to(bf16))
+            assert torch.equal(b1u[:, r:], (u.lora_B.detach() * u.scaling).to(bf16))
+            assert not b1g[:, r:].any() and not b1u[:, :r].any()
+
+    opt = make_optimizer(model, lr=1e-2)
+    model.train()
+    loss, _ = model(ids, labels)
+    check_shadow()
+    loss.backward()
+    opt.step()                      # fused AdamW: in place, no version bump
+    opt.zero_grad(set_to_none=True)
+    out = []
+    for attached in (True, False):
+        if not attached:
+            model.adapter_shadow.detach()
+            model.adapter_shadow = None
+        loss, _ = model(ids, labels)
+        if attached:
+            check_shadow()          # refreshed by this forward: the stepped adapters
+        loss.backward()
+        out.append((loss.detach(), torch.cat([p.grad.flatten()
+                                              for p in model.adapter_parameters()])))
+        opt.zero_grad(set_to_none=True)
+    assert torch.equal(out[0][0], out[1][0])
+    assert torch.equal(out[0][1], out[1][1])

@@ -191,6 +191,30 @@ def test_rmsnorm_strided_rows(cuda):
     torch.testing.assert_close(y.cpu(), yr, rtol=1.6e-2, atol=BF16_ATOL)
 
 
+@pytest.mark.parametrize("rows,hidden", [(3, 3584), (2375, 3584), (1000, 8192), (300, 5120),
+                                         (64, 8), (777, 4096)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_row_shapes(cuda, rows, hidden, dtype):
+    """Row counts and lengths around the kernels' dispatch limits: a few rows, rows that do not
+    fill the last CTA, rows of 4096 (the warp-per-row forward's longest) and beyond, a row of one
+    16-byte chunk; forward and backward against the oracle."""
+    from hackathon_b200.rmsnorm import rmsnorm
+    torch.manual_seed(rows + hidden)
+    weight = (1 + 0.1 * torch.randn(hidden)).to(dtype)
+    x = torch.randn(rows, hidden, dtype=dtype)
+    dy = torch.randn(rows, hidden).to(dtype)
+    xr = x.clone().requires_grad_()
+    yr = ops_ref.rmsnorm_ref(xr, weight, 1e-6)
+    yr.backward(dy)
+    xg = x.to(cuda).requires_grad_()
+    y = rmsnorm(xg, weight.to(cuda), 1e-6)
+    y.backward(dy.to(cuda))
+    tol = TOL[dtype]
+    atol = BF16_ATOL if dtype == torch.bfloat16 else tol
+    torch.testing.assert_close(y.cpu(), yr.detach(), rtol=tol, atol=atol)
+    torch.testing.assert_close(xg.grad.cpu(), xr.grad, rtol=tol, atol=atol)
+
+
 # ----------------------------------------------------------------------------------- RoPE
 
 @pytest.mark.parametrize("i", range(8))
