@@ -1,6 +1,6 @@
 """Generates tests/golden/*.npz by running the REFERENCE's own kernels on the CPU.
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [--ref /path/to/reference]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py --ref <checkout of the reference>
 
 The reference (imoshka2009-lab/hackathon, `solution/`) is Python + Triton; Triton's interpreter
 runs its kernels on CPU tensors. This script runs only where the reference is checked out; the
@@ -229,7 +229,7 @@ def gen_ce(torch, sol):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference (its solution/ package)")
     args = ap.parse_args()
     if os.environ.get("TRITON_INTERPRET") != "1":
         sys.exit("run with TRITON_INTERPRET=1 (the reference's kernels run in Triton's CPU interpreter)")
