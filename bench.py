@@ -260,8 +260,8 @@ def kernel_table(summary, pk):
     table = {}
     for name, d in summary.items():
         ms = d["ms_total"]
-        entry = {"launches": d["launches"], "ms_total": round(ms, 3),
-                 "bound": BOUND.get(name, "hbm")}
+        entry = {"launches": d["launches"], "kernels": d.get("kernels", d["launches"]),
+                 "ms_total": round(ms, 3), "bound": BOUND.get(name, "hbm")}
         if ms > 0 and entry["bound"] == "hbm":
             gbs = d["bytes"] / (ms * 1e-3) / 1e9
             entry.update(achieved_gbs=round(gbs, 1), frac=round(gbs / pk["hbm_gbs"], 3),
@@ -792,7 +792,7 @@ def main():
                        "l2": "working set (NF4 weights, activations) far larger than the 126 MB L2"},
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4, "last_loss": round(loss_value, 4)},
-            "gpu_launches": sum(v["launches"] for v in table.values()) * args.steps,
+            "gpu_launches": sum(v["kernels"] for v in table.values()) * args.steps,
             "roofline": roofline,
             "kernels": table,
             "kernel_ms_per_step_ours": round(ours_ms, 2),

@@ -117,7 +117,7 @@ class KernelTimer:
     can turn device time into achieved GB/s or TFLOP/s per kernel."""
 
     def __init__(self):
-        self.records = []   # (name, start event, end event, bytes, flops)
+        self.records = []   # (name, start event, end event, bytes, flops, kernels launched)
 
     def __enter__(self):
         global _timer
@@ -129,12 +129,15 @@ class KernelTimer:
         _timer = self._prev
 
     def summary(self):
-        """{name: {"launches", "ms_total", "bytes", "flops"}} (synchronises)."""
+        """{name: {"launches" (calls), "kernels", "ms_total", "bytes", "flops"}}
+        (synchronises)."""
         torch.cuda.synchronize()
         out = {}
-        for name, s, e, nbytes, flops in self.records:
-            d = out.setdefault(name, {"launches": 0, "ms_total": 0.0, "bytes": 0, "flops": 0})
+        for name, s, e, nbytes, flops, kernels in self.records:
+            d = out.setdefault(name, {"launches": 0, "kernels": 0, "ms_total": 0.0, "bytes": 0,
+                                      "flops": 0})
             d["launches"] += 1
+            d["kernels"] += kernels
             d["ms_total"] += s.elapsed_time(e)
             d["bytes"] += nbytes
             d["flops"] += flops
@@ -144,9 +147,10 @@ class KernelTimer:
 _timer = None
 
 
-def call(name, *args, work=(0, 0)):
+def call(name, *args, work=(0, 0), kernels=1):
     """Calls a C-ABI entry point; raises RuntimeError with the library's message on failure.
-    `work` = (algorithmic bytes, flops) of the call, recorded when a KernelTimer is active."""
+    `work` = (algorithmic bytes, flops) of the call and `kernels` the kernels it launches,
+    recorded when a KernelTimer is active."""
     lib = load()
     timer = _timer
     if timer is not None:
@@ -155,7 +159,7 @@ def call(name, *args, work=(0, 0)):
         s.record()
         status = getattr(lib, name)(*args)
         e.record()
-        timer.records.append((name, s, e, int(work[0]), int(work[1])))
+        timer.records.append((name, s, e, int(work[0]), int(work[1]), int(kernels)))
     else:
         status = getattr(lib, name)(*args)
     if status != 0:

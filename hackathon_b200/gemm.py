@@ -69,7 +69,9 @@ def gemm_acc_f32(a, b_t, out, alpha=1.0, accumulate=True):
     _lib.call("qb_gemm_bf16_acc_f32", a.data_ptr(), lda, int(a_mn), b_t.data_ptr(), ldb,
               int(b_mn), float(alpha), 1.0 if accumulate else 0.0, out.data_ptr(),
               out.stride(0), M, N, K, _lib.ptr(ws),
-              nws, _lib.stream(a.device), work=(0, 2 * M * N * K))
+              nws, _lib.stream(a.device),
+              work=((M + N) * K * 2 + M * N * 4 * (2 if accumulate else 1), 2 * M * N * K),
+              kernels=2 if nws else 1)
     return out
 
 

@@ -158,7 +158,8 @@ def pack_table(segments):
 class AdapterShadow:
     """bf16 copies of a model's LoRA operands, rebuilt by one launch per step (qb_adapter_pack)
     instead of one conversion per projection per use (forward, checkpoint recompute and
-    backward: the lora_A.to(bf16) and (lora_B * scaling).to(bf16) of solution/lora.py:160-172).
+    backward: the casts autocast makes of lora_A / lora_B's fp32 weights at every call of
+    solution/lora.py:172, with the scaling of :173 folded into B).
 
     For every module: a16 = bf16(A) [r, in] and sb16 = bf16(s B) [out, r]; for every (gate, up)
     pair also the [I, 2r] extra-K operands of the fused gate/up GEMM, [s B_g | 0] and [0 | s B_u]

@@ -208,7 +208,8 @@ typedef struct {
 int64_t qb_pack_segment_size(void);
 
 /* The bf16 operands of every LoRA adapter of a model in one launch (the per-projection
- * lora_A.to(bf16) and (lora_B * scaling).to(bf16) of solution/lora.py:160-172 under autocast,
+ * casts autocast makes of lora_A / lora_B's fp32 weights at every call of solution/lora.py:172,
+ * the scaling of :173 folded into B,
  * once per step instead of once per use): `segs` is a device array of nseg segments sorted by
  * first_chunk, total_chunks the sum of their chunks (ceil(rows * cols / 2048) each). */
 int qb_adapter_pack(const qb_pack_segment* segs, int nseg, int64_t total_chunks,
