@@ -147,7 +147,22 @@ dropout_mask_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out
 // The same for rows of a multiple of 32 columns with 16-byte-aligned rows: 8 elements per
 // thread (16-byte accesses for 2-byte types), four consecutive threads combine their 8 bits
 // into one mask word.
-template <typename IT, typename OT>
+// (row, first column) of work item i of n8 items per row: 32-bit division when every index fits
+// in 32 bits (a few instructions; the 64-bit one costs as much as several Philox rounds).
+template <bool SMALL>
+__device__ __forceinline__ void row_col8(int64_t i, int64_t n8, int64_t& row, int64_t& c) {
+  if (SMALL) {
+    const uint32_t ii = static_cast<uint32_t>(i), nn = static_cast<uint32_t>(n8);
+    const uint32_t r = ii / nn;
+    row = r;
+    c = static_cast<int64_t>(ii - r * nn) * 8;
+  } else {
+    row = i / n8;
+    c = (i - row * n8) * 8;
+  }
+}
+
+template <typename IT, typename OT, bool SMALL>
 __global__ void __launch_bounds__(kThreads)
 dropout_mask8_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ out, int64_t outs,
                      uint32_t* __restrict__ bits, int64_t rows, int64_t cols, uint32_t k0,
@@ -158,8 +173,9 @@ dropout_mask8_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ ou
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
        i - lane < total; i += static_cast<int64_t>(gridDim.x) * kThreads) {
     uint32_t b = 0;
+    int64_t row = 0, c = 0;
     if (i < total) {
-      const int64_t row = i / n8, c = (i % n8) * 8;
+      row_col8<SMALL>(i, n8, row, c);
       float v[8];
       qb::load8<IT>(in + row * ins + c, v);
       const uint32_t off0 = static_cast<uint32_t>(row * cols + c);
@@ -174,15 +190,12 @@ dropout_mask8_kernel(const IT* __restrict__ in, int64_t ins, OT* __restrict__ ou
     uint32_t w = b << ((lane & 3) * 8);
     w |= __shfl_xor_sync(0xffffffffu, w, 1);
     w |= __shfl_xor_sync(0xffffffffu, w, 2);
-    if (i < total && (lane & 3) == 0) {
-      const int64_t row = i / n8, c = (i % n8) * 8;
-      bits[row * (cols / 32) + c / 32] = w;
-    }
+    if (i < total && (lane & 3) == 0) bits[row * (cols / 32) + c / 32] = w;
   }
 }
 
 // out (+)= in * bit * scale from recorded mask bits: no random numbers, one HBM pass.
-template <typename IT, typename OT, bool ACC>
+template <typename IT, typename OT, bool ACC, bool SMALL>
 __global__ void __launch_bounds__(kThreads)
 dropout_apply_kernel(const IT* __restrict__ in, int64_t ins, const uint32_t* __restrict__ bits,
                      int64_t words, OT* __restrict__ out, int64_t outs, int64_t rows,
@@ -191,7 +204,8 @@ dropout_apply_kernel(const IT* __restrict__ in, int64_t ins, const uint32_t* __r
   const int64_t total = rows * n8;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * kThreads) {
-    const int64_t row = i / n8, c = (i % n8) * 8;
+    int64_t row, c;
+    row_col8<SMALL>(i, n8, row, c);
     const uint32_t b = (bits[row * words + c / 32] >> (c % 32)) & 0xffu;
     float v[8];
     qb::load8<IT>(in + row * ins + c, v);
@@ -243,6 +257,26 @@ unsigned grid_cap(int64_t work_items) {
   return static_cast<unsigned>(g);
 }
 
+template <typename IT, typename OT>
+void launch_apply(const IT* in, int64_t ins, const uint32_t* bits, int64_t words, OT* out,
+                  int64_t outs, int64_t rows, int64_t cols, float scale, bool acc,
+                  cudaStream_t stream) {
+  const unsigned grid = grid_cap(rows * (cols / 8));
+  const bool small = rows * (cols / 8) <= 0xffffffffll;
+  if (acc && small)
+    dropout_apply_kernel<IT, OT, true, true><<<grid, kThreads, 0, stream>>>(
+        in, ins, bits, words, out, outs, rows, cols, scale);
+  else if (acc)
+    dropout_apply_kernel<IT, OT, true, false><<<grid, kThreads, 0, stream>>>(
+        in, ins, bits, words, out, outs, rows, cols, scale);
+  else if (small)
+    dropout_apply_kernel<IT, OT, false, true><<<grid, kThreads, 0, stream>>>(
+        in, ins, bits, words, out, outs, rows, cols, scale);
+  else
+    dropout_apply_kernel<IT, OT, false, false><<<grid, kThreads, 0, stream>>>(
+        in, ins, bits, words, out, outs, rows, cols, scale);
+}
+
 }  // namespace
 
 extern "C" int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stride, void* out,
@@ -261,9 +295,15 @@ extern "C" int qb_dropout_mask(const void* in, int in_dtype, int64_t in_row_stri
     QB_DISPATCH_FLOAT(out_dtype, OT, {
       if (cols % 32 == 0 && rows_ok(in, in_row_stride, sizeof(IT)) &&
           rows_ok(out, out_row_stride, sizeof(OT))) {
-        dropout_mask8_kernel<IT, OT><<<grid_cap(rows * (cols / 8)), kThreads, 0, stream>>>(
-            static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out), out_row_stride,
-            bits, rows, cols, k0, k1, thresh, scale);
+        const unsigned grid = grid_cap(rows * (cols / 8));
+        if (rows * (cols / 8) <= 0xffffffffll)
+          dropout_mask8_kernel<IT, OT, true><<<grid, kThreads, 0, stream>>>(
+              static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out),
+              out_row_stride, bits, rows, cols, k0, k1, thresh, scale);
+        else
+          dropout_mask8_kernel<IT, OT, false><<<grid, kThreads, 0, stream>>>(
+              static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out),
+              out_row_stride, bits, rows, cols, k0, k1, thresh, scale);
       } else {
         dropout_mask_kernel<IT, OT><<<grid_cap(rows * words * 32), kThreads, 0, stream>>>(
             static_cast<const IT*>(in), in_row_stride, static_cast<OT*>(out), out_row_stride,
@@ -306,15 +346,9 @@ extern "C" int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_str
     QB_DISPATCH_FLOAT(out_dtype, OT, {
       if (!rows_ok(in, in_row_stride, sizeof(IT)) || !rows_ok(out, out_row_stride, sizeof(OT)))
         return qb::fail(QB_ERR_INVALID, "dropout_apply: rows must be 16-byte aligned");
-      const unsigned grid = grid_cap(rows * (cols / 8));
-      if (accumulate)
-        dropout_apply_kernel<IT, OT, true><<<grid, kThreads, 0, stream>>>(
-            static_cast<const IT*>(in), in_row_stride, bits, words, static_cast<OT*>(out),
-            out_row_stride, rows, cols, scale);
-      else
-        dropout_apply_kernel<IT, OT, false><<<grid, kThreads, 0, stream>>>(
-            static_cast<const IT*>(in), in_row_stride, bits, words, static_cast<OT*>(out),
-            out_row_stride, rows, cols, scale);
+      launch_apply<IT, OT>(static_cast<const IT*>(in), in_row_stride, bits, words,
+                           static_cast<OT*>(out), out_row_stride, rows, cols, scale,
+                           accumulate != 0, stream);
     });
   });
   return qb::check_launch("dropout_apply");
