@@ -295,16 +295,7 @@ extern "C" int qb_gemm_bf16_mask_acc(const void* A, int64_t lda, const void* B, 
              static_cast<int>((M + BM - 1) / BM), static_cast<int>((N + BN - 1) / BN), ldbits,
              scale, qb::aligned16(bits) && ldbits % 4 == 0};
   auto kernel = b_mn_major ? lora_dx_kernel<true> : lora_dx_kernel<false>;
-  static bool configured[2][64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return qb::fail(QB_ERR_UNSUPPORTED, "%s: device %d", what, dev);
-  if (!configured[b_mn_major ? 1 : 0][dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess)
-      return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
-    configured[b_mn_major ? 1 : 0][dev] = true;
-  }
+  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), kSmem, what)) return s;
   const int tiles = pb.num_m * pb.num_n;
   int grid = tc_host::sm_count();
   if (grid > tiles) grid = tiles;

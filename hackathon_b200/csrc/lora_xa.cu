@@ -353,17 +353,8 @@ extern "C" int qb_lora_xa(const void* x, int64_t ldx, const void* a, int64_t lda
   pb.masked = bits != nullptr;
   pb.store_xd = xd != nullptr;
   pb.bits_vec = bits && qb::aligned16(bits) && ldbits % 4 == 0;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return qb::fail(QB_ERR_UNSUPPORTED, "%s: device %d", what, dev);
-  if (!configured[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(lora_xa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess)
-      return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(lora_xa_kernel), kSmem, what))
+    return s;
   int grid = tc_host::sm_count();
   if (grid > pb.num_m) grid = pb.num_m;
   tc::Ctl ctl;

@@ -480,6 +480,11 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uin
 // SM count of the current device (cached).
 int sm_count();
 
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` once per kernel and driver context
+// (a function attribute belongs to the context: after cudaDeviceReset the new context needs it
+// again). Thread-safe. Returns 0 or the library's error status.
+int ensure_smem(const void* kernel, int bytes, const char* what);
+
 // Per-device error flag the tensor-core kernels raise when a bounded wait gives up (word 0 of
 // the device's tc::ErrBlock).
 int* device_error_flag();

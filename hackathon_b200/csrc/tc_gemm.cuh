@@ -270,15 +270,7 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
   static_assert(B0 != kTmaKDual || BN % 2 == 0, "dual B splits the tile in halves");
   using C = Cfg<BN>;
   auto kernel = tc_gemm_kernel<A0, B0, A1, B1, BN, Epi>;
-  static bool configured[64] = {};  // per instantiation and device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return qb::fail(QB_ERR_UNSUPPORTED, "%s: device %d", what, dev);
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), C::SMEM, what)) return s;
   const int tiles = pb.num_m * pb.num_n * (pb.splits > 1 ? pb.splits : 1);
   if (tiles == 0) return QB_OK;
   if (pb.splits > pb.nk0 + pb.nk1)

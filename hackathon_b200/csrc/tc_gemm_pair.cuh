@@ -265,16 +265,7 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
   if ((B0 == tcg::kTmaKDual && !mB0b) || (B1 == tcg::kTmaKDual && !mB1b))
     return qb::fail(QB_ERR_INVALID, "%s: dual B needs its second tensor map", what);
   auto kernel = tc_gemm_pair_kernel<B0, B1, Epi>;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return qb::fail(QB_ERR_UNSUPPORTED, "%s: device %d", what, dev);
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess)
-      return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), kSmem, what)) return s;
   const int tiles = pb.num_m * pb.num_n;
   if (tiles == 0) return QB_OK;
   tc::Ctl ctl;

@@ -4,6 +4,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "qb_common.cuh"
 #include "tc_common.cuh"
@@ -156,6 +158,20 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uin
   if (r != CUDA_SUCCESS)
     return qb::fail(QB_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, box %u x %u",
                     (int)r, (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+  return QB_OK;
+}
+
+int ensure_smem(const void* kernel, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, void*>> done;   // (kernel, context) already raised
+  const auto key = std::make_pair(kernel, current_context_handle());
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return QB_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             bytes);
+  if (e != cudaSuccess)
+    return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
+  done.insert(key);
   return QB_OK;
 }
 

@@ -408,15 +408,7 @@ int launch_nf4(const CUtensorMap& mCodes, const CUtensorMap& mB0, const CUtensor
                const NfProblem& pb, const Nf4Operand& nf4, const LoraA& lora,
                const Epi& epi, cudaStream_t stream, const char* what) {
   auto kernel = tc_nf4_kernel<A0, Epi>;
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return qb::fail(QB_ERR_UNSUPPORTED, "%s: device %d", what, dev);
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e != cudaSuccess) return qb::fail(QB_ERR_CUDA, "%s: smem attribute: %s", what, cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), kSmem, what)) return s;
   const int tiles = pb.num_m * pb.num_n;
   if (tiles == 0) return QB_OK;
   int grid = tc_host::sm_count();
