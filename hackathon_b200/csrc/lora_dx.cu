@@ -178,23 +178,34 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
     const int row = quarter * 32 + lane;     // this thread's row of the tile
     const bool storer = threadIdx.x == 64;
     const int swz = row & 7;
+    // this row's 4 mask words of a tile (they depend on nothing in flight): fetched one tile
+    // ahead, so their load latency hides under the previous tile's epilogue
+    auto fetch_words = [&](int tile, uint32_t (&w)[BN / 32]) {
+      const int m = (tile % pb.num_m) * BM + row, n0 = (tile / pb.num_m) * BN;
+      const int64_t w0 = static_cast<int64_t>(m) * pb.ldbits + (n0 >> 5);
+      if (tile >= num_tiles || m >= pb.M) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) w[c] = 0u;
+      } else if (pb.bits_vec && (n0 >> 5) + 4 <= pb.ldbits) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(bits + w0));
+        w[0] = q.x; w[1] = q.y; w[2] = q.z; w[3] = q.w;
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          w[c] = (n0 >> 5) + c < pb.ldbits ? __ldg(bits + w0 + c) : 0u;
+      }
+    };
+    uint32_t next[BN / 32];
+    fetch_words(blockIdx.x, next);
     int i = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
       const int m0 = (tile % pb.num_m) * BM, n0 = (tile / pb.num_m) * BN;
       const int buf = i & 1, cb = i % kCBufs;
       const uint32_t par = (i >> 1) & 1, cpar = (i / kCBufs) & 1;
-      // the row's 4 mask words, fetched before the waits (they depend on nothing in flight)
-      const int m = m0 + row;
       uint32_t words[BN / 32];
-      const int64_t w0 = static_cast<int64_t>(m) * pb.ldbits + (n0 >> 5);
-      if (m < pb.M && pb.bits_vec && (n0 >> 5) + 4 <= pb.ldbits) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(bits + w0));
-        words[0] = q.x; words[1] = q.y; words[2] = q.z; words[3] = q.w;
-      } else {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          words[c] = (m < pb.M && (n0 >> 5) + c < pb.ldbits) ? __ldg(bits + w0 + c) : 0u;
-      }
+      for (int c = 0; c < BN / 32; ++c) words[c] = next[c];
+      fetch_words(tile + gridDim.x, next);
       const bool ready = tc::mbar_wait(&tfull[buf], par, err, 45) &&
                          tc::mbar_wait(&cfull[cb], cpar, err, 46);
       if (!__all_sync(0xffffffffu, ready)) break;   // warp-uniform: tcgen05.ld is collective

@@ -20,24 +20,29 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;  // words per thread per CTA
 
-template <bool NESTED>
+// SHIFT: the block sizes are powers of two and indices divide by shifting (bs2_shift =
+// log2(blocksize2)); a 64-bit division costs more than the dequantisation of a word.
+template <bool NESTED, bool SHIFT>
 __device__ __forceinline__ float block_scale(int64_t blk, const void* absmax, const float* s_code2,
-                                             const float* absmax2, float offset, int blocksize2) {
+                                             const float* absmax2, float offset, int blocksize2,
+                                             int bs2_shift) {
   if (NESTED) {
     const uint8_t q = static_cast<const uint8_t*>(absmax)[blk];
-    const float a2 = __ldg(absmax2 + blk / blocksize2);
+    const float a2 = __ldg(absmax2 + (SHIFT ? blk >> bs2_shift : blk / blocksize2));
     return __fadd_rn(__fmul_rn(s_code2[q], a2), offset);
   }
   return __ldg(static_cast<const float*>(absmax) + blk);
 }
 
-// One word = 4 packed bytes = 8 weights that share one scale block (blocksize % 8 == 0).
-template <typename OutT, bool NESTED>
+// One word = 4 packed bytes = 8 weights that share one scale block (blocksize % 8 == 0);
+// wpb_shift = log2(blocksize / 8) when SHIFT.
+template <typename OutT, bool NESTED, bool SHIFT>
 __global__ void __launch_bounds__(kThreads)
 nf4_dequant_word_kernel(const uint32_t* __restrict__ packed, int64_t n_words,
                         const void* __restrict__ absmax, const float* __restrict__ code2,
                         const float* __restrict__ absmax2, float offset, int blocksize,
-                        int blocksize2, const float* __restrict__ lut16, OutT* __restrict__ out) {
+                        int blocksize2, int wpb_shift, int bs2_shift,
+                        const float* __restrict__ lut16, OutT* __restrict__ out) {
   __shared__ float s_lut[16];
   __shared__ float s_code2[NESTED ? 256 : 1];
   if (threadIdx.x < 16) s_lut[threadIdx.x] = lut16[threadIdx.x];
@@ -56,8 +61,9 @@ nf4_dequant_word_kernel(const uint32_t* __restrict__ packed, int64_t n_words,
   for (int u = 0; u < kUnroll; ++u) {
     const int64_t i = base + u * kThreads;
     if (i >= n_words) break;
-    const int64_t blk = i / words_per_block;
-    const float scale = block_scale<NESTED>(blk, absmax, s_code2, absmax2, offset, blocksize2);
+    const int64_t blk = SHIFT ? i >> wpb_shift : i / words_per_block;
+    const float scale = block_scale<NESTED, SHIFT>(blk, absmax, s_code2, absmax2, offset,
+                                                   blocksize2, bs2_shift);
     float w[8];
     const uint32_t x = word[u];
 #pragma unroll
@@ -86,7 +92,8 @@ nf4_dequant_byte_kernel(const uint8_t* __restrict__ packed, int64_t n_bytes,
        i += static_cast<int64_t>(gridDim.x) * kThreads) {
     const uint32_t byte = packed[i];
     const int64_t blk = (2 * i) / blocksize;
-    const float scale = block_scale<NESTED>(blk, absmax, s_code2, absmax2, offset, blocksize2);
+    const float scale = block_scale<NESTED, false>(blk, absmax, s_code2, absmax2, offset,
+                                                   blocksize2, 0);
     out[2 * i] = qb::from_f<OutT>(__fmul_rn(s_lut[byte >> 4], scale));
     out[2 * i + 1] = qb::from_f<OutT>(__fmul_rn(s_lut[byte & 15u], scale));
   }
@@ -103,9 +110,22 @@ int launch_dequant(const uint8_t* packed, int64_t n_weights, const void* absmax,
     const int64_t n_words = n_bytes / 4;
     const int64_t grid = (n_words + kThreads * kUnroll - 1) / (kThreads * kUnroll);
     if (grid > 0x7fffffff) return qb::fail(QB_ERR_INVALID, "nf4_dequant: tensor too large");
-    nf4_dequant_word_kernel<OutT, NESTED><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
-        reinterpret_cast<const uint32_t*>(packed), n_words, absmax, code2, absmax2, offset,
-        blocksize, blocksize2, lut16, out);
+    const int wpb = blocksize / 8;
+    const bool pow2 = (wpb & (wpb - 1)) == 0 &&
+                      (!NESTED || (blocksize2 > 0 && (blocksize2 & (blocksize2 - 1)) == 0));
+    const int wpb_shift = __builtin_ctz(static_cast<unsigned>(wpb));
+    const int bs2_shift = NESTED && blocksize2 > 0 ? __builtin_ctz(static_cast<unsigned>(blocksize2))
+                                                   : 0;
+    const auto* pw = reinterpret_cast<const uint32_t*>(packed);
+    if (pow2)
+      nf4_dequant_word_kernel<OutT, NESTED, true><<<static_cast<unsigned>(grid), kThreads, 0,
+                                                    stream>>>(
+          pw, n_words, absmax, code2, absmax2, offset, blocksize, blocksize2, wpb_shift,
+          bs2_shift, lut16, out);
+    else
+      nf4_dequant_word_kernel<OutT, NESTED, false><<<static_cast<unsigned>(grid), kThreads, 0,
+                                                     stream>>>(
+          pw, n_words, absmax, code2, absmax2, offset, blocksize, blocksize2, 0, 0, lut16, out);
   } else {
     int64_t grid = (n_bytes + kThreads - 1) / kThreads;
     if (grid > 148 * 64) grid = 148 * 64;
