@@ -15,7 +15,8 @@
 // store: it hands a buffer back once the store issued after it has been read out.
 //
 // Roles (one CTA per SM, persistent over tiles): warp 0 TMA loads (operands, dx tiles),
-// warp 1 TMEM allocation + MMA issue, warps 2-5 epilogue (thread 64 also issues the stores).
+// warp 1 TMEM allocation + MMA issue, warps 2-9 epilogue, two per TMEM lane quarter, each
+// taking one 64-column slab of the rows (thread 64 also issues the stores).
 // Hand-offs are mbarriers only, every wait bounded (tc::mbar_wait): a wait that gives up raises
 // the device error flag, the roles drain their copies in flight and TMEM is released.
 #include "qb_common.cuh"
@@ -31,7 +32,9 @@ constexpr int kSlab = BM * 128;       // 16 KiB: 128 rows x 64 columns of dx
 constexpr int kSlabs = BN / 64;
 constexpr int kC = kSlabs * kSlab;    // 32 KiB: one dx tile
 constexpr int kCBufs = 4;             // dx tiles in the ring
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;          // two per TMEM lane quarter, each half of a row's columns
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kSmem = kStages * (kA + kB) + kCBufs * kC + 1024 /*barriers*/ + 1024 /*align*/;
 
 struct Problem {
@@ -70,12 +73,12 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
     for (int s = 0; s < kStages; ++s) { tc::mbar_init(&full[s], 1); tc::mbar_init(&empty[s], 1); }
     for (int b = 0; b < kCBufs; ++b) {
       tc::mbar_init(&cfull[b], 1);
-      tc::mbar_init(&cdone[b], 128);
+      tc::mbar_init(&cdone[b], kEpiThreads);
       tc::mbar_init(&cempty[b], 1);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
-      tc::mbar_init(&tempty[b], 128);
+      tc::mbar_init(&tempty[b], kEpiThreads);
     }
     tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
@@ -173,38 +176,40 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
       tc::mbar_wait_quiet(drain, 0);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2-5)
+    // ------------------------------------------------------------------ epilogue (warps 2-9)
     const int quarter = warp & 3;            // TMEM lanes this warp may read
+    const int half = (warp - 2) >> 2;        // which 64 of the tile's 128 columns (one slab)
     const int row = quarter * 32 + lane;     // this thread's row of the tile
     const bool storer = threadIdx.x == 64;
     const int swz = row & 7;
-    // this row's 4 mask words of a tile (they depend on nothing in flight): fetched one tile
-    // ahead, so their load latency hides under the previous tile's epilogue
-    auto fetch_words = [&](int tile, uint32_t (&w)[BN / 32]) {
-      const int m = (tile % pb.num_m) * BM + row, n0 = (tile / pb.num_m) * BN;
+    constexpr int kWords = BN / 64;          // mask words of a row's half tile
+    // this row's mask words of its half of a tile (they depend on nothing in flight): fetched
+    // one tile ahead, so their load latency hides under the previous tile's epilogue
+    auto fetch_words = [&](int tile, uint32_t (&w)[kWords]) {
+      const int m = (tile % pb.num_m) * BM + row, n0 = (tile / pb.num_m) * BN + half * 64;
       const int64_t w0 = static_cast<int64_t>(m) * pb.ldbits + (n0 >> 5);
       if (tile >= num_tiles || m >= pb.M) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) w[c] = 0u;
-      } else if (pb.bits_vec && (n0 >> 5) + 4 <= pb.ldbits) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(bits + w0));
-        w[0] = q.x; w[1] = q.y; w[2] = q.z; w[3] = q.w;
+        for (int c = 0; c < kWords; ++c) w[c] = 0u;
+      } else if (pb.bits_vec && (n0 >> 5) + kWords <= pb.ldbits) {
+        const uint2 q = __ldg(reinterpret_cast<const uint2*>(bits + w0));
+        w[0] = q.x; w[1] = q.y;
       } else {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
+        for (int c = 0; c < kWords; ++c)
           w[c] = (n0 >> 5) + c < pb.ldbits ? __ldg(bits + w0 + c) : 0u;
       }
     };
-    uint32_t next[BN / 32];
+    uint32_t next[kWords];
     fetch_words(blockIdx.x, next);
     int i = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
       const int m0 = (tile % pb.num_m) * BM, n0 = (tile / pb.num_m) * BN;
       const int buf = i & 1, cb = i % kCBufs;
       const uint32_t par = (i >> 1) & 1, cpar = (i / kCBufs) & 1;
-      uint32_t words[BN / 32];
+      uint32_t words[kWords];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) words[c] = next[c];
+      for (int c = 0; c < kWords; ++c) words[c] = next[c];
       fetch_words(tile + gridDim.x, next);
       const bool ready = tc::mbar_wait(&tfull[buf], par, err, 45) &&
                          tc::mbar_wait(&cfull[cb], cpar, err, 46);
@@ -213,10 +218,11 @@ lora_dx_kernel(const __grid_constant__ CUtensorMap mV, const __grid_constant__ C
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
       uint8_t* crow = cbuf + cb * kC + row * 128;
 #pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      for (int cc = 0; cc < kWords; ++cc) {
+        const int ch = half * kWords + cc;   // 32-column chunk of the tile
         float v[32];
         tc::tmem_ld32(taddr + ch * 32, v);
-        const uint32_t word = words[ch];
+        const uint32_t word = words[cc];
         uint8_t* slab_row = crow + (ch >> 1) * kSlab;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
