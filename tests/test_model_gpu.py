@@ -457,3 +457,29 @@ def test_adapter_shadow_matches_per_use_conversion(cuda):
         opt.zero_grad(set_to_none=True)
     assert torch.equal(out[0][0], out[1][0])
     assert torch.equal(out[0][1], out[1][1])
+
+
+def test_step_launches_no_library_gemm(cuda):
+    """One 7B-shaped training step (2 layers, the step's 4 x 4096 tokens) launches no cuBLAS /
+    cuBLASLt / CUTLASS GEMM: every matrix product - projections, their input gradients, the LoRA
+    products and weight gradients, the head - is one of this library's tcgen05 kernels. Kernel
+    names come from the CUDA activity of torch.profiler; attention stays on cuDNN's SDPA."""
+    from torch.profiler import ProfilerActivity, profile
+    from hackathon_b200.qlora import QwenQLoRA, make_optimizer, preset, synthetic_batch, \
+        train_step
+    shape = preset("7b", layers=2)
+    model = QwenQLoRA(shape, cuda, seed=0)
+    opt = make_optimizer(model)
+    ids, labels = synthetic_batch(shape, 4, 4096, cuda, seed=0)
+    train_step(model, opt, ids, labels)          # warm-up: workspaces, library handles
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        train_step(model, opt, ids, labels)
+        torch.cuda.synchronize()
+    names = {e.key for e in prof.key_averages() if e.device_time_total > 0}
+    ours = [n for n in names if "tc_gemm_kernel" in n]
+    assert ours, sorted(names)
+    library_gemms = [n for n in names if any(k in n.lower() for k in
+                                             ("cublas", "nvjet", "cutlass", "xmma", "gemv",
+                                              "splitkreduce", "sm100_gemm", "sm90_gemm"))]
+    assert not library_gemms, library_gemms
