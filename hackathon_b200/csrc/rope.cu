@@ -1,9 +1,9 @@
 // Rotate-half RoPE on q and k in one launch, forward and backward (solution/rope.py:25-62).
 //
-// One CTA per (batch, position) handles every q head and every k head of that position. A work
-// item is one chunk of 8 dims in the first half and the matching 8 dims of the second half of
-// one head: it reads x1, x2 (16-byte loads for 2-byte dtypes) and the cos/sin chunks, and writes
-// o1, o2. With (B,S,H,D) buffers seen as (B,H,S,D) — how the attention builds q and k — the
+// One CTA per (batch, position) - or per a few consecutive positions when a position has few
+// heads - handles every q head and every k head of that position. A work item is one chunk of 8
+// dims in the first half and the matching 8 dims of the second half of one head: it reads x1,
+// x2 (16-byte loads for 2-byte dtypes) and the cos/sin chunks, and writes o1, o2. With (B,S,H,D) buffers seen as (B,H,S,D) — how the attention builds q and k — the
 // heads of one position are contiguous, so a CTA's loads and stores cover whole cache lines.
 #include "qb_common.cuh"
 
@@ -25,19 +25,26 @@ __device__ __forceinline__ void st(T* p, const float* in) {
   else p[0] = qb::from_f<T>(in[0]);
 }
 
-template <typename QT, typename OT, typename CT, int VEC, bool BACKWARD>
+// A CTA takes `ppc` consecutive (batch, position) pairs, `span` threads each (ppc > 1 when a
+// position has few items, e.g. the 4 k heads: one CTA per position would leave 32-thread CTAs).
+template <typename QT, typename OT, typename CT, int VEC, bool BACKWARD, bool MULTI>
 __global__ void rope_qk_kernel(const QT* __restrict__ q, const QT* __restrict__ k,
                                OT* __restrict__ qo, OT* __restrict__ ko,
                                const CT* __restrict__ cosp, const CT* __restrict__ sinp, int S,
                                int HQ, int HK, int half, Strides3 sq, Strides3 sk, Strides3 sqo,
-                               Strides3 sko, int64_t csb, int64_t css) {
-  const int64_t pid = blockIdx.x;
+                               Strides3 sko, int64_t csb, int64_t css, int64_t npos, int ppc,
+                               int span) {
+  // MULTI: ppc positions of span threads each; else one position of blockDim.x threads
+  const int local = MULTI ? static_cast<int>(threadIdx.x) / span : 0;
+  const int64_t pid = MULTI ? static_cast<int64_t>(blockIdx.x) * ppc + local : blockIdx.x;
+  if (MULTI && pid >= npos) return;    // no barrier below
+  const int stride = MULTI ? span : static_cast<int>(blockDim.x);
   const int64_t b = pid / S, s = pid % S;
   const int chunks = half / VEC;
   const int items = (HQ + HK) * chunks;
   const CT* cb = cosp + b * csb + s * css;
   const CT* sb = sinp + b * csb + s * css;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+  for (int it = static_cast<int>(threadIdx.x) - local * span; it < items; it += stride) {
     const int head = it / chunks;
     const int d = (it % chunks) * VEC;
     float c1[VEC], c2[VEC], s1[VEC], s2[VEC];
@@ -89,10 +96,13 @@ int rope_typed(const void* q, const void* k, void* qo, void* ko, const void* c, 
                    (half * qs) % 16 == 0 && (half * os) % 16 == 0 && (half * cs) % 16 == 0;
   const int vecw = vec ? 8 : 1;
   const int64_t items = (HQ + HK) * (half / vecw);
-  int threads = static_cast<int>(((items + 31) / 32) * 32);
-  if (threads > 512) threads = 512;
-  if (threads < 32) threads = 32;
-  const dim3 grid(static_cast<unsigned>(B * S));
+  int span = static_cast<int>(((items + 31) / 32) * 32);
+  if (span > 512) span = 512;
+  if (span < 32) span = 32;
+  const int ppc = span >= 256 ? 1 : 256 / span;     // positions per CTA
+  const int threads = span * ppc;
+  const int64_t npos = B * S;
+  const dim3 grid(static_cast<unsigned>((npos + ppc - 1) / ppc));
   auto* qp = static_cast<const QT*>(q);
   auto* kp = static_cast<const QT*>(k);
   auto* qop = static_cast<OT*>(qo);
@@ -100,14 +110,22 @@ int rope_typed(const void* q, const void* k, void* qo, void* ko, const void* c, 
   auto* cp = static_cast<const CT*>(c);
   auto* sp = static_cast<const CT*>(s);
   const int Si = static_cast<int>(S), HQi = static_cast<int>(HQ), HKi = static_cast<int>(HK);
-#define QB_ROPE_LAUNCH(V, BW)                                                                    \
-  rope_qk_kernel<QT, OT, CT, V, BW><<<grid, threads, 0, stream>>>(qp, kp, qop, kop, cp, sp, Si, \
-                                                                  HQi, HKi, half, sq, sk, sqo,  \
-                                                                  sko, csb, css)
+#define QB_ROPE_LAUNCH(V, BW, M)                                                                  \
+  rope_qk_kernel<QT, OT, CT, V, BW, M><<<grid, threads, 0, stream>>>(                             \
+      qp, kp, qop, kop, cp, sp, Si, HQi, HKi, half, sq, sk, sqo, sko, csb, css, npos, ppc, span)
+  const bool multi = ppc > 1;
   if (vec) {
-    if (backward) QB_ROPE_LAUNCH(8, true); else QB_ROPE_LAUNCH(8, false);
+    if (backward) {
+      if (multi) QB_ROPE_LAUNCH(8, true, true); else QB_ROPE_LAUNCH(8, true, false);
+    } else {
+      if (multi) QB_ROPE_LAUNCH(8, false, true); else QB_ROPE_LAUNCH(8, false, false);
+    }
   } else {
-    if (backward) QB_ROPE_LAUNCH(1, true); else QB_ROPE_LAUNCH(1, false);
+    if (backward) {
+      if (multi) QB_ROPE_LAUNCH(1, true, true); else QB_ROPE_LAUNCH(1, true, false);
+    } else {
+      if (multi) QB_ROPE_LAUNCH(1, false, true); else QB_ROPE_LAUNCH(1, false, false);
+    }
   }
 #undef QB_ROPE_LAUNCH
   return qb::check_launch("rope_qk");

@@ -261,6 +261,31 @@ def test_rope_vs_oracle(cuda, dtype, shape):
         torch.testing.assert_close(a.cpu(), b.detach(), rtol=tol, atol=atol)
 
 
+@pytest.mark.parametrize("heads", [4, 1, 28])
+@pytest.mark.parametrize("backward", [False, True])
+def test_rope_rows_few_heads(cuda, heads, backward):
+    """rope_rows (the step's RoPE on projection outputs laid out as token rows) with few heads
+    per position - several positions per CTA, the last CTA's positions running past the row
+    count - against the rotation and its transpose computed in fp32 on the host."""
+    from hackathon_b200.rope import rope_rows
+    B, S, D = 3, 37, 128
+    torch.manual_seed(heads)
+    x2 = torch.randn(B * S, heads * D, device=cuda).to(torch.bfloat16)
+    cos, sin = ops_ref.qwen_cos_sin(1, S, D, dtype=torch.bfloat16)
+    cos, sin = cos[0].to(cuda), sin[0].to(cuda)
+    out = rope_rows(x2, cos, sin, backward=backward)
+    q = x2.view(B, S, heads, D).transpose(1, 2).float().cpu()
+    c, s_ = cos.float().cpu()[None, None], sin.float().cpu()[None, None]
+    x1, xh = q[..., :D // 2], q[..., D // 2:]
+    c1, c2, s1, s2 = c[..., :D // 2], c[..., D // 2:], s_[..., :D // 2], s_[..., D // 2:]
+    if backward:
+        ref = torch.cat([x1 * c1 + xh * s2, xh * c2 - x1 * s1], -1)
+    else:
+        ref = torch.cat([x1 * c1 - xh * s1, xh * c2 + x1 * s2], -1)
+    ref = ref.transpose(1, 2).reshape(B * S, heads * D)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=1.6e-2, atol=BF16_ATOL)
+
+
 # ----------------------------------------------------------------------------------- SwiGLU
 
 @pytest.mark.parametrize("i", range(2))
