@@ -48,7 +48,7 @@ WORKLOADS = {
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the dominant kernel,
 # from ncu captures of each of its launch shapes in the step, averaged over the step's launch mix.
 # Keyed by --config.
-TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1793e6, "qb_gemm_gateup_swiglu": 4211e6}}
+TRAFFIC_PER_LAUNCH = {"7b": {"qb_gemm2_bf16": 1793e6, "qb_gemm_gateup_swiglu": 4207e6}}
 TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the one-CTA tcgen05 GEMM "
                   "(the kernel the step runs) at the step's launch shapes")
 
