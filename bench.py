@@ -328,7 +328,8 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant",
+KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_fwd_dequant", "nf4_dgrad_fused",
+           "nf4_dequant",
            "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "rmsnorm_bwd",
            "rope_bwd", "linear_ce", "mask_acc", "gateup_swiglu", "gemm2_dgrad_pair",
            "gemm2_rope", "dropout_bits", "lora_xa", "lora_xa_xd", "lora_grads")
@@ -359,7 +360,8 @@ def kernel_case(args):
 
     name = args.kernel
     flops, nbytes, draws = 0, 0, 0
-    if name in ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_dgrad_fused", "nf4_dequant"):
+    if name in ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_fwd_dequant", "nf4_dgrad_fused",
+                "nf4_dequant"):
         packed, st = nf4m.quantize_nf4(rnd(fo, fi, s=0.02))
         w = nf4m.dequantize_nf4(packed, st, torch.bfloat16)
         if name == "gemm2":
@@ -373,6 +375,11 @@ def kernel_case(args):
         elif name == "nf4_fwd_fused":
             x, u, sb = rnd(T, fi), rnd(T, r), rnd(fo, r, s=0.05)
             fn = lambda: nf4m.nf4_linear_fwd(x, packed, st, None, u, sb, path="fused")  # noqa
+            flops = 2 * T * fo * (fi + r)
+        elif name == "nf4_fwd_dequant":
+            # the same projection on the long-token path: transient bf16 W, then the TMA GEMM
+            x, u, sb = rnd(T, fi), rnd(T, r), rnd(fo, r, s=0.05)
+            fn = lambda: nf4m.nf4_linear_fwd(x, packed, st, None, u, sb, path="dequant")  # noqa
             flops = 2 * T * fo * (fi + r)
         elif name == "nf4_dgrad_fused":
             dy = rnd(T, fo)

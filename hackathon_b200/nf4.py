@@ -235,7 +235,13 @@ def _rows2d(t):
 # of the fused kernel. The fused kernel reads 0.5 byte per weight but its thread-written operand
 # caps it near 1 PFLOP/s; the TMA-fed GEMM runs at 1.1-1.4 PFLOP/s and the rebuild costs one
 # streaming pass over the weight (tens of microseconds), so long token counts win by 10-40%.
-DEQUANT_GEMM_MIN_TOKENS = 8192
+# From this many rows on, a projection rebuilds W into a transient bf16 buffer and runs the
+# TMA-fed GEMM; below, the fused kernel rebuilds W inside the GEMM. Measured (forward with the
+# rank-64 LoRA term, `bench.py --kernel nf4_fwd_fused / nf4_fwd_dequant`): at 18944 x 3584 the
+# fused kernel wins at 512 rows (79 against 103 us) and ties at 1024, the transient weight wins
+# from 2048 on (0.25 against 0.30 ms; 1.29 against 1.00 PFLOP/s at 8192 rows); at 3584 x 3584
+# the transient weight wins at every size measured.
+DEQUANT_GEMM_MIN_TOKENS = 2048
 
 _WEIGHT_WS = {}
 
