@@ -122,15 +122,19 @@ def test_masks_drawn_ahead_give_the_same_step(cuda):
     assert torch.equal(out[0][1], out[1][1])
 
 
-def test_decoder_layer_matches_eager_oracle(cuda):
+@pytest.mark.parametrize("name,S", [("0.5b", 64), ("1.5b", 2048)])
+def test_decoder_layer_matches_eager_oracle(cuda, name, S):
     """One decoder layer (dropout off): GPU ops vs the eager CPU oracle with the same NF4
-    bytes, bf16 activations; forward and the LoRA-A gradient within bf16 tolerance."""
+    bytes, bf16 activations; forward and the LoRA-A gradient within bf16 tolerance. 0.5B shapes
+    at 64 tokens (the fused NF4 kernel, RoPE as its own kernel for 64-dim heads); 1.5B shapes
+    (SURVEY Cfg4: 12 / 2 heads of 128) at 2048 tokens (transient weights, RoPE in the q / k
+    GEMM epilogue)."""
     from hackathon_b200.qlora import DecoderLayer, preset
     from oracle import ops_ref
-    shape = preset("0.5b", layers=1, lora_dropout=0.0)
+    shape = preset(name, layers=1, lora_dropout=0.0)
     gen = torch.Generator(device=cuda).manual_seed(0)
     layer = DecoderLayer(shape, cuda, gen)
-    B, S = 1, 64
+    B = 1
     torch.manual_seed(0)
     h = (torch.randn(B, S, shape.hidden) * 0.5).to(torch.bfloat16)
     cos, sin = ops_ref.qwen_cos_sin(1, S, shape.head_dim, shape.theta, torch.bfloat16)
@@ -166,7 +170,13 @@ def test_decoder_layer_matches_eager_oracle(cuda):
     ref.backward(gout.cpu())
     torch.testing.assert_close(out.detach().float().cpu(), ref.detach().float(), rtol=5e-2,
                                atol=5e-2)
-    torch.testing.assert_close(hg.grad.float().cpu(), hr.grad.float(), rtol=5e-2, atol=5e-2)
+    # the input gradient runs through every projection's backward, attention and two norms, each
+    # side rounding to bf16 in its own order: elementwise at the same tolerance except for a
+    # 1e-4 fraction of outliers, and within 2 % in norm
+    got, want = hg.grad.float().cpu(), hr.grad.float()
+    outside = ((got - want).abs() > 5e-2 + 5e-2 * want.abs()).float().mean()
+    assert float(outside) < 1e-4, float(outside)
+    assert float((got - want).norm() / want.norm()) < 2e-2
     ga = layer.down.lora_B.grad.cpu()
     gr = t["down"].lora_b.grad
     rel = (ga - gr).norm() / gr.norm()
