@@ -9,6 +9,7 @@
 // ahead as bits (qb_dropout_bits) and applied later (qb_dropout_apply), or drawn and applied in
 // one pass that also records the bits (qb_dropout_mask).
 #include "qb_common.cuh"
+#include "philox.cuh"
 
 namespace tc_host {
 int sm_count();   // tc_host.cu: SMs of the current device (cached)
@@ -18,55 +19,9 @@ namespace {
 
 constexpr int kThreads = 256;
 
-__device__ __forceinline__ uint32_t philox_first_word(uint32_t c0, uint32_t k0, uint32_t k1) {
-  uint32_t c1 = 0, c2 = 0, c3 = 0;
-  const uint32_t mA = 0xD2511F53u, mB = 0xCD9E8D57u;  // round multipliers
-  const uint32_t wA = 0x9E3779B9u, wB = 0xBB67AE85u;  // key increments (Weyl sequence)
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint32_t hiB = __umulhi(mB, c2), loB = mB * c2;
-    const uint32_t hiA = __umulhi(mA, c0), loA = mA * c0;
-    const uint32_t n0 = hiB ^ c1 ^ k0;
-    const uint32_t n2 = hiA ^ c3 ^ k1;
-    c0 = n0;
-    c1 = loB;
-    c2 = n2;
-    c3 = loA;
-    k0 += wA;
-    k1 += wB;
-  }
-  return c0;
-}
-
-// The reference keeps an element when uniform(w) > p, with uniform(w) = fl(fl(x) * 2^-31-ish),
-// x = w as int32 folded onto [0, 2^31) (x < 0 -> -x - 1). uniform is non-decreasing in x, so the
-// test is x > T for one integer T per call (keep_threshold, host side, same IEEE single
-// operations): the kernels compare integers and never convert to float.
-constexpr float kUniformScale = 4.6566127342e-10f;
-
-__device__ __forceinline__ bool keep_of(uint32_t w, int32_t thresh) {
-  const int32_t x = static_cast<int32_t>(w ^ static_cast<uint32_t>(static_cast<int32_t>(w) >> 31));
-  return x > thresh;
-}
-
-// Largest x in [0, 2^31) with fl(fl(x) * kUniformScale) <= p, or -1 when there is none
-// (p below every uniform: everything kept). Bisection over a non-decreasing function.
-int32_t keep_threshold(float p) {
-  auto u = [](int32_t x) {
-    volatile float f = static_cast<float>(x);   // round to nearest, as __int2float_rn
-    volatile float r = f * kUniformScale;       // round to nearest, as __fmul_rn
-    return static_cast<float>(r);
-  };
-  if (!(u(0) <= p)) return -1;
-  int32_t lo = 0, hi = 0x7fffffff;              // u(lo) <= p
-  if (u(hi) <= p) return hi;                    // nothing kept
-  while (hi - lo > 1) {                         // u(hi) > p
-    const int32_t mid = lo + (hi - lo) / 2;
-    if (u(mid) <= p) lo = mid;
-    else hi = mid;
-  }
-  return lo;
-}
+using qb::keep_of;
+using qb::keep_threshold;
+using qb::philox_first_word;
 
 template <typename IT, typename OT, bool DROP, int VEC>
 __global__ void __launch_bounds__(kThreads)
@@ -236,16 +191,7 @@ dropout_bits_kernel(uint32_t* __restrict__ bits, int64_t words, int64_t rows, in
     const int64_t row = t / words, w = t % words;
     const int64_t c0 = w * 32;
     const int n = cols - c0 < 32 ? static_cast<int>(cols - c0) : 32;
-    const uint32_t off0 = static_cast<uint32_t>(row * cols + c0);  // int32 wrap, as the reference
-    uint32_t word = 0;
-    if (n == 32) {
-#pragma unroll 8
-      for (int j = 0; j < 32; ++j)
-        word |= static_cast<uint32_t>(keep_of(philox_first_word(off0 + j, k0, k1), thresh)) << j;
-    } else {
-      for (int j = 0; j < n; ++j)
-        word |= static_cast<uint32_t>(keep_of(philox_first_word(off0 + j, k0, k1), thresh)) << j;
-    }
+    const uint32_t word = qb::mask_word(row, cols, c0, n, k0, k1, thresh);
     bits[t] = word;
   }
 }
