@@ -62,6 +62,9 @@ BOUND = {"qb_nf4_dequant": "hbm", "qb_rmsnorm_fwd": "hbm", "qb_rmsnorm_bwd": "hb
          "qb_linear_ce_grad": "tensor", "qb_linear_ce_stats_logits": "tensor",
          "qb_ce_grad_from_logits": "hbm", "qb_gemm_bf16_mask_acc": "hbm",
          "qb_gemm_gateup_swiglu": "tensor", "qb_gemm2_rope_bf16": "tensor",
+         # the forward's gate/up GEMM with the next masks drawn in its side warps: its flops are
+         # the GEMM's (the Philox rounds it also runs are counted under no roofline)
+         "qb_gemm_gateup_swiglu_masks": "tensor",
          "qb_dropout_mask": "hbm", "qb_dropout_apply": "hbm",
          # integer-pipe work (Philox rounds), counted in mask elements drawn: no HBM or tensor
          # roofline applies; on a side stream its events span the GEMMs it shares the SMs with

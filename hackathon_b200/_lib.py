@@ -62,6 +62,9 @@ _SIGNATURES = {
                            _p, _i64, _i64, _i64, _i64, _i64, _p],
     "qb_gemm_gateup_swiglu": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _p,
                               _i64, _p, _p, _i64, _i64, _i64, _p],
+    "qb_gemm_gateup_swiglu_masks": [_p, _i64, _p, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64,
+                                    _p, _i64, _p, _p, _i64, _i64, _i64, _p, _i32, _p],
+    "qb_mask_job_size": [],
     "qb_gemm_bf16_mask_acc": [_p, _i64, _p, _i64, _i32, _p, _i64, _f32, _p, _i64, _i64, _i64,
                               _i64, _p],
     "qb_nf4_linear_fwd": [_p, _i64, _p, _p, _p, _p, _f32, _i32, _p, _i64, _i64, _i64, _p, _p,
@@ -81,7 +84,7 @@ _RESTYPE = {"qb_last_error": ctypes.c_char_p, "qb_nf4_double_quant_workspace": c
             "qb_nf4_double_quant_noalloc_max_blocks": ctypes.c_int64,
             "qb_linear_ce_vocab_tiles": ctypes.c_int64,
             "qb_gemm_bf16_acc_f32_workspace": ctypes.c_int64,
-            "qb_pack_segment_size": ctypes.c_int64}
+            "qb_pack_segment_size": ctypes.c_int64, "qb_mask_job_size": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib = None

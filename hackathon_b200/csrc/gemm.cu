@@ -654,13 +654,49 @@ extern "C" int qb_gemm2_bf16(const void* A0, int64_t lda0, int a0_mn_major, cons
                                                  vec, stream, what, mpp);
 }
 
-extern "C" int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_gate,
-                                     const void* w_up, int64_t ldw, int64_t K0, const void* u1,
-                                     int64_t ldu1, const void* b1_gate, const void* b1_up,
-                                     int64_t ldb1, int64_t K1, void* h, int64_t ldh,
-                                     void* g_out, void* u_out, int64_t ldgu, int64_t M,
-                                     int64_t I, cudaStream_t stream) {
-  const char* what = "gemm_gateup_swiglu";
+namespace {
+
+// Mask jobs of the C-ABI -> the kernel's side work (words, thresholds and each job's first word
+// in the launch's word space).
+int side_work(const qb_mask_job* jobs, int njobs, tcg::SideWork* side, const char* what) {
+  if (njobs < 0 || njobs > tcg::kMaxMaskJobs || (njobs > 0 && !jobs))
+    return qb::fail(QB_ERR_INVALID, "%s: 0..%d mask jobs", what, tcg::kMaxMaskJobs);
+  *side = tcg::SideWork{};
+  int64_t total = 0;
+  for (int i = 0; i < njobs; ++i) {
+    const qb_mask_job& j = jobs[i];
+    if (j.rows < 0 || j.cols <= 0 || j.rows > (int64_t(1) << 31) || j.cols > (int64_t(1) << 31))
+      return qb::fail(QB_ERR_INVALID, "%s: mask job %d: bad shape", what, i);
+    if (!(j.p < 1.0f)) return qb::fail(QB_ERR_INVALID, "%s: mask job %d: p must be < 1", what, i);
+    if (!j.bits || reinterpret_cast<uintptr_t>(j.bits) % 4)
+      return qb::fail(QB_ERR_INVALID, "%s: mask job %d: bits must be 4-byte aligned", what, i);
+    tcg::MaskJob& m = side->job[side->njobs++];
+    m.bits = j.bits;
+    m.rows = j.rows;
+    m.cols = j.cols;
+    m.words = (j.cols + 31) / 32;
+    m.k0 = static_cast<uint32_t>(j.seed & 0xffffffffu);
+    m.k1 = static_cast<uint32_t>(j.seed >> 32);
+    m.thresh = qb::keep_threshold(j.p);
+    m.first = total;
+    total += j.rows * m.words;
+  }
+  side->total = total;
+  return QB_OK;
+}
+
+// Side warps beside the GEMM's six: the 7B forward's seven masks (0.66 G Philox draws, 1.8 ms
+// as their own launches) add 1.2 ms to the 3.3 ms gate/up GEMM with 8 side warps and 0.7-0.9 ms
+// with 4 to 6 (the SMs share the power cap, so the draws are not free; fewer warps take fewer
+// issue slots from the GEMM's producer, MMA and epilogue warps).
+constexpr int kSideWarps = 6;
+
+int gateup_swiglu(const void* x, int64_t ldx, const void* w_gate, const void* w_up, int64_t ldw,
+                  int64_t K0, const void* u1, int64_t ldu1, const void* b1_gate,
+                  const void* b1_up, int64_t ldb1, int64_t K1, void* h, int64_t ldh, void* g_out,
+                  void* u_out, int64_t ldgu, int64_t M, int64_t I, const tcg::SideWork* side,
+                  cudaStream_t stream) {
+  const char* what = side ? "gemm_gateup_swiglu_masks" : "gemm_gateup_swiglu";
   if (M < 0 || I < 0 || K0 <= 0 || K1 < 0 || M > (1 << 30) || I > (1 << 29) || K0 > (1 << 30) ||
       K1 > (1 << 30))
     return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
@@ -694,11 +730,39 @@ extern "C" int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_g
                 static_cast<__nv_bfloat16*>(u_out), ldgu, static_cast<int>(M), static_cast<int>(I),
                 vec};
   using namespace tcg;
+  if (side)
+    return launch<kTmaK, kTmaKDual, kTmaK, kTmaKDual, kBN, EpiSwiGLU, kSideWarps>(
+        m[0], m[1], m[2], m[3], pb, epi, stream, what, &mb0b, &mb1b, *side);
   if (use_pair(true, M, 2 * halves * kHalf))   // the dual maps already have 128-row boxes
     return tcp::launch<kTmaKDual, kTmaKDual>(m[0], m[1], m[2], m[3], pair_problem(pb), epi, stream,
                                              what, &mb0b, &mb1b);
   return launch<kTmaK, kTmaKDual, kTmaK, kTmaKDual, kBN>(m[0], m[1], m[2], m[3], pb, epi, stream,
                                                          what, &mb0b, &mb1b);
+}
+
+}  // namespace
+
+extern "C" int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_gate,
+                                     const void* w_up, int64_t ldw, int64_t K0, const void* u1,
+                                     int64_t ldu1, const void* b1_gate, const void* b1_up,
+                                     int64_t ldb1, int64_t K1, void* h, int64_t ldh,
+                                     void* g_out, void* u_out, int64_t ldgu, int64_t M,
+                                     int64_t I, cudaStream_t stream) {
+  return gateup_swiglu(x, ldx, w_gate, w_up, ldw, K0, u1, ldu1, b1_gate, b1_up, ldb1, K1, h, ldh,
+                       g_out, u_out, ldgu, M, I, nullptr, stream);
+}
+
+extern "C" int64_t qb_mask_job_size(void) { return sizeof(qb_mask_job); }
+
+extern "C" int qb_gemm_gateup_swiglu_masks(
+    const void* x, int64_t ldx, const void* w_gate, const void* w_up, int64_t ldw, int64_t K0,
+    const void* u1, int64_t ldu1, const void* b1_gate, const void* b1_up, int64_t ldb1,
+    int64_t K1, void* h, int64_t ldh, void* g_out, void* u_out, int64_t ldgu, int64_t M,
+    int64_t I, const qb_mask_job* jobs, int njobs, cudaStream_t stream) {
+  tcg::SideWork side;
+  if (int s = side_work(jobs, njobs, &side, "gemm_gateup_swiglu_masks")) return s;
+  return gateup_swiglu(x, ldx, w_gate, w_up, ldw, K0, u1, ldu1, b1_gate, b1_up, ldb1, K1, h, ldh,
+                       g_out, u_out, ldgu, M, I, njobs > 0 ? &side : nullptr, stream);
 }
 
 extern "C" int qb_gemm2_rope_bf16(const void* A0, int64_t lda0, const void* B0, int64_t ldb0,

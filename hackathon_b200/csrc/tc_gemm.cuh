@@ -20,6 +20,9 @@
 
 #include "qb_common.cuh"
 #include "tc_common.cuh"
+#include "philox.cuh"
+
+#include <type_traits>
 
 namespace tcg {
 
@@ -81,12 +84,53 @@ struct Cfg {
 
 constexpr bool is_mn(int s) { return s == kTmaMN; }
 
-template <int A0, int B0, int A1, int B1, int BN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
+// Side work for warps past the GEMM's six: dropout-mask words (the Philox stream of philox.cuh)
+// drawn on the integer pipes while the tensor cores run the product. The jobs' words form one
+// index space (job j owns [first, first + rows * words)); the side warps stride over it with the
+// whole grid and never wait on the GEMM's barriers, so they only meet the other warps at the
+// block's entry and exit.
+struct MaskJob {
+  uint32_t* bits;       // [rows, words]: bit (c & 31) of word c / 32 keeps column c
+  int64_t rows, cols, words;
+  uint32_t k0, k1;      // the seed's low and high words
+  int32_t thresh;       // keep when the folded Philox word is above this (qb::keep_threshold)
+  int64_t first;
+};
+constexpr int kMaxMaskJobs = 8;
+struct SideWork {
+  int njobs;
+  int64_t total;
+  MaskJob job[kMaxMaskJobs];
+};
+struct NoSide {};
+template <int SIDE>
+using SideArg = typename std::conditional<SIDE == 0, NoSide, SideWork>::type;
+
+template <int SIDE>
+__device__ __forceinline__ void side_masks(const SideArg<SIDE>& side, int side_thread) {
+  if constexpr (SIDE > 0) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * (SIDE * 32);
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * (SIDE * 32) + side_thread; t < side.total;
+         t += stride) {
+      int j = 0;
+      while (j + 1 < side.njobs && t >= side.job[j + 1].first) ++j;
+      const MaskJob& jb = side.job[j];
+      const int64_t local = t - jb.first;
+      const int64_t row = local / jb.words, w = local - row * jb.words;
+      const int64_t c0 = w * 32;
+      const int n = jb.cols - c0 < 32 ? static_cast<int>(jb.cols - c0) : 32;
+      jb.bits[local] = qb::mask_word(row, jb.cols, c0, n, jb.k0, jb.k1, jb.thresh);
+    }
+  }
+}
+
+template <int A0, int B0, int A1, int B1, int BN, class Epi, int SIDE = 0>
+__global__ void __launch_bounds__(kThreads + 32 * SIDE, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mB0,
                const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mB1,
                const __grid_constant__ CUtensorMap mB0b, const __grid_constant__ CUtensorMap mB1b,
-               const Problem pb, Epi epi, const tc::Ctl ctl) {
+               const Problem pb, Epi epi, const tc::Ctl ctl,
+               const __grid_constant__ SideArg<SIDE> side) {
   using C = Cfg<BN>;
   int* err = ctl.err;
   tc::trace_begin(ctl);
@@ -225,7 +269,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       tc::mma_commit(drain);
       tc::mbar_wait_quiet(drain, 0);
     }
-  } else {
+  } else if (warp < kThreads / 32) {
     // ---------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may read
     const int row = quarter * 32 + lane;
@@ -249,6 +293,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       tc::fence_before_sync();
       tc::mbar_arrive(&tempty[buf]);
     }
+  } else {
+    // ---------------------------------------------------------------- side warps
+    side_masks<SIDE>(side, threadIdx.x - kThreads);
   }
 
   // ------------------------------------------------------------------ teardown
@@ -262,14 +309,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
 }
 
 // Host: one launch of the kernel above on a persistent grid.
-template <int A0, int B0, int A1, int B1, int BN, class Epi>
+template <int A0, int B0, int A1, int B1, int BN, class Epi, int SIDE = 0>
 int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA1,
            const CUtensorMap& mB1, const Problem& pb, const Epi& epi, cudaStream_t stream,
            const char* what, const CUtensorMap* mB0b = nullptr,
-           const CUtensorMap* mB1b = nullptr) {
+           const CUtensorMap* mB1b = nullptr, const SideArg<SIDE>& side = SideArg<SIDE>{}) {
   static_assert(B0 != kTmaKDual || BN % 2 == 0, "dual B splits the tile in halves");
   using C = Cfg<BN>;
-  auto kernel = tc_gemm_kernel<A0, B0, A1, B1, BN, Epi>;
+  auto kernel = tc_gemm_kernel<A0, B0, A1, B1, BN, Epi, SIDE>;
   if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), C::SMEM, what)) return s;
   const int tiles = pb.num_m * pb.num_n * (pb.splits > 1 ? pb.splits : 1);
   if (tiles == 0) return QB_OK;
@@ -281,8 +328,8 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
     return qb::fail(QB_ERR_INVALID, "%s: dual B needs its second tensor map", what);
   tc::Ctl ctl;
   if (int s = tc_host::launch_ctl(&ctl, what)) return s;
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
-                                              mB1b ? *mB1b : mB1, pb, epi, ctl);
+  kernel<<<grid, kThreads + 32 * SIDE, C::SMEM, stream>>>(mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
+                                                         mB1b ? *mB1b : mB1, pb, epi, ctl, side);
   return qb::check_launch(what);
 }
 

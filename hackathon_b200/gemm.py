@@ -1,5 +1,7 @@
 """bf16 GEMM on the tcgen05 kernel (C-ABI qb_gemm_bf16), for the contractions of the step."""
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -167,10 +169,36 @@ def gemm2_rope(a0, b0_t, a1, b1_t, cos, sin, bias=None):
     return out
 
 
-def gemm_gateup_swiglu(x, w_gate, w_up, lora_u=None, b1_gate=None, b1_up=None, save_gu=False):
+class MaskJob(ctypes.Structure):
+    """qb_mask_job: one dropout mask drawn as bits [rows, ceil(cols / 32)] int32 words."""
+    _fields_ = [("bits", ctypes.c_void_p), ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+                ("seed", ctypes.c_uint64), ("p", ctypes.c_float)]
+
+
+MAX_MASK_JOBS = 8
+
+
+def mask_jobs_array(jobs):
+    """A qb_mask_job array of (bits, rows, cols, seed, p) tuples; bits an int32 CUDA tensor of
+    [rows, ceil(cols / 32)] contiguous words."""
+    if len(jobs) > MAX_MASK_JOBS:
+        raise ValueError(f"at most {MAX_MASK_JOBS} mask jobs per launch")
+    arr = (MaskJob * max(len(jobs), 1))()
+    for i, (bits, rows, cols, seed, p) in enumerate(jobs):
+        if (bits.dtype != torch.int32 or not bits.is_contiguous()
+                or bits.shape != (rows, (cols + 31) // 32)):
+            raise ValueError("mask job: bits must be contiguous int32 [rows, ceil(cols / 32)]")
+        arr[i] = MaskJob(bits.data_ptr(), rows, cols, int(seed) & 0xFFFFFFFFFFFFFFFF, float(p))
+    return arr
+
+
+def gemm_gateup_swiglu(x, w_gate, w_up, lora_u=None, b1_gate=None, b1_up=None, save_gu=False,
+                       mask_jobs=None):
     """h = silu(g) * u for the gate/up pair in one tcgen05 GEMM (C-ABI qb_gemm_gateup_swiglu):
     g = x @ w_gate.T (+ lora_u @ b1_gate.T), u = x @ w_up.T (+ lora_u @ b1_up.T), rounded to bf16
-    before the SwiGLU. Returns h, or (h, g, u) with save_gu. All bf16, row-major."""
+    before the SwiGLU. Returns h, or (h, g, u) with save_gu. All bf16, row-major.
+    mask_jobs: up to 8 (bits, rows, cols, seed, p) dropout masks the same launch draws as bits
+    in warps beside the GEMM's (qb_gemm_gateup_swiglu_masks); the bits equal dropout_bits'."""
     _lib.require_cuda(x, w_gate, w_up, what="gemm_gateup_swiglu")
     M, K0 = x.shape
     I, K0w = w_gate.shape
@@ -191,10 +219,16 @@ def gemm_gateup_swiglu(x, w_gate, w_up, lora_u=None, b1_gate=None, b1_up=None, s
     g = u = None
     if save_gu:
         g, u = torch.empty_like(h), torch.empty_like(h)
-    _lib.call("qb_gemm_gateup_swiglu", x.data_ptr(), x.stride(0), w_gate.data_ptr(),
-              w_up.data_ptr(), w_gate.stride(0), K0, up_, ldu1, bg, bu, ldb1, K1, h.data_ptr(),
-              h.stride(0), _lib.ptr(g), _lib.ptr(u), I, M, I, _lib.stream(x.device),
-              work=(0, 2 * M * 2 * I * (K0 + K1)))
+    args = (x.data_ptr(), x.stride(0), w_gate.data_ptr(), w_up.data_ptr(), w_gate.stride(0), K0,
+            up_, ldu1, bg, bu, ldb1, K1, h.data_ptr(), h.stride(0), _lib.ptr(g), _lib.ptr(u), I,
+            M, I)
+    if mask_jobs:
+        _lib.require_cuda(*(j[0] for j in mask_jobs), what="gemm_gateup_swiglu")
+        _lib.call("qb_gemm_gateup_swiglu_masks", *args, mask_jobs_array(mask_jobs),
+                  len(mask_jobs), _lib.stream(x.device), work=(0, 2 * M * 2 * I * (K0 + K1)))
+    else:
+        _lib.call("qb_gemm_gateup_swiglu", *args, _lib.stream(x.device),
+                  work=(0, 2 * M * 2 * I * (K0 + K1)))
     return (h, g, u) if save_gu else h
 
 

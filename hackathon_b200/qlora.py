@@ -106,6 +106,22 @@ def prefetch_masks(layer, seed, rows, device):
     return ev
 
 
+def gemm_mask_jobs(pairs, rows, device):
+    """Allocates the bits of the (projection, seed) masks that are not drawn yet, enters them in
+    MASKS and returns them as qb_mask_job tuples for the gate/up GEMM that draws them in its side
+    warps (the GEMM runs on the current stream before any projection reads the bits)."""
+    jobs = []
+    for mod, sd in pairs:
+        key = (id(mod), sd)
+        if (mod.training and mod.p > 0 and mod.fused and mod.in_features % 8 == 0
+                and key not in MASKS):
+            bits = torch.empty((rows, (mod.in_features + 31) // 32), dtype=torch.int32,
+                               device=device)
+            MASKS[key] = bits
+            jobs.append((bits, rows, mod.in_features, sd, mod.p))
+    return jobs
+
+
 def _mask_bits(x2, mod, p, seed):
     """The step's mask bits for (mod, seed) over x2's shape: drawn ahead (prefetch_masks) or
     drawn now (mask only, no data pass)."""
@@ -182,7 +198,8 @@ class GateUpSwiGLU(torch.autograd.Function):
     The recompute keeps the two rebuilt bf16 weights for the backward of the same layer."""
 
     @staticmethod
-    def forward(ctx, x, a_g, b_g, a_u, b_u, gate, up, p, seed_g, seed_u, save_gu):
+    def forward(ctx, x, a_g, b_g, a_u, b_u, gate, up, p, seed_g, seed_u, save_gu,
+                mask_jobs=None):
         from .gemm import gemm_gateup_swiglu
         from .nf4 import _weight_workspace, dequantize_nf4
         x2 = x.reshape(-1, x.shape[-1])
@@ -215,11 +232,12 @@ class GateUpSwiGLU(torch.autograd.Function):
         kept = (ws[0], ws[1]) if keep_w else \
             ((empty, empty) if ctx.needs_input_grad[0] else (None, None))
         if save_gu:
-            h, g, u = gemm_gateup_swiglu(x2, ws[0], ws[1], lora_u, b1_g, b1_u, save_gu=True)
+            h, g, u = gemm_gateup_swiglu(x2, ws[0], ws[1], lora_u, b1_g, b1_u, save_gu=True,
+                                         mask_jobs=mask_jobs)
         else:
             # the activation checkpoint's first pass: what it saves is discarded and the
             # recompute's tensors are unpacked in the same slots, so empty placeholders do
-            h = gemm_gateup_swiglu(x2, ws[0], ws[1], lora_u, b1_g, b1_u)
+            h = gemm_gateup_swiglu(x2, ws[0], ws[1], lora_u, b1_g, b1_u, mask_jobs=mask_jobs)
             g = u = empty
         ctx.save_for_backward(xd_g, xd_u, u_g, u_u, a_g, b_g, a_u, b_u, bits_g, bits_u,
                               kept[0], kept[1], g, u)
@@ -266,7 +284,7 @@ class GateUpSwiGLU(torch.autograd.Function):
             else:   # no mask: both adapter terms as one more tcgen05 GEMM over dx in place
                 gemm2(v_g, a16_g.t(), v_u, a16_u.t(), out=dx, residual=dx)
             dx = dx.view(ctx.shape)
-        return dx, da_g, db_g, da_u, db_u, None, None, None, None, None, None
+        return dx, da_g, db_g, da_u, db_u, None, None, None, None, None, None, None
 
 
 class LoRANF4Proj(torch.autograd.Function):
@@ -443,13 +461,15 @@ class DecoderLayer(torch.nn.Module):
                 and uses_dequant_path(x.numel() // x.shape[-1]) and g.in_features % 64 == 0
                 and g.lora_A.shape == u.lora_A.shape and g.p == u.p)
 
-    def forward(self, h, cos, sin, seed, ckpt_calls=None, prefetch=None):
+    def forward(self, h, cos, sin, seed, ckpt_calls=None, prefetch=None, masks=None):
         """ckpt_calls: a one-element list the activation checkpoint passes to both of its calls;
         the first call's saved tensors are discarded, so it skips storing what only a backward
         reads; the second call (the recompute) has its output discarded, so the last
         projection, whose output is the layer's output, builds only what its backward reads.
         prefetch: called once, in the first pass only, as the o projection starts (the next
-        layer's dropout masks then overlap this layer's o / gate / up / down GEMMs)."""
+        layer's dropout masks then overlap this layer's o / gate / up / down GEMMs).
+        masks: called once, in the first pass only, for the mask jobs the gate/up GEMM draws in
+        its side warps (this layer's down mask and the next layer's six)."""
         first_of_checkpoint = recompute = False
         if ckpt_calls is not None:
             first_of_checkpoint = ckpt_calls[0] == 0
@@ -481,9 +501,10 @@ class DecoderLayer(torch.nn.Module):
         x = rmsnorm(h, self.ln2, s.eps)
         if self.mlp_fused_ok(x):
             p = self.gate.p if self.training else 0.0
+            jobs = masks() if masks is not None and not recompute else None
             m = GateUpSwiGLU.apply(x, self.gate.lora_A, self.gate.lora_B, self.up.lora_A,
                                    self.up.lora_B, self.gate, self.up, p, seed + 4, seed + 5,
-                                   torch.is_grad_enabled() and not first_of_checkpoint)
+                                   torch.is_grad_enabled() and not first_of_checkpoint, jobs)
         else:
             m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
         return self.down(m, seed + 6, residual=h, output_dead=recompute, keep_saved=keep)
@@ -512,6 +533,10 @@ class QwenQLoRA(torch.nn.Module):
         # default: it entered the step together with the 2-SM GEMM and qb_lora_xa, when runs of
         # the 7B step began to stall, and stays opt-in until that is explained.
         self.mask_prefetch = False
+        # True: each layer's gate/up GEMM draws its down projection's dropout mask and the next
+        # layer's six in warps beside the GEMM's own (one kernel, one stream); the projections
+        # then apply recorded bits instead of running the Philox rounds themselves.
+        self.gemm_masks = True
         self._rope = {}
         self.step_seed = 0
         # the bf16 adapter operands of every projection, rebuilt by one launch per forward
@@ -553,6 +578,16 @@ class QwenQLoRA(torch.nn.Module):
                 ready[j] = prefetch_masks(self.layers[j], seeds[j], B * S, dev)
             return run
 
+        def mask_jobs(i):
+            if not (self.gemm_masks and not self.mask_prefetch and self.training
+                    and torch.is_grad_enabled()):
+                return None
+            pairs = [(self.layers[i].down, seeds[i] + 6)]
+            if i + 1 < len(self.layers):
+                nxt = self.layers[i + 1]
+                pairs += [(getattr(nxt, n), seeds[i + 1] + k) for k, n in enumerate(_PROJ[:6])]
+            return lambda: gemm_mask_jobs(pairs, B * S, dev)
+
         for i, layer in enumerate(self.layers):
             if ready[i] is not None:
                 torch.cuda.current_stream(dev).wait_event(ready[i])
@@ -561,10 +596,11 @@ class QwenQLoRA(torch.nn.Module):
                 # deterministic; the first pass saves placeholders where only the recompute's
                 # tensors are ever read (shape check off for those)
                 h = torch.utils.checkpoint.checkpoint(layer, h, cos, sin, seeds[i], [0],
-                                                      prefetcher(i + 1), use_reentrant=False,
+                                                      prefetcher(i + 1), mask_jobs(i),
+                                                      use_reentrant=False,
                                                       determinism_check="none")
             else:
-                h = layer(h, cos, sin, seeds[i], None, prefetcher(i + 1))
+                h = layer(h, cos, sin, seeds[i], None, prefetcher(i + 1), mask_jobs(i))
         h = rmsnorm(h, self.norm, self.shape.eps)
         return fused_causal_lm_loss(h, self.lm_head, labels, num_items_in_batch=num_items_in_batch)
 

@@ -289,6 +289,30 @@ int qb_gemm_gateup_swiglu(const void* x, int64_t ldx, const void* w_gate, const 
                           void* h, int64_t ldh, void* g_out, void* u_out, int64_t ldgu, int64_t M,
                           int64_t I, cudaStream_t stream);
 
+/* One dropout mask drawn as bits: words[r * ceil(cols / 32) + c / 32] bit (c & 31) is set when
+ * element (r, c) is kept, the same words qb_dropout_bits writes for (rows, cols, seed, p). */
+typedef struct qb_mask_job {
+  uint32_t* bits;          /* device, 4-byte aligned, rows * ceil(cols / 32) words */
+  int64_t rows, cols;
+  uint64_t seed;
+  float p;                 /* < 1 */
+} qb_mask_job;
+
+/* sizeof(qb_mask_job): the layout check of a binding that builds the array itself. */
+int64_t qb_mask_job_size(void);
+
+/* qb_gemm_gateup_swiglu, and in the same launch up to 8 dropout masks drawn as bits by warps the
+ * GEMM adds beside its own (the Philox rounds run on the integer pipes while the tensor cores
+ * run the product). `jobs` is a host array of njobs entries; the bits are complete when the
+ * launch is. The model draws the next projections' masks here, which the projections then only
+ * apply (solution/lora.py:29-46 draws each mask inside its own dropout pass). */
+int qb_gemm_gateup_swiglu_masks(const void* x, int64_t ldx, const void* w_gate,
+                                const void* w_up, int64_t ldw, int64_t K0, const void* u1,
+                                int64_t ldu1, const void* b1_gate, const void* b1_up,
+                                int64_t ldb1, int64_t K1, void* h, int64_t ldh, void* g_out,
+                                void* u_out, int64_t ldgu, int64_t M, int64_t I,
+                                const qb_mask_job* jobs, int njobs, cudaStream_t stream);
+
 /* C[M, N] (bf16, in place) += scale * mask .* (A[M, K] * B[N, K]^T): fp32 product, one rounding
  * per element, A K-major, B K- or MN-major; mask bit (n & 31) of bits[m * ldbits + n / 32] (the
  * words qb_dropout_mask records). The input gradient of a dropped-out LoRA branch,

@@ -182,6 +182,32 @@ def test_ctypes_bindings_match_the_header_declarations():
         assert have == want, f"{name}: binding {have} vs declaration {want}"
 
 
+def test_mask_job_layout_and_argument_checks():
+    """The ctypes qb_mask_job has the C struct's size; the gate/up GEMM with mask jobs refuses
+    too many jobs, bad shapes and unaligned bits before any CUDA call."""
+    import ctypes
+    from hackathon_b200 import _lib
+    from hackathon_b200.gemm import MaskJob
+    assert _lib.load().qb_mask_job_size() == ctypes.sizeof(MaskJob) == 40
+    fake = 1 << 20
+    args = (fake, 896, fake, fake, 896, 896, None, 0, None, None, 0, 0, fake, 1536, None, None,
+            1536, 128, 1536)
+
+    def run(jobs, n):
+        arr = (MaskJob * max(len(jobs), 1))(*jobs)
+        _lib.call("qb_gemm_gateup_swiglu_masks", *args, arr, n, None)
+
+    ok = MaskJob(fake, 16, 64, 1, 0.1)
+    with pytest.raises(RuntimeError, match="mask jobs"):
+        run([ok] * 9, 9)
+    with pytest.raises(RuntimeError, match="bad shape"):
+        run([ok, MaskJob(fake, 16, 0, 1, 0.1)], 2)
+    with pytest.raises(RuntimeError, match="p must be < 1"):
+        run([MaskJob(fake, 16, 64, 1, 1.0)], 1)
+    with pytest.raises(RuntimeError, match="4-byte aligned"):
+        run([MaskJob(fake + 2, 16, 64, 1, 0.1)], 1)
+
+
 def test_pack_segment_layout_and_table():
     """The Python table of qb_adapter_pack has the C struct's size, and its chunk offsets are the
     running sum of each segment's 2048-element chunks (host only: no launch)."""

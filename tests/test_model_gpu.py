@@ -122,6 +122,41 @@ def test_masks_drawn_ahead_give_the_same_step(cuda):
     assert torch.equal(out[0][1], out[1][1])
 
 
+def test_masks_drawn_in_the_gate_up_gemm_give_the_same_step(cuda):
+    """Dropout masks drawn by the gate/up GEMM's side warps (each layer's down mask and the next
+    layer's six) are the words drawn at their use, bit for bit, and the forward is unchanged
+    bit for bit; only layer 0's six projections draw their own. (The gradients are compared
+    within a tolerance: the attention backward accumulates dQ in a run-dependent order.)"""
+    from hackathon_b200 import _lib
+    from hackathon_b200.qlora import MASKS, QwenQLoRA, preset, synthetic_batch
+    shape = preset("0.5b", layers=3, lora_dropout=0.1)
+    ids, labels = synthetic_batch(shape, 1, 2048, cuda, seed=5)
+    model = QwenQLoRA(shape, cuda, seed=0)
+    model.train()
+    out = []
+    for in_gemm in (True, False):
+        model.gemm_masks = in_gemm
+        model.zero_grad(set_to_none=True)
+        with _lib.KernelTimer() as timer:
+            loss, _ = model(ids, labels)
+        calls = timer.summary()
+        masks = {k: v.clone() for k, v in MASKS.items()}
+        loss.backward()
+        out.append((loss.detach(), torch.cat([p.grad.flatten()
+                                              for p in model.adapter_parameters()]), calls,
+                    masks))
+    assert torch.equal(out[0][0], out[1][0])
+    assert out[0][3].keys() == out[1][3].keys() and len(out[0][3]) == 7 * shape.layers
+    for key, bits in out[0][3].items():
+        assert torch.equal(bits, out[1][3][key]), key
+    rel = (out[0][1] - out[1][1]).norm() / out[1][1].norm()
+    assert rel < 1e-2, float(rel)
+    with_jobs, without = out[0][2], out[1][2]
+    assert with_jobs["qb_gemm_gateup_swiglu_masks"]["launches"] == shape.layers
+    assert with_jobs["qb_dropout_mask"]["launches"] == 6
+    assert without["qb_dropout_mask"]["launches"] == 7 * shape.layers
+
+
 @pytest.mark.parametrize("name,S", [("0.5b", 64), ("1.5b", 2048)])
 def test_decoder_layer_matches_eager_oracle(cuda, name, S):
     """One decoder layer (dropout off): GPU ops vs the eager CPU oracle with the same NF4

@@ -437,6 +437,40 @@ def test_bits_drawn_ahead_equal_recorded_mask(cuda, rows, cols, ctas):
         assert np.array_equal(got, want), r
 
 
+def test_gate_up_gemm_side_warps_draw_the_recorded_masks(cuda):
+    """qb_gemm_gateup_swiglu_masks: the masks its side warps draw are the very words
+    qb_dropout_bits writes (ragged last words, a seed with a high word, tiny and large jobs in
+    one launch), and the GEMM's output equals the launch without side work bit for bit."""
+    from hackathon_b200.gemm import gemm_gateup_swiglu
+    from hackathon_b200.lora import dropout_bits
+    torch.manual_seed(0)
+    M, K0, I, r = 2000, 896, 1536, 16
+    x = (torch.randn(M, K0, device=cuda) * 0.5).to(torch.bfloat16)
+    wg = (torch.randn(I, K0, device=cuda) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(I, K0, device=cuda) * 0.05).to(torch.bfloat16)
+    lu = (torch.randn(M, 2 * r, device=cuda) * 0.5).to(torch.bfloat16)
+    bg = (torch.randn(I, 2 * r, device=cuda) * 0.05).to(torch.bfloat16)
+    bu = (torch.randn(I, 2 * r, device=cuda) * 0.05).to(torch.bfloat16)
+    specs = [(M, K0, 0.1, 1234567890123), (M, 4864, 0.05, 7), (7, 40, 0.5, 3), (5, 33, 0.0, 11),
+             (16384, 3584, 0.05, 20240607), (1, 1, 0.3, 5)]
+    jobs = [(torch.full((rows, (cols + 31) // 32), -1, dtype=torch.int32, device=cuda), rows,
+             cols, seed, p) for rows, cols, p, seed in specs]
+    h0, g0, u0 = gemm_gateup_swiglu(x, wg, wu, lu, bg, bu, save_gu=True)
+    h1, g1, u1 = gemm_gateup_swiglu(x, wg, wu, lu, bg, bu, save_gu=True, mask_jobs=jobs)
+    assert torch.equal(h1, h0) and torch.equal(g1, g0) and torch.equal(u1, u0)
+    for bits, rows, cols, seed, p in jobs:
+        assert torch.equal(bits, dropout_bits(rows, cols, p, seed, cuda)), (rows, cols)
+    r0 = jobs[0][0][M - 1].cpu().numpy().view(np.uint32)
+    got = ((r0[:, None] >> np.arange(32)) & 1).reshape(-1)[:K0].astype(bool)
+    want = nf4_ref.philox_uniform(specs[0][3], (M - 1) * K0 + np.arange(K0)) > np.float32(0.1)
+    assert np.array_equal(got, want)
+    # without the LoRA segment and without saving g / u
+    h2 = gemm_gateup_swiglu(x, wg, wu, mask_jobs=jobs[2:4])
+    assert torch.equal(h2, gemm_gateup_swiglu(x, wg, wu))
+    with pytest.raises(ValueError):
+        gemm_gateup_swiglu(x, wg, wu, mask_jobs=jobs + jobs[:3])
+
+
 def test_bits_drawn_on_a_side_stream_beside_a_gemm(cuda):
     """The prefetch pattern of the model: bits drawn on another stream while a tcgen05 GEMM
     runs, the consumer stream waiting on an event; the result equals the inline mask."""
