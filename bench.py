@@ -335,7 +335,8 @@ KERNELS = ("gemm2", "gemm_dgrad", "nf4_fwd_fused", "nf4_fwd_dequant", "nf4_dgrad
            "nf4_dequant",
            "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd", "rmsnorm_bwd",
            "rope_bwd", "linear_ce", "mask_acc", "gateup_swiglu", "gemm2_dgrad_pair",
-           "gemm2_rope", "dropout_bits", "lora_xa", "lora_xa_xd", "lora_grads")
+           "gemm2_rope", "dropout_bits", "lora_xa", "lora_xa_xd", "lora_grads",
+           "gateup_swiglu_masks")
 GRAPHABLE = ("nf4_dequant", "dropout_mask", "dropout_apply", "swiglu_fwd", "rmsnorm_fwd",
              "rmsnorm_bwd", "rope_bwd", "dropout_bits")
 
@@ -417,9 +418,11 @@ def kernel_case(args):
         gate, up = rnd(T, fo), rnd(T, fo)
         fn = lambda: swiglu(gate, up)  # noqa: E731
         nbytes = 3 * T * fo * 2
-    elif name in ("gateup_swiglu", "gemm2_dgrad_pair"):
+    elif name in ("gateup_swiglu", "gemm2_dgrad_pair", "gateup_swiglu_masks"):
         # the MLP pair at intermediate size --out-features: h = silu(g) * u in one GEMM (LoRA
-        # terms as extra K), or its input gradient dx = dg W_g + du W_u
+        # terms as extra K), or its input gradient dx = dg W_g + du W_u; `_masks`: the forward's
+        # launch, h only, with the side warps drawing a layer's seven masks (six --in-features
+        # wide, one --out-features wide, p = 0.05)
         from hackathon_b200.gemm import gemm_gateup_swiglu
         wg, wu = rnd(fo, fi, s=0.02), rnd(fo, fi, s=0.02)
         if name == "gateup_swiglu":
@@ -427,6 +430,14 @@ def kernel_case(args):
             bg, bu = rnd(fo, 2 * r, s=0.05), rnd(fo, 2 * r, s=0.05)
             fn = lambda: gemm_gateup_swiglu(x, wg, wu, lu, bg, bu, save_gu=True)  # noqa
             flops = 2 * T * 2 * fo * (fi + 2 * r)
+        elif name == "gateup_swiglu_masks":
+            x, lu = rnd(T, fi), rnd(T, 2 * r)
+            bg, bu = rnd(fo, 2 * r, s=0.05), rnd(fo, 2 * r, s=0.05)
+            jobs = [(torch.empty((T, (c + 31) // 32), dtype=torch.int32, device=dev), T, c,
+                     1000 + k, 0.05) for k, c in enumerate([fi] * 6 + [fo])]
+            fn = lambda: gemm_gateup_swiglu(x, wg, wu, lu, bg, bu, mask_jobs=jobs)  # noqa
+            flops = 2 * T * 2 * fo * (fi + 2 * r)
+            draws = T * (6 * fi + fo)
         else:
             dg, du = rnd(T, fo), rnd(T, fo)
             fn = lambda: gemm2(dg, wg.t(), du, wu.t())  # noqa: E731
@@ -514,11 +525,13 @@ def kernel_case(args):
     pk = peaks()
     line = {"kernel": name, "tokens": T, "in_features": fi, "out_features": fo, "ms": round(ms, 4),
             "graph": bool(args.graph)}
-    if draws:      # integer-pipe work: Philox draws per second, no HBM / tensor peak applies
+    if draws and not flops:   # integer-pipe work: Philox draws/s, no HBM / tensor peak applies
         line.update(achieved=round(draws / (ms * 1e-3) / 1e9, 1), unit="Gdraws/s",
                     draws_per_launch=draws)
         print(json.dumps(line), flush=True)
         return
+    if draws:      # a GEMM that also draws masks in its side warps
+        line.update(draws_per_s_g=round(draws / (ms * 1e-3) / 1e9, 1), draws_per_launch=draws)
     if flops:
         tf = flops / (ms * 1e-3) / 1e12
         line.update(achieved=round(tf, 1), unit="TFLOP/s", peak=pk["bf16_tflops"],
