@@ -142,10 +142,42 @@ def _mask_bits(x2, mod, p, seed):
 FUSED_ADAPTER_INPUT = False
 
 
-def _adapter_input(x2, mod, a16, p, seed, keep_xd, u_out=None):
+# The rank-r products U = xd A^T of an activation checkpoint's first pass, kept for its
+# recompute, keyed by (projection, seed) (the gate / up pair by ("pair", gate, seed)): the
+# recompute forms the same xd from the same recorded mask and multiplies it by the same A (the
+# adapters change only at the optimizer step), so it reuses U — [tokens, r], 2 MB a projection
+# at 16384 tokens and r = 64 — and rebuilds only xd. Cleared with MASKS at every forward.
+UPRODS = {}
+KEEP_UPRODS = True
+
+
+def _keep_uprod(keep_xd, graph):
+    """True when this call is an activation checkpoint's first pass that a recompute follows:
+    nothing saved is kept (keep_xd False) and the adapters take part in an autograd graph
+    (`graph`: the autograd Function's needs_input_grad for them; grad mode itself is off inside
+    a Function's forward)."""
+    return KEEP_UPRODS and not keep_xd and graph
+
+
+def _adapter_input(x2, mod, a16, p, seed, keep_xd, u_out=None, stash=False):
     """(xd, U = xd a16^T, bits, scale) of one projection with xd = dropout(x2) * scale: U comes
     from x2 and the mask bits in one kernel (qb_lora_xa); xd is stored only when the backward
-    will read it (keep_xd), else an empty placeholder stands in its saved slot."""
+    will read it (keep_xd), else an empty placeholder stands in its saved slot. stash (the
+    caller's graph flag of _keep_uprod): keep U of a checkpoint's first pass for its recompute
+    (UPRODS); a recompute (keep_xd) takes it from there."""
+    key = (id(mod), seed)
+    kept = UPRODS.pop(key, None) if keep_xd and u_out is None else None
+    if kept is not None and kept.shape == (x2.shape[0], a16.shape[0]):
+        xd, bits, scale = _dropped(x2, mod, p, seed)
+        return xd, kept, bits, scale
+    xd, u, bits, scale = _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out)
+    if u_out is None and _keep_uprod(keep_xd, stash):
+        UPRODS[key] = u
+    return xd, u, bits, scale
+
+
+def _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out):
+    """_adapter_input's computation: xd and U = xd a16^T."""
     from .gemm import gemm
     from .lora import lora_xa, lora_xa_ok
     if (not FUSED_ADAPTER_INPUT or not lora_xa_ok(x2, a16)
@@ -207,11 +239,22 @@ class GateUpSwiGLU(torch.autograd.Function):
         I, r = gate.out_features, a_g.shape[0]
         a16_g, _ = gate.adapter16(x.dtype)
         a16_u, _ = up.adapter16(x.dtype)
-        lora_u = torch.empty((T, 2 * r), dtype=x.dtype, device=x.device)   # [U_g | U_u]
-        xd_g, u_g, bits_g, scale = _adapter_input(x2, gate, a16_g, p, seed_g, save_gu,
-                                                  u_out=lora_u[:, :r])
-        xd_u, u_u, bits_u, _ = _adapter_input(x2, up, a16_u, p, seed_u, save_gu,
-                                              u_out=lora_u[:, r:])
+        pair = ("pair", id(gate), seed_g)
+        kept = UPRODS.pop(pair, None) if save_gu else None
+        if kept is not None and kept.shape == (T, 2 * r):
+            # the recompute: [U_g | U_u] from the first pass, only xd_g / xd_u rebuilt
+            lora_u = kept
+            xd_g, bits_g, scale = _dropped(x2, gate, p, seed_g)
+            xd_u, bits_u, _ = _dropped(x2, up, p, seed_u)
+            u_g, u_u = lora_u[:, :r], lora_u[:, r:]
+        else:
+            lora_u = torch.empty((T, 2 * r), dtype=x.dtype, device=x.device)   # [U_g | U_u]
+            xd_g, u_g, bits_g, scale = _adapter_input(x2, gate, a16_g, p, seed_g, save_gu,
+                                                      u_out=lora_u[:, :r])
+            xd_u, u_u, bits_u, _ = _adapter_input(x2, up, a16_u, p, seed_u, save_gu,
+                                                  u_out=lora_u[:, r:])
+            if _keep_uprod(save_gu, any(ctx.needs_input_grad[1:5])):
+                UPRODS[pair] = lora_u
         if gate._shadow_b1 is not None and x.dtype == torch.bfloat16:
             b1_g, b1_u = gate._shadow_b1
         else:
@@ -314,7 +357,8 @@ class LoRANF4Proj(torch.autograd.Function):
         from .nf4 import dequantize_nf4, nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
         a16, sb16 = mod.adapter16(x.dtype)
-        xd, u, bits, scale = _adapter_input(x2, mod, a16, p, seed, keep_saved)
+        graph = ctx.needs_input_grad[1] or ctx.needs_input_grad[2]
+        xd, u, bits, scale = _adapter_input(x2, mod, a16, p, seed, keep_saved, stash=graph)
         w_keep = None
         if ctx.needs_input_grad[0] and uses_dequant_path(x2.shape[0]):
             w_keep = dequantize_nf4(mod.packed, mod.quant_state, torch.bfloat16,
@@ -562,6 +606,7 @@ class QwenQLoRA(torch.nn.Module):
         if MASKS and dev in _SIDE_STREAMS:   # masks a side stream may still be writing
             torch.cuda.current_stream(dev).wait_stream(_SIDE_STREAMS[dev])
         MASKS.clear()
+        UPRODS.clear()
         if self.adapter_shadow is not None:   # the adapters changed since the last forward
             self.adapter_shadow.refresh()
         cos, sin = self.rope_tables(S, dev)

@@ -157,6 +157,50 @@ def test_masks_drawn_in_the_gate_up_gemm_give_the_same_step(cuda):
     assert without["qb_dropout_mask"]["launches"] == 7 * shape.layers
 
 
+@pytest.mark.parametrize("S", [256, 2048])
+def test_recompute_reuses_first_pass_lora_products(cuda, S):
+    """The checkpoint recompute takes U = xd Aᵀ of every projection from the first pass instead
+    of running the rank-r GEMM again: the same loss and adapter gradients (bit for bit where the
+    attention backward is deterministic, S = 256; within a tolerance at S = 2048, where it
+    accumulates dQ in a run-dependent order), and one rank-r GEMM call fewer in the backward
+    for every product kept (two for the gate / up pair's)."""
+    from hackathon_b200 import _lib
+    from hackathon_b200 import qlora
+    from hackathon_b200.qlora import QwenQLoRA, preset, synthetic_batch
+    shape = preset("0.5b", layers=3, lora_dropout=0.1)
+    ids, labels = synthetic_batch(shape, 1, S, cuda, seed=7)
+    model = QwenQLoRA(shape, cuda, seed=0)
+    model.train()
+    out = []
+    try:
+        for keep in (True, False):
+            qlora.KEEP_UPRODS = keep
+            model.zero_grad(set_to_none=True)
+            loss, _ = model(ids, labels)
+            kept = len(qlora.UPRODS)
+            with _lib.KernelTimer() as timer:
+                loss.backward()
+            calls = timer.summary()
+            out.append((loss.detach(), torch.cat([p.grad.flatten()
+                                                  for p in model.adapter_parameters()]),
+                        calls["qb_gemm_bf16"]["launches"], kept, len(qlora.UPRODS)))
+    finally:
+        qlora.KEEP_UPRODS = True
+    (l1, g1, n1, k1, left1), (l0, g0, n0, k0, _) = out
+    assert torch.equal(l1, l0)
+    pairs = 0 if S == 256 else shape.layers     # the gate / up pair from 2048 tokens on
+    if S == 256:
+        assert torch.equal(g1, g0)
+    else:
+        rel = (g1 - g0).norm() / g0.norm()
+        assert rel < 1e-2, float(rel)
+    # every kept product saves one GEMM call in the recompute, a kept pair two; at least the q,
+    # o and down projections (and gate / up) of every layer take the fused path here
+    assert k1 >= 3 * shape.layers + pairs
+    assert n0 - n1 == k1 + pairs
+    assert k0 == 0 and left1 == 0
+
+
 @pytest.mark.parametrize("name,S", [("0.5b", 64), ("1.5b", 2048)])
 def test_decoder_layer_matches_eager_oracle(cuda, name, S):
     """One decoder layer (dropout off): GPU ops vs the eager CPU oracle with the same NF4
