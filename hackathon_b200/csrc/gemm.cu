@@ -18,6 +18,13 @@ constexpr int kBN = 256;
 // Row-major store: each epilogue thread owns one output row of the tile and writes its 32
 // consecutive columns per TMEM chunk with 16-byte stores; optionally adds a bias row and a
 // residual matrix of the output's type first (one rounding of acc + bias + residual).
+//
+// With a tensor map of C (`tma`), the one-CTA kernel gives each epilogue warp two [32 x 32]
+// staging boxes in shared memory: each thread writes its row of the box (16-byte pieces, in the
+// 64-byte / 128-byte swizzle of the map, so a warp's writes hit every bank once), and one lane
+// stores the box with a TMA store — whole lines to L2 instead of 32 rows of 16 bytes per store
+// instruction. The two boxes alternate; a box is rewritten only after its previous store has
+// read it.
 template <typename OutT>
 struct EpiStoreRow {
   OutT* c;
@@ -27,6 +34,79 @@ struct EpiStoreRow {
   const OutT* resid;  // [M, N] (row stride ldr) or null
   int64_t ldr;
   bool vec;           // 16-byte aligned rows (output and residual)
+  bool tma = false;   // cmap holds C: [M, N], box 32 x 32, 64-byte (bf16) / 128-byte (fp32) swizzle
+  CUtensorMap cmap;
+
+  static constexpr int kRowBytes = 32 * static_cast<int>(sizeof(OutT));   // one box row
+  static constexpr int kBoxBytes = 32 * kRowBytes;
+  static constexpr int kStageBytes = 2 * kBoxBytes;
+
+  // acc (+ bias) (+ residual) of 32 columns n.. of row m
+  __device__ __forceinline__ void finish(float (&v)[32], int m, int n) const {
+    if (bias) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += (n + i < N) ? __ldg(bias + n + i) : 0.f;
+    }
+    if (resid && m < M) {
+      const OutT* res = resid + static_cast<int64_t>(m) * ldr + n;
+      if (vec && n + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          float r[8];
+          qb::load8(res + i, r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i + j] += r[j];
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < N) v[i] += qb::to_f(res[i]);
+      }
+    }
+  }
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr,
+                                       uint8_t* stage) const {
+    if (!tma) {
+      tile<BN>(m0, n0, row, taddr);
+      return;
+    }
+    const int lane = row & 31;
+    const int m = m0 + row;
+    const int mw = m - lane;   // the warp's first row
+    if (lane == 0) tc::bulk_wait_read_all();   // the previous tile's boxes are free
+    __syncwarp();
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      float v[32];
+      tc::tmem_ld32(taddr + ch * 32, v);
+      const int n = n0 + ch * 32;
+      if (n >= N) continue;   // warp-uniform
+      finish(v, m, n);
+      uint8_t* box = stage + (ch & 1) * kBoxBytes;
+      if (ch >= 2) {   // the store of chunk ch - 2 read this box
+        if (lane == 0) tc::bulk_wait_read_newest_pending();
+        __syncwarp();
+      }
+      uint8_t* dst = box + lane * kRowBytes;
+#pragma unroll
+      for (int p = 0; p < kRowBytes / 16; ++p) {
+        const int sp = sizeof(OutT) == 2 ? (p ^ ((lane >> 1) & 3)) : (p ^ (lane & 7));
+        constexpr int kPer = qb::Vec16<OutT>::N;   // elements per 16 bytes
+        qb::Vec16<OutT> w;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) w.v[i] = qb::from_f<OutT>(v[p * kPer + i]);
+        *reinterpret_cast<uint4*>(dst + sp * 16) = w.u;
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && mw < M) {   // rows past M and columns past N are clipped by the store
+        tc::tma_store_2d(&cmap, box, n, mw);
+        tc::bulk_commit();
+      }
+    }
+  }
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -315,6 +395,17 @@ int run(const CUtensorMap (&m)[4], const tcg::Problem& pb, void* c, int64_t ldc,
         const char* what) {
   EpiStoreRow<OutT> epi{static_cast<OutT*>(c), ldc, pb.M, pb.N, bias,
                         static_cast<const OutT*>(resid), ldr, vec};
+  if (qb::aligned16(c) && (ldc * static_cast<int64_t>(sizeof(OutT))) % 16 == 0) {
+    // C as TMA stores it from the epilogue's staging boxes (EpiStoreRow)
+    const bool f32 = sizeof(OutT) == 4;
+    if (int e = tc_host::encode_2d(&epi.cmap,
+                                   f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                   c, pb.N, pb.M, ldc * sizeof(OutT), 32, 32,
+                                   f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+    epi.tma = true;
+  }
   return tcg::launch<A0, B0, A1, B1, BN>(m[0], m[1], m[2], m[3], pb, epi, s, what);
 }
 

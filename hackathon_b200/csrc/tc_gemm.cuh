@@ -84,6 +84,27 @@ struct Cfg {
 
 constexpr bool is_mn(int s) { return s == kTmaMN; }
 
+// Epilogues that store through shared memory declare kStageBytes: the bytes each of the four
+// epilogue warps gets for staging its 32 rows of the output before a TMA store. Others get none.
+template <class E, class = void>
+struct EpiStage {
+  static constexpr int bytes = 0;
+};
+template <class E>
+struct EpiStage<E, std::void_t<decltype(E::kStageBytes)>> {
+  static constexpr int bytes = E::kStageBytes;
+};
+
+// Ring stages of Cfg<BN> that fit beside `epi_bytes` of epilogue staging in the 227 KB a CTA
+// may have.
+template <int BN>
+constexpr int stages_with(int epi_bytes) {
+  using C = Cfg<BN>;
+  return (232448 - C::EXTRA - epi_bytes) / C::STAGE < C::STAGES
+             ? (232448 - C::EXTRA - epi_bytes) / C::STAGE
+             : C::STAGES;
+}
+
 // Side work for warps past the GEMM's six: dropout-mask words (the Philox stream of philox.cuh)
 // drawn on the integer pipes while the tensor cores run the product. The jobs' words form one
 // index space (job j owns [first, first + rows * words)); the side warps stride over it with the
@@ -129,19 +150,23 @@ __global__ void __launch_bounds__(kThreads + 32 * SIDE, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mB0,
                const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mB1,
                const __grid_constant__ CUtensorMap mB0b, const __grid_constant__ CUtensorMap mB1b,
-               const Problem pb, Epi epi, const tc::Ctl ctl,
+               const Problem pb, const __grid_constant__ Epi epi, const tc::Ctl ctl,
                const __grid_constant__ SideArg<SIDE> side) {
   using C = Cfg<BN>;
   int* err = ctl.err;
   tc::trace_begin(ctl);
-  constexpr int STAGES = C::STAGES;
+  constexpr int kEpiWarpBytes = EpiStage<Epi>::bytes;
+  constexpr int kEpiBytes = 4 * kEpiWarpBytes;
+  constexpr int STAGES = stages_with<BN>(kEpiBytes);
+  static_assert(STAGES >= 2, "at least two ring stages");
   constexpr uint32_t kIdesc0 = tc::idesc_bf16(BM, BN, is_mn(A0), is_mn(B0));
   constexpr uint32_t kIdesc1 = tc::idesc_bf16(BM, BN, is_mn(A1), is_mn(B1));
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE);
+  uint8_t* epi_stage = smem + STAGES * C::STAGE;   // 1024-aligned: STAGE is a multiple of 1024
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + kEpiBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -289,9 +314,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ 
       // with split-K, split sp's partial tile lands sp x (padded M) rows further down: the
       // epilogue of a split launch writes partial products that a reduction sums in split order
       const int m_off = (item - tile * (pb.splits > 1 ? pb.splits : 1)) * pb.num_m * BM;
-      epi.template tile<BN>(mb * BM + m_off, nb * BN, row, taddr);
+      if constexpr (kEpiWarpBytes > 0)
+        epi.template tile<BN>(mb * BM + m_off, nb * BN, row, taddr,
+                              epi_stage + (warp - 2) * kEpiWarpBytes);
+      else
+        epi.template tile<BN>(mb * BM + m_off, nb * BN, row, taddr);
       tc::fence_before_sync();
       tc::mbar_arrive(&tempty[buf]);
+    }
+    if constexpr (kEpiWarpBytes > 0) {   // this warp's TMA stores are complete before exit
+      if (lane == 0) tc::bulk_wait_all();
+      __syncwarp();
     }
   } else {
     // ---------------------------------------------------------------- side warps
@@ -317,7 +350,10 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
   static_assert(B0 != kTmaKDual || BN % 2 == 0, "dual B splits the tile in halves");
   using C = Cfg<BN>;
   auto kernel = tc_gemm_kernel<A0, B0, A1, B1, BN, Epi, SIDE>;
-  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), C::SMEM, what)) return s;
+  constexpr int kEpiBytes = 4 * EpiStage<Epi>::bytes;
+  constexpr int kSmem = stages_with<BN>(kEpiBytes) * C::STAGE + kEpiBytes + C::EXTRA;
+  static_assert(kSmem <= 232448, "shared memory of one CTA");
+  if (int s = tc_host::ensure_smem(reinterpret_cast<const void*>(kernel), kSmem, what)) return s;
   const int tiles = pb.num_m * pb.num_n * (pb.splits > 1 ? pb.splits : 1);
   if (tiles == 0) return QB_OK;
   if (pb.splits > pb.nk0 + pb.nk1)
@@ -328,7 +364,7 @@ int launch(const CUtensorMap& mA0, const CUtensorMap& mB0, const CUtensorMap& mA
     return qb::fail(QB_ERR_INVALID, "%s: dual B needs its second tensor map", what);
   tc::Ctl ctl;
   if (int s = tc_host::launch_ctl(&ctl, what)) return s;
-  kernel<<<grid, kThreads + 32 * SIDE, C::SMEM, stream>>>(mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
+  kernel<<<grid, kThreads + 32 * SIDE, kSmem, stream>>>(mA0, mB0, mA1, mB1, mB0b ? *mB0b : mB0,
                                                          mB1b ? *mB1b : mB1, pb, epi, ctl, side);
   return qb::check_launch(what);
 }
