@@ -261,6 +261,10 @@ split_reduce_kernel(const float* __restrict__ ws, int64_t ldw, int64_t split_str
 // (the backward's inputs).
 __device__ __forceinline__ float swiglu_sigmoid(float g) { return 1.0f / (1.0f + __expf(-g)); }
 
+//
+// With tensor maps of h (and g, u) (`tma`), the one-CTA kernel stages each 32-column chunk of the
+// warp's 32 rows in shared memory (64-byte swizzle: a warp's 16-byte writes hit every bank once)
+// and one lane stores h (and g, u) with TMA stores.
 struct EpiSwiGLU {
   __nv_bfloat16* h;
   int64_t ldh;
@@ -269,6 +273,66 @@ struct EpiSwiGLU {
   int64_t ldgu;
   int M, I;
   bool vec;
+  bool tma = false;   // hmap (and gmap, umap when g is stored): [M, I], box 32 x 32, 64-byte swizzle
+  CUtensorMap hmap, gmap, umap;
+
+  static constexpr int kBoxBytes = 32 * 64;
+  static constexpr int kStageBytes = 3 * kBoxBytes;   // h, g, u boxes of one chunk
+
+  __device__ __forceinline__ static void put_row(uint8_t* box, int lane, const float* v) {
+    uint8_t* dst = box + lane * 64;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      qb::Vec16<__nv_bfloat16> w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w.v[i] = __float2bfloat16_rn(v[8 * p + i]);
+      *reinterpret_cast<uint4*>(dst + ((p ^ ((lane >> 1) & 3)) << 4)) = w.u;
+    }
+  }
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr,
+                                       uint8_t* stage) const {
+    if (!tma) {
+      tile<BN>(m0, n0, row, taddr);
+      return;
+    }
+    const int lane = row & 31;
+    const int mw = m0 + row - lane;   // the warp's first row
+    const int j0 = n0 / 2;
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      float gv[32], uv[32];
+      tc::tmem_ld32(taddr + c * 32, gv);
+      tc::tmem_ld32(taddr + BN / 2 + c * 32, uv);
+      const int j = j0 + c * 32;
+      if (j >= I) continue;   // warp-uniform
+      float hv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        gv[i] = __bfloat162float(__float2bfloat16_rn(gv[i]));
+        uv[i] = __bfloat162float(__float2bfloat16_rn(uv[i]));
+        hv[i] = gv[i] * swiglu_sigmoid(gv[i]) * uv[i];
+      }
+      if (lane == 0) tc::bulk_wait_read_all();   // the previous chunk's boxes are free
+      __syncwarp();
+      put_row(stage, lane, hv);
+      if (g) {
+        put_row(stage + kBoxBytes, lane, gv);
+        put_row(stage + 2 * kBoxBytes, lane, uv);
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && mw < M) {   // rows past M and columns past I are clipped by the stores
+        tc::tma_store_2d(&hmap, stage, j, mw);
+        if (g) {
+          tc::tma_store_2d(&gmap, stage + kBoxBytes, j, mw);
+          tc::tma_store_2d(&umap, stage + 2 * kBoxBytes, j, mw);
+        }
+        tc::bulk_commit();
+      }
+    }
+  }
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -820,6 +884,20 @@ int gateup_swiglu(const void* x, int64_t ldx, const void* w_gate, const void* w_
   EpiSwiGLU epi{static_cast<__nv_bfloat16*>(h), ldh, static_cast<__nv_bfloat16*>(g_out),
                 static_cast<__nv_bfloat16*>(u_out), ldgu, static_cast<int>(M), static_cast<int>(I),
                 vec};
+  if (vec) {   // 16-byte aligned rows: h (and g, u) as TMA stores them from the staging boxes
+    if (int e = tc_host::encode_2d(&epi.hmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h, I, M, ldh * 2,
+                                   32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+    if (g_out) {
+      if (int e = tc_host::encode_2d(&epi.gmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g_out, I, M,
+                                     ldgu * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return e;
+      if (int e = tc_host::encode_2d(&epi.umap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, u_out, I, M,
+                                     ldgu * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return e;
+    }
+    epi.tma = true;
+  }
   using namespace tcg;
   if (side)
     return launch<kTmaK, kTmaKDual, kTmaK, kTmaKDual, kBN, EpiSwiGLU, kSideWarps>(
