@@ -21,6 +21,10 @@ namespace {
 
 constexpr int kBN = 256;
 
+//
+// With a tensor map of dz (`tma`), each epilogue warp stages its 32 rows of a 32-column chunk in
+// shared memory (two alternating boxes, 64-byte swizzle) and one lane stores the box with a TMA
+// store: whole lines to L2 for the [rows, vocab] gradient, the pass's only large output.
 struct EpiGrad {
   __nv_bfloat16* dz;       // [rows, ldz]
   int64_t ldz;
@@ -29,6 +33,51 @@ struct EpiGrad {
   const float* scale_dev;  // device scalar: the factor dZ carries
   int rows, vocab;
   bool vec;
+  bool tma = false;        // dmap holds dz: [rows, vocab], box 32 x 32, 64-byte swizzle
+  CUtensorMap dmap;
+
+  static constexpr int kBoxBytes = 32 * 64;
+  static constexpr int kStageBytes = 2 * kBoxBytes;
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr,
+                                       uint8_t* stage) const {
+    if (!tma) {
+      tile<BN>(m0, n0, row, taddr);
+      return;
+    }
+    const int lane = row & 31;
+    const int r = m0 + row;
+    const int rw = r - lane;   // the warp's first row
+    const bool live = r < rows;
+    const int64_t label = live ? __ldg(target + r) : -1;
+    const float l = live ? __ldg(lse + r) : 0.f;
+    const float sc = (live && label >= 0) ? __ldg(scale_dev) : 0.f;
+    if (lane == 0) tc::bulk_wait_read_all();   // the previous tile's boxes are free
+    __syncwarp();
+#pragma unroll 1
+    for (int ch = 0; ch < BN / 32; ++ch) {
+      float v[32];
+      tc::tmem_ld32(taddr + ch * 32, v);
+      const int n = n0 + ch * 32;
+      if (n >= vocab) continue;   // warp-uniform
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        v[i] = live ? (__expf(v[i] - l) - (n + i == label ? 1.f : 0.f)) * sc : 0.f;
+      uint8_t* box = stage + (ch & 1) * kBoxBytes;
+      if (ch >= 2) {   // the store of chunk ch - 2 read this box
+        if (lane == 0) tc::bulk_wait_read_newest_pending();
+        __syncwarp();
+      }
+      tcg::stage_row_bf16(box, lane, v);
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && rw < rows) {   // rows past `rows` and columns past vocab are clipped
+        tc::tma_store_2d(&dmap, box, n, rw);
+        tc::bulk_commit();
+      }
+    }
+  }
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -314,6 +363,12 @@ extern "C" int qb_linear_ce_grad(const void* hidden, int64_t ldh, const void* we
   const bool vec = qb::aligned16(dz) && (ldz * 2) % 16 == 0;
   EpiGrad epi{static_cast<__nv_bfloat16*>(dz), ldz, target, lse, scale_dev,
               static_cast<int>(rows), static_cast<int>(vocab), vec};
+  if (vec) {   // dz as TMA stores it from the epilogue's staging boxes
+    if (int s = tc_host::encode_2d(&epi.dmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dz, vocab, rows,
+                                   ldz * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return s;
+    epi.tma = true;
+  }
   return tcg::launch<tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, tcg::kTmaK, kBN>(
       mh, mw, mh, mw, pb, epi, stream, "linear_ce_grad");
 }

@@ -279,17 +279,6 @@ struct EpiSwiGLU {
   static constexpr int kBoxBytes = 32 * 64;
   static constexpr int kStageBytes = 3 * kBoxBytes;   // h, g, u boxes of one chunk
 
-  __device__ __forceinline__ static void put_row(uint8_t* box, int lane, const float* v) {
-    uint8_t* dst = box + lane * 64;
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      qb::Vec16<__nv_bfloat16> w;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) w.v[i] = __float2bfloat16_rn(v[8 * p + i]);
-      *reinterpret_cast<uint4*>(dst + ((p ^ ((lane >> 1) & 3)) << 4)) = w.u;
-    }
-  }
-
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr,
                                        uint8_t* stage) const {
@@ -316,10 +305,10 @@ struct EpiSwiGLU {
       }
       if (lane == 0) tc::bulk_wait_read_all();   // the previous chunk's boxes are free
       __syncwarp();
-      put_row(stage, lane, hv);
+      tcg::stage_row_bf16(stage, lane, hv);
       if (g) {
-        put_row(stage + kBoxBytes, lane, gv);
-        put_row(stage + 2 * kBoxBytes, lane, uv);
+        tcg::stage_row_bf16(stage + kBoxBytes, lane, gv);
+        tcg::stage_row_bf16(stage + 2 * kBoxBytes, lane, uv);
       }
       tc::fence_proxy_async_smem();
       __syncwarp();
@@ -383,6 +372,10 @@ struct EpiSwiGLU {
 // then rotated in fp32 with that position's cos/sin (qb::rope_rotate, the RoPE kernel's
 // arithmetic) and rounded again. A 256-wide tile holds two whole heads; chunk c (32 columns)
 // pairs with chunk c + 2 (dims d and d + 64 of the same head).
+//
+// With a tensor map of C (`tma`), the one-CTA kernel stages the two 32-column pieces of each
+// (first half, second half) pair in shared memory and one lane stores them with TMA stores; the
+// two pair buffers alternate.
 struct EpiStoreRope {
   __nv_bfloat16* c;
   int64_t ldc;
@@ -392,6 +385,76 @@ struct EpiStoreRope {
   const __nv_bfloat16* sinp;
   int64_t css;
   bool vec;
+  bool tma = false;   // cmap holds C: [M, N], box 32 x 32, 64-byte swizzle
+  CUtensorMap cmap;
+
+  static constexpr int kBoxBytes = 32 * 64;
+  static constexpr int kStageBytes = 4 * kBoxBytes;
+
+  // the rotated pair (x1 at column n1 = n0 + ch * 32, x2 at n1 + 64) of one row
+  __device__ __forceinline__ void rotate(float (&x1)[32], float (&x2)[32], int ch, int n1,
+                                         const __nv_bfloat16* cr,
+                                         const __nv_bfloat16* sr) const {
+    const int d = (ch & 1) * 32;             // dim of x1[0] within its head
+    float c1[32], c2[32], s1[32], s2[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      qb::load8(cr + d + i, c1 + i);
+      qb::load8(cr + 64 + d + i, c2 + i);
+      qb::load8(sr + d + i, s1 + i);
+      qb::load8(sr + 64 + d + i, s2 + i);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float a = x1[i] + (bias ? __ldg(bias + n1 + i) : 0.f);
+      const float b = x2[i] + (bias ? __ldg(bias + n1 + 64 + i) : 0.f);
+      qb::rope_rotate(__bfloat162float(__float2bfloat16_rn(a)),
+                      __bfloat162float(__float2bfloat16_rn(b)), c1[i], c2[i], s1[i], s2[i],
+                      x1[i], x2[i]);
+    }
+  }
+
+  template <int BN>
+  __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr,
+                                       uint8_t* stage) const {
+    static_assert(BN % 128 == 0, "whole heads of 128 per tile");
+    if (!tma) {
+      tile<BN>(m0, n0, row, taddr);
+      return;
+    }
+    const int lane = row & 31;
+    const int m = m0 + row;
+    const int mw = m - lane;   // the warp's first row
+    const bool live = m < M;
+    const __nv_bfloat16* cr = cosp + static_cast<int64_t>(live ? m % S : 0) * css;
+    const __nv_bfloat16* sr = sinp + static_cast<int64_t>(live ? m % S : 0) * css;
+    if (lane == 0) tc::bulk_wait_read_all();   // the previous tile's buffers are free
+    __syncwarp();
+#pragma unroll 1
+    for (int p = 0; p < BN / 64; ++p) {
+      const int ch = (p & 1) + (p >> 1) * 4;   // 0, 1, 4, 5: first halves of the two heads
+      float x1[32], x2[32];
+      tc::tmem_ld32(taddr + ch * 32, x1);
+      tc::tmem_ld32(taddr + (ch + 2) * 32, x2);
+      const int n1 = n0 + ch * 32;
+      if (n1 >= N) continue;   // warp-uniform; N is whole heads, so n1 + 64 < N too
+      rotate(x1, x2, ch, n1, cr, sr);
+      uint8_t* pair = stage + (p & 1) * 2 * kBoxBytes;
+      if (p >= 2) {   // the stores of pair p - 2 read this buffer
+        if (lane == 0) tc::bulk_wait_read_newest_pending();
+        __syncwarp();
+      }
+      tcg::stage_row_bf16(pair, lane, x1);
+      tcg::stage_row_bf16(pair + kBoxBytes, lane, x2);
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && mw < M) {   // rows past M are clipped by the stores
+        tc::tma_store_2d(&cmap, pair, n1, mw);
+        tc::tma_store_2d(&cmap, pair + kBoxBytes, n1 + 64, mw);
+        tc::bulk_commit();
+      }
+    }
+  }
 
   template <int BN>
   __device__ __forceinline__ void tile(int m0, int n0, int row, uint32_t taddr) const {
@@ -408,23 +471,7 @@ struct EpiStoreRope {
       tc::tmem_ld32(taddr + (ch + 2) * 32, x2);
       const int n1 = n0 + ch * 32, n2 = n1 + 64;
       if (!live || n1 >= N) continue;
-      const int d = (ch & 1) * 32;             // dim of x1[0] within its head
-      float c1[32], c2[32], s1[32], s2[32];
-#pragma unroll
-      for (int i = 0; i < 32; i += 8) {
-        qb::load8(cr + d + i, c1 + i);
-        qb::load8(cr + 64 + d + i, c2 + i);
-        qb::load8(sr + d + i, s1 + i);
-        qb::load8(sr + 64 + d + i, s2 + i);
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = x1[i] + (bias ? __ldg(bias + n1 + i) : 0.f);
-        const float b = x2[i] + (bias ? __ldg(bias + n2 + i) : 0.f);
-        qb::rope_rotate(__bfloat162float(__float2bfloat16_rn(a)),
-                        __bfloat162float(__float2bfloat16_rn(b)), c1[i], c2[i], s1[i], s2[i],
-                        x1[i], x2[i]);
-      }
+      rotate(x1, x2, ch, n1, cr, sr);
       __nv_bfloat16* dst = c + static_cast<int64_t>(m) * ldc;
       if (vec) {
 #pragma unroll
@@ -966,6 +1013,12 @@ extern "C" int qb_gemm2_rope_bf16(const void* A0, int64_t lda0, const void* B0, 
                    static_cast<int>(S), bias, static_cast<const __nv_bfloat16*>(cos_),
                    static_cast<const __nv_bfloat16*>(sin_), cs_stride_s,
                    qb::aligned16(C) && (ldc * 2) % 16 == 0};
+  if (epi.vec) {   // C as TMA stores it from the epilogue's staging boxes
+    if (int e = tc_host::encode_2d(&epi.cmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, C, N, M, ldc * 2,
+                                   32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+    epi.tma = true;
+  }
   using namespace tcg;
   if (use_pair(true, M, N)) {
     if (int s = map_operand(&m[1], B0, ldb0, false, N, K0, tcp::kHalfN)) return s;

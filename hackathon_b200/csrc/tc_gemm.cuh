@@ -95,6 +95,20 @@ struct EpiStage<E, std::void_t<decltype(E::kStageBytes)>> {
   static constexpr int bytes = E::kStageBytes;
 };
 
+// Row `lane` of a [32 x 32] bf16 staging box (64-byte rows) from 32 floats, in the 64-byte swizzle
+// of the box's tensor map: 16-byte piece p of row r sits at r * 64 + ((p ^ ((r >> 1) & 3)) * 16),
+// so the 32 lanes' writes of one piece cover every bank once per 128 bytes.
+__device__ __forceinline__ void stage_row_bf16(uint8_t* box, int lane, const float* v) {
+  uint8_t* dst = box + lane * 64;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    qb::Vec16<__nv_bfloat16> w;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w.v[i] = __float2bfloat16_rn(v[8 * p + i]);
+    *reinterpret_cast<uint4*>(dst + ((p ^ ((lane >> 1) & 3)) << 4)) = w.u;
+  }
+}
+
 // Ring stages of Cfg<BN> that fit beside `epi_bytes` of epilogue staging in the 227 KB a CTA
 // may have.
 template <int BN>
