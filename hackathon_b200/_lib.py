@@ -45,6 +45,7 @@ _SIGNATURES = {
     "qb_scaled_add": [_p, _i32, _i64, _p, _i32, _i64, _p, _i32, _i64, _i64, _i64, _f32, _p],
     "qb_dropout_mask": [_p, _i32, _i64, _p, _i32, _i64, _p, _i64, _i64, _u64, _f32, _f32, _p],
     "qb_dropout_apply": [_p, _i32, _i64, _p, _p, _i32, _i64, _i64, _i64, _f32, _i32, _p],
+    "qb_dropout_apply_multi": [_p, _i32, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _i64, _p],
     "qb_dropout_bits": [_p, _i64, _i64, _u64, _f32, _i32, _p],
     "qb_lora_xa": [_p, _i64, _p, _i64, _p, _i64, _f32, _p, _i64, _p, _i64, _i64, _i64, _i64,
                    _p],

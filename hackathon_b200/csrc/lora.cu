@@ -177,6 +177,43 @@ dropout_apply_kernel(const IT* __restrict__ in, int64_t ins, const uint32_t* __r
   }
 }
 
+// Up to four dropouts of one input with their own recorded masks (the q / k / v projections'
+// common input, the gate / up pair's): each 8-element piece of `in` is read once and written
+// once per output, with dropout_apply_kernel's arithmetic (in * scale where the bit is set).
+constexpr int kMaxApplyOuts = 4;
+struct ApplyOuts {
+  const uint32_t* bits[kMaxApplyOuts];   // [rows, words] each
+  void* out[kMaxApplyOuts];
+  int64_t outs[kMaxApplyOuts];           // row strides (elements)
+  float scale[kMaxApplyOuts];
+  int n;
+};
+
+template <typename IT, typename OT, bool SMALL>
+__global__ void __launch_bounds__(kThreads)
+dropout_apply_multi_kernel(const IT* __restrict__ in, int64_t ins,
+                           const __grid_constant__ ApplyOuts o, int64_t words, int64_t rows,
+                           int64_t cols) {
+  const int64_t n8 = cols / 8;
+  const int64_t total = rows * n8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    int64_t row, c;
+    row_col8<SMALL>(i, n8, row, c);
+    float x[8];
+    qb::load8<IT>(in + row * ins + c, x);
+#pragma unroll
+    for (int j = 0; j < kMaxApplyOuts; ++j) {
+      if (j >= o.n) break;
+      const uint32_t b = (__ldg(o.bits[j] + row * words + c / 32) >> (c % 32)) & 0xffu;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = ((b >> e) & 1u) ? x[e] * o.scale[j] : 0.0f;
+      qb::store8<OT>(static_cast<OT*>(o.out[j]) + row * o.outs[j] + c, v);
+    }
+  }
+}
+
 // Mask bits only, no data: one thread per 32-bit word (bit j = column 32w + j; bits past the
 // row's end are 0, as the ballot of dropout_mask_kernel leaves them). A fixed grid of a few
 // 256-thread blocks per SM with at most 32 registers a thread, so that the kernel can run on a
@@ -298,6 +335,51 @@ extern "C" int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_str
     });
   });
   return qb::check_launch("dropout_apply");
+}
+
+extern "C" int qb_dropout_apply_multi(const void* in, int in_dtype, int64_t in_row_stride, int n,
+                                      const uint32_t* const* bits, void* const* outs,
+                                      int out_dtype, const int64_t* out_row_strides,
+                                      const float* scales, int64_t rows, int64_t cols,
+                                      cudaStream_t stream) {
+  const char* what = "dropout_apply_multi";
+  if (n < 1 || n > kMaxApplyOuts)
+    return qb::fail(QB_ERR_INVALID, "%s: 1..%d outputs", what, kMaxApplyOuts);
+  if (!bits || !outs || !out_row_strides || !scales)
+    return qb::fail(QB_ERR_INVALID, "%s: null output table", what);
+  if (rows < 0 || cols < 0) return qb::fail(QB_ERR_INVALID, "%s: bad shape", what);
+  if (rows == 0 || cols == 0) return QB_OK;
+  if (cols % 8) return qb::fail(QB_ERR_UNSUPPORTED, "%s: cols must be a multiple of 8", what);
+  if (!in) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+  ApplyOuts o{};
+  o.n = n;
+  for (int j = 0; j < n; ++j) {
+    if (!bits[j] || !outs[j]) return qb::fail(QB_ERR_INVALID, "%s: null pointer", what);
+    if (reinterpret_cast<uintptr_t>(bits[j]) % 4)
+      return qb::fail(QB_ERR_INVALID, "%s: mask bits must be 4-byte aligned", what);
+    o.bits[j] = bits[j];
+    o.out[j] = outs[j];
+    o.outs[j] = out_row_strides[j];
+    o.scale[j] = scales[j];
+  }
+  const int64_t words = (cols + 31) / 32;
+  QB_DISPATCH_FLOAT(in_dtype, IT, {
+    QB_DISPATCH_FLOAT(out_dtype, OT, {
+      if (!rows_ok(in, in_row_stride, sizeof(IT)))
+        return qb::fail(QB_ERR_INVALID, "%s: rows must be 16-byte aligned", what);
+      for (int j = 0; j < n; ++j)
+        if (!rows_ok(outs[j], out_row_strides[j], sizeof(OT)))
+          return qb::fail(QB_ERR_INVALID, "%s: rows must be 16-byte aligned", what);
+      const unsigned grid = grid_cap(rows * (cols / 8));
+      if (rows * (cols / 8) <= 0xffffffffll)
+        dropout_apply_multi_kernel<IT, OT, true><<<grid, kThreads, 0, stream>>>(
+            static_cast<const IT*>(in), in_row_stride, o, words, rows, cols);
+      else
+        dropout_apply_multi_kernel<IT, OT, false><<<grid, kThreads, 0, stream>>>(
+            static_cast<const IT*>(in), in_row_stride, o, words, rows, cols);
+    });
+  });
+  return qb::check_launch(what);
 }
 
 extern "C" int qb_dropout_scale(const void* in, int in_dtype, int64_t in_row_stride, void* out,

@@ -127,6 +127,34 @@ def dropout_apply(x2, bits, scale, out=None, accumulate=False):
     return out
 
 
+def dropout_apply_multi(x2, masks, out_dtype=None):
+    """[x2 * mask_j * scale_j] for masks = [(bits_j, scale_j)] (1..4 of them) from recorded mask
+    bits, x2 read once (C-ABI qb_dropout_apply_multi); each result equals dropout_apply's."""
+    import ctypes
+    rows, cols = x2.shape
+    n = len(masks)
+    if not 1 <= n <= 4:
+        raise ValueError("dropout_apply_multi: 1..4 masks")
+    words = (cols + 31) // 32
+    for bits, _ in masks:
+        if bits.dtype != torch.int32 or not bits.is_contiguous() or bits.shape != (rows, words):
+            raise ValueError("dropout_apply_multi: bits must be contiguous int32 "
+                             "[rows, ceil(cols / 32)]")
+    _lib.require_cuda(x2, *(b for b, _ in masks), what="dropout_apply_multi")
+    dtype = out_dtype or x2.dtype
+    outs = [torch.empty((rows, cols), dtype=dtype, device=x2.device) for _ in masks]
+    bits_arr = (ctypes.c_void_p * n)(*(b.data_ptr() for b, _ in masks))
+    outs_arr = (ctypes.c_void_p * n)(*(o.data_ptr() for o in outs))
+    ld_arr = (ctypes.c_int64 * n)(*(o.stride(0) for o in outs))
+    sc_arr = (ctypes.c_float * n)(*(float(sc) for _, sc in masks))
+    _lib.call("qb_dropout_apply_multi", x2.data_ptr(), _lib.tag(x2.dtype), x2.stride(0), n,
+              bits_arr, outs_arr, _lib.tag(dtype), ld_arr, sc_arr, rows, cols,
+              _lib.stream(x2.device),
+              work=(rows * cols * (x2.element_size() + n * outs[0].element_size())
+                    + sum(b.numel() * 4 for b, _ in masks), 0))
+    return outs
+
+
 # The C layout of qb_pack_segment (include/qlora_b200.h): a table of these, built once, drives
 # the one launch of qb_adapter_pack.
 PACK_SEGMENT = [("src", "<u8"), ("dst", "<u8"), ("src_ld", "<i8"), ("dst_ld", "<i8"),

@@ -106,6 +106,31 @@ def prefetch_masks(layer, seed, rows, device):
     return ev
 
 
+def recorded_mask(mod, seed, rows):
+    """(bits, scale) of mod's dropout mask for `seed` when the step has it recorded for `rows`
+    rows and mod's fused path will use it, else None."""
+    if not (mod.training and mod.p > 0 and mod.fused and mod.in_features % 8 == 0):
+        return None
+    bits = MASKS.get((id(mod), seed))
+    if bits is None or bits.shape[0] != rows:
+        return None
+    return bits, 1.0 / (1.0 - mod.p)
+
+
+def shared_dropouts(x2, pairs):
+    """The dropped-out inputs of projections that share x2, [(mod, seed)] -> [xd or None]: one
+    pass over x2 (dropout_apply_multi) when every mask is recorded already, else all None (each
+    projection then draws or applies its own)."""
+    from .lora import dropout_apply_multi
+    from .nf4 import fused_ok
+    masks = [recorded_mask(mod, sd, x2.shape[0]) if fused_ok(x2, mod.quant_state) else None
+             for mod, sd in pairs]
+    if (len(pairs) < 2 or any(m is None for m in masks) or x2.shape[1] % 8
+            or x2.stride(-1) != 1):
+        return [None] * len(pairs)
+    return dropout_apply_multi(x2, masks)
+
+
 def gemm_mask_jobs(pairs, rows, device):
     """Allocates the bits of the (projection, seed) masks that are not drawn yet, enters them in
     MASKS and returns them as qb_mask_job tuples for the gate/up GEMM that draws them in its side
@@ -159,30 +184,31 @@ def _keep_uprod(keep_xd, graph):
     return KEEP_UPRODS and not keep_xd and graph
 
 
-def _adapter_input(x2, mod, a16, p, seed, keep_xd, u_out=None, stash=False):
+def _adapter_input(x2, mod, a16, p, seed, keep_xd, u_out=None, stash=False, xd=None):
     """(xd, U = xd a16^T, bits, scale) of one projection with xd = dropout(x2) * scale: U comes
     from x2 and the mask bits in one kernel (qb_lora_xa); xd is stored only when the backward
     will read it (keep_xd), else an empty placeholder stands in its saved slot. stash (the
     caller's graph flag of _keep_uprod): keep U of a checkpoint's first pass for its recompute
-    (UPRODS); a recompute (keep_xd) takes it from there."""
+    (UPRODS); a recompute (keep_xd) takes it from there. xd: dropout(x2) already formed from the
+    step's recorded mask (one pass over an input several projections share)."""
     key = (id(mod), seed)
     kept = UPRODS.pop(key, None) if keep_xd and u_out is None else None
     if kept is not None and kept.shape == (x2.shape[0], a16.shape[0]):
-        xd, bits, scale = _dropped(x2, mod, p, seed)
+        xd, bits, scale = _dropped(x2, mod, p, seed, xd)
         return xd, kept, bits, scale
-    xd, u, bits, scale = _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out)
+    xd, u, bits, scale = _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out, xd)
     if u_out is None and _keep_uprod(keep_xd, stash):
         UPRODS[key] = u
     return xd, u, bits, scale
 
 
-def _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out):
+def _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out, xd=None):
     """_adapter_input's computation: xd and U = xd a16^T."""
     from .gemm import gemm
     from .lora import lora_xa, lora_xa_ok
-    if (not FUSED_ADAPTER_INPUT or not lora_xa_ok(x2, a16)
+    if (xd is not None or not FUSED_ADAPTER_INPUT or not lora_xa_ok(x2, a16)
             or (p > 0 and x2.shape[1] % 8)):
-        xd, bits, scale = _dropped(x2, mod, p, seed)
+        xd, bits, scale = _dropped(x2, mod, p, seed, xd)
         if u_out is not None and u_out.stride(-1) == 1 and u_out.stride(0) % 8 == 0:
             u = gemm(xd, a16, out=u_out)
         else:
@@ -199,15 +225,20 @@ def _adapter_product(x2, mod, a16, p, seed, keep_xd, u_out):
     return xd, u, bits, scale
 
 
-def _dropped(x2, mod, p, seed):
+def _dropped(x2, mod, p, seed, xd=None):
     """(dropout(x2) * scale, mask bits or None, scale) with the step's mask for (mod, seed): drawn
-    once (Philox, the reference's stream) and replayed from the bits afterwards."""
+    once (Philox, the reference's stream) and replayed from the bits afterwards. xd: that
+    product already formed from the recorded bits (dropout_apply_multi)."""
     from .lora import dropout_apply, dropout_mask
     if p <= 0:
         return x2, None, 1.0
     scale = 1.0 / (1.0 - p)
     key = (id(mod), seed)
     bits = MASKS.get(key)
+    if xd is not None:
+        if bits is None or bits.shape[0] != x2.shape[0] or xd.shape != x2.shape:
+            raise RuntimeError("a dropped-out input was passed without its recorded mask")
+        return xd, bits, scale
     if bits is None or bits.shape[0] != x2.shape[0]:
         xd, bits = dropout_mask(x2, p, seed, scale)
         MASKS[key] = bits
@@ -241,18 +272,20 @@ class GateUpSwiGLU(torch.autograd.Function):
         a16_u, _ = up.adapter16(x.dtype)
         pair = ("pair", id(gate), seed_g)
         kept = UPRODS.pop(pair, None) if save_gu else None
+        # both masks recorded: one pass over x forms the two dropouts
+        dg, du = shared_dropouts(x2, [(gate, seed_g), (up, seed_u)]) if p > 0 else (None, None)
         if kept is not None and kept.shape == (T, 2 * r):
             # the recompute: [U_g | U_u] from the first pass, only xd_g / xd_u rebuilt
             lora_u = kept
-            xd_g, bits_g, scale = _dropped(x2, gate, p, seed_g)
-            xd_u, bits_u, _ = _dropped(x2, up, p, seed_u)
+            xd_g, bits_g, scale = _dropped(x2, gate, p, seed_g, dg)
+            xd_u, bits_u, _ = _dropped(x2, up, p, seed_u, du)
             u_g, u_u = lora_u[:, :r], lora_u[:, r:]
         else:
             lora_u = torch.empty((T, 2 * r), dtype=x.dtype, device=x.device)   # [U_g | U_u]
             xd_g, u_g, bits_g, scale = _adapter_input(x2, gate, a16_g, p, seed_g, save_gu,
-                                                      u_out=lora_u[:, :r])
+                                                      u_out=lora_u[:, :r], xd=dg)
             xd_u, u_u, bits_u, _ = _adapter_input(x2, up, a16_u, p, seed_u, save_gu,
-                                                  u_out=lora_u[:, r:])
+                                                  u_out=lora_u[:, r:], xd=du)
             if _keep_uprod(save_gu, any(ctx.needs_input_grad[1:5])):
                 UPRODS[pair] = lora_u
         if gate._shadow_b1 is not None and x.dtype == torch.bfloat16:
@@ -353,12 +386,14 @@ class LoRANF4Proj(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, lora_a, lora_b, mod, p, seed, residual, rope, output_dead=False,
-                keep_saved=True):
+                keep_saved=True, dropped=None):
         from .nf4 import dequantize_nf4, nf4_linear_fwd, uses_dequant_path
         x2 = x.reshape(-1, x.shape[-1])
         a16, sb16 = mod.adapter16(x.dtype)
         graph = ctx.needs_input_grad[1] or ctx.needs_input_grad[2]
-        xd, u, bits, scale = _adapter_input(x2, mod, a16, p, seed, keep_saved, stash=graph)
+        xd, u, bits, scale = _adapter_input(
+            x2, mod, a16, p, seed, keep_saved, stash=graph,
+            xd=None if dropped is None else dropped.reshape(x2.shape))
         w_keep = None
         if ctx.needs_input_grad[0] and uses_dequant_path(x2.shape[0]):
             w_keep = dequantize_nf4(mod.packed, mod.quant_state, torch.bfloat16,
@@ -405,7 +440,7 @@ class LoRANF4Proj(torch.autograd.Function):
             dx = nf4_linear_dgrad(g2, mod.packed, mod.quant_state, v, a16, weight=w_keep)
             dx = dx.view(ctx.shape)
         dres = g if ctx.has_residual and ctx.needs_input_grad[6] else None
-        return dx, da, db, None, None, None, dres, None, None, None
+        return dx, da, db, None, None, None, dres, None, None, None, None
 
 
 class LoRANF4Linear(torch.nn.Module):
@@ -444,13 +479,16 @@ class LoRANF4Linear(torch.nn.Module):
         return (self.lora_A.detach().to(dtype),
                 (self.lora_B.detach() * self.scaling).to(dtype))
 
-    def forward(self, x, seed, residual=None, rope=None, output_dead=False, keep_saved=True):
+    def forward(self, x, seed, residual=None, rope=None, output_dead=False, keep_saved=True,
+                dropped=None):
         """residual + this projection of x (the residual add of the decoder layer rides in the
         projection's epilogue on the fused path); rope = (cos, sin) [S, 128] applies the
         rotate-half RoPE to the output heads (fused path only); output_dead: the caller only
         needs what the backward saves (a checkpoint recompute), the result is left unwritten;
         keep_saved=False: the caller discards what the forward saves (a checkpoint's first
-        pass)."""
+        pass); dropped: dropout(x) already formed from this step's recorded mask for `seed` (the
+        fused path uses it in place of its own dropout pass; the reference composition redraws
+        the same mask)."""
         from .nf4 import fused_ok
         p = self.p if self.training else 0.0
         if self.fused and fused_ok(x, self.quant_state):
@@ -458,7 +496,7 @@ class LoRANF4Linear(torch.nn.Module):
                                          or residual.shape[:-1] != x.shape[:-1]):
                 raise ValueError("residual: bf16, one row per input row")
             return LoRANF4Proj.apply(x, self.lora_A, self.lora_B, self, p, seed, residual, rope,
-                                     output_dead, keep_saved)
+                                     output_dead, keep_saved, dropped if p > 0 else None)
         if rope is not None:
             raise ValueError("rope: only on the fused path")
         # the reference's composition: NF4Linear + DropoutCast + adapter GEMMs + ScaledAdd
@@ -523,20 +561,24 @@ class DecoderLayer(torch.nn.Module):
         B, S, _ = h.shape
         keep = not first_of_checkpoint    # the first pass's saved tensors are discarded
         x = rmsnorm(h, self.ln1, s.eps)
+        # q / k / v share x: with their masks recorded, one pass forms the three dropouts
+        dq, dk, dv = shared_dropouts(x.reshape(-1, x.shape[-1]),
+                                     [(self.q, seed + 0), (self.k, seed + 1), (self.v, seed + 2)])
         if self.rope_fused_ok(x, cos):
             # RoPE in the q / k projections' epilogue (tables [S, 128] of this sequence)
             cs = (cos[0], sin[0])
-            q = self.q(x, seed + 0, rope=cs, keep_saved=keep).view(
+            q = self.q(x, seed + 0, rope=cs, keep_saved=keep, dropped=dq).view(
                 B, S, s.heads, s.head_dim).transpose(1, 2)
-            k = self.k(x, seed + 1, rope=cs, keep_saved=keep).view(
+            k = self.k(x, seed + 1, rope=cs, keep_saved=keep, dropped=dk).view(
                 B, S, s.kv_heads, s.head_dim).transpose(1, 2)
         else:
-            q = self.q(x, seed + 0, keep_saved=keep).view(
+            q = self.q(x, seed + 0, keep_saved=keep, dropped=dq).view(
                 B, S, s.heads, s.head_dim).transpose(1, 2)
-            k = self.k(x, seed + 1, keep_saved=keep).view(
+            k = self.k(x, seed + 1, keep_saved=keep, dropped=dk).view(
                 B, S, s.kv_heads, s.head_dim).transpose(1, 2)
             q, k = CudaRoPE.apply(q, k, cos, sin)
-        v = self.v(x, seed + 2, keep_saved=keep).view(B, S, s.kv_heads, s.head_dim).transpose(1, 2)
+        v = self.v(x, seed + 2, keep_saved=keep, dropped=dv).view(
+            B, S, s.kv_heads, s.head_dim).transpose(1, 2)
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         a = a.transpose(1, 2).reshape(B, S, s.heads * s.head_dim)
         if prefetch is not None and not recompute:
@@ -550,7 +592,9 @@ class DecoderLayer(torch.nn.Module):
                                    self.up.lora_B, self.gate, self.up, p, seed + 4, seed + 5,
                                    torch.is_grad_enabled() and not first_of_checkpoint, jobs)
         else:
-            m = swiglu(self.gate(x, seed + 4), self.up(x, seed + 5))
+            dg, du = shared_dropouts(x.reshape(-1, x.shape[-1]),
+                                     [(self.gate, seed + 4), (self.up, seed + 5)])
+            m = swiglu(self.gate(x, seed + 4, dropped=dg), self.up(x, seed + 5, dropped=du))
         return self.down(m, seed + 6, residual=h, output_dead=recompute, keep_saved=keep)
 
 

@@ -183,6 +183,16 @@ int qb_dropout_apply(const void* in, int in_dtype, int64_t in_row_stride, const 
                      void* out, int out_dtype, int64_t out_row_stride, int64_t rows,
                      int64_t cols, float scale, int accumulate, cudaStream_t stream);
 
+/* qb_dropout_apply of one input with up to four masks at once: outs[j] = in * bit_j * scales[j]
+ * (bits[j]: [rows, ceil(cols / 32)] words), `in` read once. Host arrays of n (1..4) entries;
+ * cols a multiple of 8, 16-byte-aligned rows. The dropouts the reference draws one
+ * DropoutCast at a time (solution/lora.py:84-93) on the q / k / v projections' common input and
+ * on the gate / up pair's. */
+int qb_dropout_apply_multi(const void* in, int in_dtype, int64_t in_row_stride, int n,
+                           const uint32_t* const* bits, void* const* outs, int out_dtype,
+                           const int64_t* out_row_strides, const float* scales, int64_t rows,
+                           int64_t cols, cudaStream_t stream);
+
 /* out = base + lo * scaling (fp32 math). Replaces solution/lora.py:49-60
  * (lora_scaled_add_kernel). */
 int qb_scaled_add(const void* base, int base_dtype, int64_t base_row_stride, const void* lo,

@@ -208,6 +208,26 @@ def test_mask_job_layout_and_argument_checks():
         run([MaskJob(fake + 2, 16, 64, 1, 0.1)], 1)
 
 
+def test_dropout_apply_multi_argument_checks():
+    """qb_dropout_apply_multi refuses 0 or more than 4 outputs, an empty output table and
+    columns that are not a multiple of 8 before any CUDA call."""
+    import ctypes
+    from hackathon_b200 import _lib
+    fake = 1 << 20
+    bits = (ctypes.c_void_p * 5)(*([fake] * 5))
+    outs = (ctypes.c_void_p * 5)(*([fake] * 5))
+    lds = (ctypes.c_int64 * 5)(*([64] * 5))
+    scs = (ctypes.c_float * 5)(*([2.0] * 5))
+    for n in (0, 5):
+        with pytest.raises(RuntimeError, match="1..4 outputs"):
+            _lib.call("qb_dropout_apply_multi", fake, 2, 64, n, bits, outs, 2, lds, scs, 16, 64,
+                      None)
+    with pytest.raises(RuntimeError, match="null output table"):
+        _lib.call("qb_dropout_apply_multi", fake, 2, 64, 2, None, outs, 2, lds, scs, 16, 64, None)
+    with pytest.raises(RuntimeError, match="multiple of 8"):
+        _lib.call("qb_dropout_apply_multi", fake, 2, 64, 2, bits, outs, 2, lds, scs, 16, 60, None)
+
+
 def test_pack_segment_layout_and_table():
     """The Python table of qb_adapter_pack has the C struct's size, and its chunk offsets are the
     running sum of each segment's 2048-element chunks (host only: no launch)."""

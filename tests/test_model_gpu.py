@@ -155,6 +155,11 @@ def test_masks_drawn_in_the_gate_up_gemm_give_the_same_step(cuda):
     assert with_jobs["qb_gemm_gateup_swiglu_masks"]["launches"] == shape.layers
     assert with_jobs["qb_dropout_mask"]["launches"] == 6
     assert without["qb_dropout_mask"]["launches"] == 7 * shape.layers
+    # from layer 1 on the masks are recorded before use: q / k / v take one pass over their
+    # common input, gate / up one over theirs; o and down apply their own (layer 0's down too)
+    assert with_jobs["qb_dropout_apply_multi"]["launches"] == 2 * (shape.layers - 1)
+    assert with_jobs["qb_dropout_apply"]["launches"] == 2 * (shape.layers - 1) + 1
+    assert "qb_dropout_apply_multi" not in without
 
 
 @pytest.mark.parametrize("S", [256, 2048])

@@ -471,6 +471,27 @@ def test_gate_up_gemm_side_warps_draw_the_recorded_masks(cuda):
         gemm_gateup_swiglu(x, wg, wu, mask_jobs=jobs + jobs[:3])
 
 
+@pytest.mark.parametrize("rows,cols,n,in_dtype", [(16384, 3584, 3, torch.bfloat16),
+                                                  (300, 1000, 2, torch.bfloat16),
+                                                  (7, 40, 4, torch.float32),
+                                                  (129, 264, 1, torch.bfloat16)])
+def test_dropout_apply_multi_equals_single_applies(cuda, rows, cols, n, in_dtype):
+    """qb_dropout_apply_multi (one input read once, 1..4 masks) writes, for every mask, the very
+    bits dropout_apply writes for it alone: ragged last mask words, fp32 input into bf16."""
+    from hackathon_b200.lora import dropout_apply, dropout_apply_multi, dropout_bits
+    torch.manual_seed(3)
+    x = torch.randn(rows, cols, device=cuda).to(in_dtype)
+    masks = [(dropout_bits(rows, cols, p, 50 + j, cuda), 1.0 / (1.0 - p))
+             for j, p in enumerate([0.1, 0.05, 0.3, 0.0][:n])]
+    outs = dropout_apply_multi(x, masks, out_dtype=torch.bfloat16)
+    for (bits, scale), got in zip(masks, outs):
+        want = dropout_apply(x, bits, scale, out=torch.empty(rows, cols, dtype=torch.bfloat16,
+                                                             device=cuda))
+        assert torch.equal(got, want)
+    with pytest.raises(ValueError):
+        dropout_apply_multi(x, masks * 5)
+
+
 def test_bits_drawn_on_a_side_stream_beside_a_gemm(cuda):
     """The prefetch pattern of the model: bits drawn on another stream while a tcgen05 GEMM
     runs, the consumer stream waiting on an event; the result equals the inline mask."""
