@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 7b|1.5b|0.5b] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
 
-Workload (default): BASELINE configs[4], the Qwen2.5-7B-shaped QLoRA step — 28 layers, hidden
+Workload (default): the headline configuration, the Qwen2.5-7B-shaped QLoRA step — 28 layers, hidden
 3584, intermediate 18944, 28/4 heads x 128, vocab 152064, NF4 (bs 64, double quant) base, LoRA
 r=64 alpha=128 (dropout 0.05) on all seven linears, batch 4 x 4096 per GPU, activation
 checkpointing, AdamW on the adapters; data-parallel with an fp32 NCCL all-reduce of the adapter

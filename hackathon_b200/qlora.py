@@ -43,11 +43,11 @@ class QwenShape:
 
 
 PRESETS = {
-    # Qwen2.5-0.5B shapes, r=16
+    # Qwen2.5-0.5B shapes, r=16 (the smallest benchmark configuration)
     "0.5b": QwenShape("qwen2.5-0.5b", 896, 4864, 24, 14, 2, 64, 151936, True),
-    # configs[3]: Qwen2.5-1.5B shapes, r=16
+    # Qwen2.5-1.5B shapes, r=16
     "1.5b": QwenShape("qwen2.5-1.5b", 1536, 8960, 28, 12, 2, 128, 151936, True),
-    # Qwen2.5-7B shapes, r=64 alpha=128
+    # Qwen2.5-7B shapes, r=64 alpha=128 (the headline benchmark configuration)
     "7b": QwenShape("qwen2.5-7b", 3584, 18944, 28, 28, 4, 128, 152064, False,
                     lora_r=64, lora_alpha=128),
 }

@@ -211,7 +211,7 @@ def test_decoder_layer_matches_eager_oracle(cuda, name, S):
     """One decoder layer (dropout off): GPU ops vs the eager CPU oracle with the same NF4
     bytes, bf16 activations; forward and the LoRA-A gradient within bf16 tolerance. 0.5B shapes
     at 64 tokens (the fused NF4 kernel, RoPE as its own kernel for 64-dim heads); 1.5B shapes
-    (SURVEY Cfg4: 12 / 2 heads of 128) at 2048 tokens (transient weights, RoPE in the q / k
+    (the 1.5B configuration: 12 / 2 heads of 128) at 2048 tokens (transient weights, RoPE in the q / k
     GEMM epilogue)."""
     from hackathon_b200.qlora import DecoderLayer, preset
     from oracle import ops_ref
