@@ -248,3 +248,36 @@ def test_pack_segment_layout_and_table():
         pack_table([(src[0].double(), dst[0], 1.0)])
     with pytest.raises(ValueError):
         pack_table([(src[0], dst[1], 1.0)])
+
+
+def test_mask_and_product_bookkeeping_on_the_host():
+    """The host logic that decides which dropout masks a gate/up GEMM draws, which recorded masks
+    a projection may use, and when a rank-r product is kept for the recompute (no launch)."""
+    import torch
+    from hackathon_b200 import qlora
+
+    class Proj:
+        def __init__(self, in_features, p=0.05, fused=True, training=True):
+            self.in_features, self.p, self.fused, self.training = in_features, p, fused, training
+            self.quant_state = None
+
+    a, b, off, odd = Proj(3584), Proj(18944), Proj(3584, p=0.0), Proj(3580)
+    qlora.MASKS.clear()
+    try:
+        qlora.MASKS[(id(b), 7)] = torch.zeros((16, 592), dtype=torch.int32)   # drawn already
+        jobs = qlora.gemm_mask_jobs([(a, 5), (b, 7), (off, 9), (odd, 11)], 16, "cpu")
+        assert [(j[1], j[2], j[3], j[4]) for j in jobs] == [(16, 3584, 5, 0.05)]
+        assert jobs[0][0].shape == (16, 112) and jobs[0][0].dtype == torch.int32
+        assert qlora.MASKS[(id(a), 5)] is jobs[0][0]
+        bits, scale = qlora.recorded_mask(a, 5, 16)
+        assert bits is jobs[0][0] and abs(scale - 1 / 0.95) < 1e-12
+        assert qlora.recorded_mask(a, 5, 32) is None          # other rows
+        assert qlora.recorded_mask(off, 9, 16) is None        # no dropout
+        assert qlora.recorded_mask(Proj(3584, training=False), 5, 16) is None
+        # on the CPU no projection takes the fused path: every shared dropout is left to it
+        x = torch.zeros(16, 3584, dtype=torch.bfloat16)
+        assert qlora.shared_dropouts(x, [(a, 5), (a, 5)]) == [None, None]
+    finally:
+        qlora.MASKS.clear()
+    assert qlora._keep_uprod(False, True) and not qlora._keep_uprod(True, True)
+    assert not qlora._keep_uprod(False, False)
